@@ -1,0 +1,289 @@
+// capi.cu -- host side of the C ABI declared in include/qgemm.h.
+//
+// Validates shapes / alignment / layouts, encodes the TMA tensor maps
+// (cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library needs no link-time libcuda), and launches the kernels.  It never
+// allocates device memory and never exits the process.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/qgemm.h"
+#include "qg_gemm.h"
+
+namespace qg {
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return QG_ERR_CUDA;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return QG_ERR_CUDA;
+  return major == 10 ? QG_OK : QG_ERR_UNSUPPORTED;
+}
+
+// Operand values: uint8 [rows][row_bytes], box 128 B x box_rows, SWIZZLE_128B.
+bool make_operand_map(CUtensorMap* m, const void* base, int64_t rows, int64_t row_bytes,
+                      int box_rows) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  const cuuint32_t box[2] = {128u, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Scale chunks: uint32 [scale_blocks][row_blocks][128] with the chunk
+// strides of the chosen MMA order; box (128, box_row_blocks, box_chunks).
+bool make_scale_map(CUtensorMap* m, const void* base, int64_t mn, int64_t k, int sv, int layout,
+                    int box_row_blocks, int box_chunks) {
+  const int64_t row_blocks = (mn + 127) / 128;
+  const int64_t sf_blocks = ((k + sv - 1) / sv + 3) / 4;
+  const cuuint64_t dims[3] = {128u, static_cast<cuuint64_t>(row_blocks),
+                              static_cast<cuuint64_t>(sf_blocks)};
+  cuuint64_t strides[2];
+  if (layout == QG_LAYOUT_MMA) {
+    strides[0] = 512u;
+    strides[1] = static_cast<cuuint64_t>(row_blocks) * 512u;
+  } else {
+    strides[0] = static_cast<cuuint64_t>(sf_blocks) * 512u;
+    strides[1] = 512u;
+  }
+  const cuuint32_t box[3] = {128u, static_cast<cuuint32_t>(box_row_blocks),
+                             static_cast<cuuint32_t>(box_chunks)};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(base), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+uint64_t default_timeout_ns() {
+  static uint64_t t = [] {
+    const char* e = std::getenv("QG_WAIT_TIMEOUT_NS");
+    return e ? static_cast<uint64_t>(std::strtoull(e, nullptr, 10)) : 2000000000ull;
+  }();
+  return t;
+}
+
+int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
+                const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
+                int64_t k, int64_t ldc, int sf_layout, uint32_t* status, cudaStream_t stream) {
+  if (!a_q || !a_sf || !b_q || !b_sf || !c) return QG_ERR_ARG;
+  if (c_dtype != QG_DTYPE_F32 && c_dtype != QG_DTYPE_BF16) return QG_ERR_DTYPE;
+  if (sf_layout != QG_LAYOUT_MMA && sf_layout != QG_LAYOUT_MMA_KMAJOR) return QG_ERR_LAYOUT;
+  if (m < 1 || n < 1 || k < 32 || (k % 32) != 0 || ldc < n) return QG_ERR_SHAPE;
+  if (m > (1ll << 31) - 1 || n > (1ll << 31) - 1 || k > (1ll << 31) - 1) return QG_ERR_SHAPE;
+  if (!aligned16(a_q) || !aligned16(b_q) || !aligned16(a_sf) || !aligned16(b_sf))
+    return QG_ERR_ALIGN;
+  const int64_t row_bytes = fp4 ? k / 2 : k;
+  if (row_bytes % 16 != 0) return QG_ERR_ALIGN;
+  if (int d = check_device()) return d;
+  if (!encode_fn()) return QG_ERR_CUDA;
+  const int sv = fp4 ? 16 : 32;
+  const int bm = gemm_tile_m(), bn = gemm_tile_n();
+  const int chunks = gemm_sf_chunks_per_stage(fp4);
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  if (!make_operand_map(&p.tm_a, a_q, m, row_bytes, bm)) return QG_ERR_CUDA;
+  if (!make_operand_map(&p.tm_b, b_q, n, row_bytes, bn)) return QG_ERR_CUDA;
+  if (!make_scale_map(&p.tm_sfa, a_sf, m, k, sv, sf_layout, bm / 128, chunks)) return QG_ERR_CUDA;
+  if (!make_scale_map(&p.tm_sfb, b_sf, n, k, sv, sf_layout, bn / 128, chunks)) return QG_ERR_CUDA;
+  const int esize = c_dtype == QG_DTYPE_BF16 ? 2 : 4;
+  p.c = c;
+  p.ldc = ldc;
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.num_m_tiles = static_cast<int>((m + bm - 1) / bm);
+  p.num_n_tiles = static_cast<int>((n + bn - 1) / bn);
+  p.num_k_blocks = static_cast<int>((row_bytes + gemm_stage_k_bytes() - 1) / gemm_stage_k_bytes());
+  p.vec_ok = aligned16(c) && ((ldc * esize) % 16 == 0);
+  p.a_ts = fp4 ? a_ts : nullptr;
+  p.b_ts = fp4 ? b_ts : nullptr;
+  p.status = status;
+  p.timeout_ns = default_timeout_ns();
+  const int64_t tiles = static_cast<int64_t>(p.num_m_tiles) * p.num_n_tiles;
+  const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
+  cudaError_t e = launch_gemm_blockscaled(p, fp4, c_dtype == QG_DTYPE_BF16, grid, stream);
+  return e == cudaSuccess ? QG_OK : QG_ERR_CUDA;
+}
+
+}  // namespace
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cached[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = v > 0 ? v : 148;
+  }
+  return cached[dev];
+}
+
+}  // namespace qg
+
+using namespace qg;
+
+extern "C" {
+
+const char* qg_status_string(int s) {
+  switch (s) {
+    case QG_OK: return "ok";
+    case QG_ERR_SHAPE: return "unsupported shape";
+    case QG_ERR_ALIGN: return "misaligned pointer or leading dimension";
+    case QG_ERR_LAYOUT: return "layout not accepted here";
+    case QG_ERR_DTYPE: return "unknown dtype";
+    case QG_ERR_CUDA: return "CUDA error";
+    case QG_ERR_TIMEOUT: return "device wait timed out";
+    case QG_ERR_ARG: return "bad argument";
+    case QG_ERR_UNSUPPORTED: return "device is not sm_100";
+    default: return "unknown status";
+  }
+}
+
+const char* qg_version(void) { return "qgemm-b200 0.1.0 (sm_100a)"; }
+
+int64_t qg_scale_bytes(int64_t mn, int64_t k, int sv) {
+  if (mn < 0 || k < 0 || sv <= 0) return -1;
+  return ((mn + 127) / 128) * (((k + sv - 1) / sv + 3) / 4) * 512;
+}
+
+size_t qg_quantize_workspace_bytes(void) { return 256; }
+
+int qg_quantize_nvfp4(const void* x, int x_dtype, int64_t rows, int64_t k, int layout, void* q,
+                      void* sf, float* ts, void* workspace, qg_stream_t stream) {
+  if (!x || !q || !sf || !workspace) return QG_ERR_ARG;
+  if (x_dtype != QG_DTYPE_F32 && x_dtype != QG_DTYPE_BF16) return QG_ERR_DTYPE;
+  if (layout < QG_LAYOUT_REF_LINEAR || layout > QG_LAYOUT_MMA_KMAJOR) return QG_ERR_LAYOUT;
+  if (rows < 1 || k < 1) return QG_ERR_SHAPE;
+  if (layout != QG_LAYOUT_REF_LINEAR && (k % 16) != 0) return QG_ERR_SHAPE;
+  if (!aligned16(x) || !aligned16(q) || !aligned16(workspace)) return QG_ERR_ALIGN;
+  if (int d = check_device()) return d;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool bf16 = x_dtype == QG_DTYPE_BF16;
+  uint32_t* amax = static_cast<uint32_t*>(workspace);
+  if (cudaMemsetAsync(amax, 0, sizeof(uint32_t), s) != cudaSuccess) return QG_ERR_CUDA;
+  if (layout != QG_LAYOUT_REF_LINEAR && ((rows % 128) != 0 || ((k / 16) % 4) != 0)) {
+    // Padded scale slots must read as zero scales.
+    if (cudaMemsetAsync(sf, 0, static_cast<size_t>(qg_scale_bytes(rows, k, 16)), s) != cudaSuccess)
+      return QG_ERR_CUDA;
+  }
+  if (launch_amax(x, bf16, rows * k, amax, s) != cudaSuccess) return QG_ERR_CUDA;
+  if (launch_quantize_nvfp4(x, bf16, rows, k, layout, static_cast<uint8_t*>(q),
+                            static_cast<uint8_t*>(sf), ts, amax, s) != cudaSuccess)
+    return QG_ERR_CUDA;
+  return QG_OK;
+}
+
+int qg_quantize_mxfp8(const void* x, int x_dtype, int64_t rows, int64_t k, int layout, void* q,
+                      void* sf, qg_stream_t stream) {
+  if (!x || !q || !sf) return QG_ERR_ARG;
+  if (x_dtype != QG_DTYPE_F32 && x_dtype != QG_DTYPE_BF16) return QG_ERR_DTYPE;
+  if (layout < QG_LAYOUT_REF_LINEAR || layout > QG_LAYOUT_MMA_KMAJOR) return QG_ERR_LAYOUT;
+  if (rows < 1 || k < 32 || (k % 32) != 0) return QG_ERR_SHAPE;
+  if (!aligned16(x) || !aligned16(q)) return QG_ERR_ALIGN;
+  if (int d = check_device()) return d;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (layout != QG_LAYOUT_REF_LINEAR && ((rows % 128) != 0 || ((k / 32) % 4) != 0)) {
+    if (cudaMemsetAsync(sf, 0, static_cast<size_t>(qg_scale_bytes(rows, k, 32)), s) != cudaSuccess)
+      return QG_ERR_CUDA;
+  }
+  return launch_quantize_mxfp8(x, x_dtype == QG_DTYPE_BF16, rows, k, layout,
+                               static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf),
+                               s) == cudaSuccess
+             ? QG_OK
+             : QG_ERR_CUDA;
+}
+
+int qg_repack_nvfp4(const void* src_q, const void* src_sf, int src_layout, void* dst_q,
+                    void* dst_sf, int dst_layout, int64_t rows, int64_t k, qg_stream_t stream) {
+  if (!src_q || !src_sf || !dst_q || !dst_sf) return QG_ERR_ARG;
+  if (src_layout < 0 || src_layout > 2 || dst_layout < 0 || dst_layout > 2) return QG_ERR_LAYOUT;
+  if (rows < 1 || k < 16 || (k % 16) != 0) return QG_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(src_q) & 7u) || (reinterpret_cast<uintptr_t>(dst_q) & 7u))
+    return QG_ERR_ALIGN;
+  if (int d = check_device()) return d;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dst_layout != QG_LAYOUT_REF_LINEAR && ((rows % 128) != 0 || ((k / 16) % 4) != 0)) {
+    if (cudaMemsetAsync(dst_sf, 0, static_cast<size_t>(qg_scale_bytes(rows, k, 16)), s) !=
+        cudaSuccess)
+      return QG_ERR_CUDA;
+  }
+  return launch_repack_nvfp4(static_cast<const uint8_t*>(src_q),
+                             static_cast<const uint8_t*>(src_sf), src_layout,
+                             static_cast<uint8_t*>(dst_q), static_cast<uint8_t*>(dst_sf),
+                             dst_layout, rows, k, s) == cudaSuccess
+             ? QG_OK
+             : QG_ERR_CUDA;
+}
+
+int qg_gemm_nvfp4(const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
+                  const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
+                  int64_t k, int64_t ldc, int sf_layout, uint32_t* status, qg_stream_t stream) {
+  return gemm_common(true, a_q, a_sf, a_ts, b_q, b_sf, b_ts, c, c_dtype, m, n, k, ldc, sf_layout,
+                     status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, void* c,
+                  int c_dtype, int64_t m, int64_t n, int64_t k, int64_t ldc, int sf_layout,
+                  uint32_t* status, qg_stream_t stream) {
+  return gemm_common(false, a_q, a_sf, nullptr, b_q, b_sf, nullptr, c, c_dtype, m, n, k, ldc,
+                     sf_layout, status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int qg_read_status(uint32_t* status, uint32_t* device_code, qg_stream_t stream) {
+  if (!status) return QG_ERR_ARG;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  if (cudaMemcpyAsync(&v, status, sizeof(v), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return QG_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return QG_ERR_CUDA;
+  if (cudaMemsetAsync(status, 0, sizeof(uint32_t), s) != cudaSuccess) return QG_ERR_CUDA;
+  if (device_code) *device_code = v;
+  return v == 0 ? QG_OK : QG_ERR_TIMEOUT;
+}
+
+int qg_selftest_wait_timeout(uint64_t timeout_ns, uint32_t* status, qg_stream_t stream) {
+  if (!status) return QG_ERR_ARG;
+  if (timeout_ns > 1000000000ull) return QG_ERR_ARG;  // keep the self test short
+  if (int d = check_device()) return d;
+  return launch_wait_timeout_selftest(timeout_ns, status, reinterpret_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? QG_OK
+             : QG_ERR_CUDA;
+}
+
+}  // extern "C"

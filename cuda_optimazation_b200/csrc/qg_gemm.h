@@ -1,0 +1,49 @@
+// qg_gemm.h -- internal launch interface between the C-ABI host code and
+// the kernels.  Not part of the public ABI (include/qgemm.h is).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace qg {
+
+struct GemmParams {
+  CUtensorMap tm_a;    // uint8 [rows][K bytes], box 128 B x kBM, SWIZZLE_128B
+  CUtensorMap tm_b;    // uint8 [rows][K bytes], box 128 B x kBN, SWIZZLE_128B
+  CUtensorMap tm_sfa;  // uint32 [scale_blocks][row_blocks][128], box (128, kBM/128, chunks)
+  CUtensorMap tm_sfb;
+  void* c;
+  int64_t ldc;  // elements
+  int m, n, k;
+  int num_m_tiles, num_n_tiles, num_k_blocks;
+  int vec_ok;  // 16-byte vector stores are legal for every full 32-column run
+  const float* a_ts;
+  const float* b_ts;
+  uint32_t* status;
+  uint64_t timeout_ns;
+};
+
+cudaError_t launch_gemm_blockscaled(const GemmParams& p, bool fp4, bool out_bf16, int grid,
+                                    cudaStream_t stream);
+int gemm_tile_m();
+int gemm_tile_n();
+int gemm_stage_k_bytes();
+int gemm_sf_chunks_per_stage(bool fp4);
+
+// Quantizer launches (quantize.cu).
+cudaError_t launch_amax(const void* x, bool bf16, int64_t n, uint32_t* amax_bits,
+                        cudaStream_t stream);
+cudaError_t launch_quantize_nvfp4(const void* x, bool bf16, int64_t rows, int64_t k, int layout,
+                                  uint8_t* q, uint8_t* sf, float* ts, const uint32_t* amax_bits,
+                                  cudaStream_t stream);
+cudaError_t launch_quantize_mxfp8(const void* x, bool bf16, int64_t rows, int64_t k, int layout,
+                                  uint8_t* q, uint8_t* sf, cudaStream_t stream);
+cudaError_t launch_repack_nvfp4(const uint8_t* sq, const uint8_t* ssf, int src_layout,
+                                uint8_t* dq, uint8_t* dsf, int dst_layout, int64_t rows,
+                                int64_t k, cudaStream_t stream);
+cudaError_t launch_wait_timeout_selftest(uint64_t timeout_ns, uint32_t* status,
+                                         cudaStream_t stream);
+
+int num_sms();
+
+}  // namespace qg

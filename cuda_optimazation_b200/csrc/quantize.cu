@@ -1,0 +1,339 @@
+// quantize.cu -- NVFP4 / MXFP8 activation quantizers, the NVFP4 layout
+// repack, and the bounded-wait self test.
+//
+// NVFP4 follows make_nvfp4_reference
+// (GEMMsm110/include/requant/nvfp4_reference.cuh:76-112) bit for bit:
+//   ts      = amax / (448 * 6)            (1 if amax == 0)
+//   s_blk   = e4m3_round_up(max|x * (1/ts)| / 6)
+//   mult    = (1/ts) / decode(s_blk)      (0 if the scale decodes to 0)
+//   q_i     = e2m1_rne(x_i * mult)
+// Every step uses IEEE round-to-nearest fp32 operations (__fdiv_rn /
+// __fmul_rn) so the device result equals the host reference exactly; the
+// reference's own device twin used inv_ts * (1/s) instead
+// (sm110_tcgen05_epilogue.cuh:148-150), which is not bit-identical.
+//
+// The work is HBM-bound (4 or 2 bytes in, 0.5625 out per element): loads are
+// 16-byte vectors, one thread per 16-element block, grid sized in multiples
+// of the SM count.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "qg_gemm.h"
+#include "qg_ptx.cuh"
+
+namespace qg {
+
+// ------------------------------------------------------------------ codecs
+// fp32 -> e2m1 nibble, round to nearest even, sign kept on zero, NaN -> +0,
+// saturating at 6.  The seven thresholds are the fp32 bit patterns of the
+// rounding boundaries of the e2m1 grid {0, .5, 1, 1.5, 2, 3, 4, 6}: a tie
+// that must round to the even lower code starts one ulp above the midpoint.
+__device__ __forceinline__ uint32_t e2m1_encode(float v) {
+  const uint32_t raw = __float_as_uint(v);
+  const uint32_t mag = raw & 0x7fffffffu;
+  if (mag > 0x7f800000u) return 0u;
+  const uint32_t code = (mag >= 0x3e800001u) + (mag >= 0x3f400000u) + (mag >= 0x3fa00001u) +
+                        (mag >= 0x3fe00000u) + (mag >= 0x40200001u) + (mag >= 0x40600000u) +
+                        (mag >= 0x40a00001u);
+  return ((raw >> 28) & 0x8u) | code;
+}
+
+// Smallest positive finite e4m3 code whose value is >= v (0 for v <= 0,
+// 0x7e = 448 above the range).  Normal range: truncate the fp32 mantissa to
+// 3 bits and bump by one code when any dropped bit is set; subnormal range
+// (v < 2^-6): ceil(v * 2^9) subnormal steps.
+__device__ __forceinline__ uint32_t e4m3_round_up(float v) {
+  if (!(v > 0.0f)) return 0u;
+  if (v >= 448.0f) return 0x7eu;
+  if (v < 0.015625f) return static_cast<uint32_t>(ceilf(v * 512.0f));
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t e = ((b >> 23) & 0xffu) - 127u + 7u;
+  uint32_t code = (e << 3) | ((b >> 20) & 7u);
+  if (b & 0xfffffu) code += 1u;
+  return code;
+}
+
+__device__ __forceinline__ float e4m3_decode_positive(uint32_t c) {
+  const uint32_t e = (c >> 3) & 0xfu, m = c & 7u;
+  if (e == 0u) return static_cast<float>(m) * 0.001953125f;  // m * 2^-9
+  return __uint_as_float(((e + 120u) << 23) | (m << 20));
+}
+
+// Byte offset of scale (row, scale column) in an MMA scale layout.
+__device__ __forceinline__ int64_t mma_scale_offset(int64_t row, int64_t sfc, int64_t row_blocks,
+                                                    int64_t sf_blocks, int layout) {
+  const int64_t br = row >> 7, bs = sfc >> 2, w = row & 127;
+  const int64_t chunk = (layout == 1) ? bs * row_blocks + br : br * sf_blocks + bs;
+  return chunk * 512 + (w & 31) * 16 + (w >> 5) * 4 + (sfc & 3);
+}
+
+template <bool kBf16>
+__device__ __forceinline__ void load16(const void* x, int64_t elem, float (&v)[16]) {
+  if (kBf16) {
+    const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(x) + elem);
+    const uint4 a = __ldg(p), b = __ldg(p + 1);
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  } else {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + elem);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 f = __ldg(p + i);
+      v[4 * i] = f.x;
+      v[4 * i + 1] = f.y;
+      v[4 * i + 2] = f.z;
+      v[4 * i + 3] = f.w;
+    }
+  }
+}
+
+template <bool kBf16>
+__device__ __forceinline__ float load1(const void* x, int64_t i) {
+  if (kBf16) {
+    const uint16_t h = reinterpret_cast<const uint16_t*>(x)[i];
+    return __uint_as_float(static_cast<uint32_t>(h) << 16);
+  }
+  return reinterpret_cast<const float*>(x)[i];
+}
+
+// ------------------------------------------------------------------ amax
+template <bool kBf16>
+__global__ void __launch_bounds__(256) amax_kernel(const void* x, int64_t n, uint32_t* amax_bits) {
+  float m = 0.0f;
+  const int64_t nvec = n / 16;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t v = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; v < nvec;
+       v += stride) {
+    float f[16];
+    load16<kBf16>(x, v * 16, f);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(f[i]));
+  }
+  for (int64_t i = nvec * 16 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += stride)
+    m = fmaxf(m, fabsf(load1<kBf16>(x, i)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    // Non-negative floats order like their bit patterns.
+    if (threadIdx.x == 0) atomicMax(amax_bits, __float_as_uint(m));
+  }
+}
+
+// ------------------------------------------------------------------ NVFP4
+// One thread per 16-element block.  layout: 0 REF_LINEAR (flat blocks, high
+// nibble first, linear scales), 1 MMA, 2 MMA_KMAJOR (row blocks, low nibble
+// first, chunked scales).
+template <bool kBf16>
+__global__ void __launch_bounds__(256)
+    nvfp4_quantize_kernel(const void* x, int64_t rows, int64_t k, int layout, uint8_t* q,
+                          uint8_t* sf, float* ts_out, const uint32_t* amax_bits) {
+  const float amax = __uint_as_float(*amax_bits);
+  const float ts = amax > 0.0f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
+  const float inv_ts = __fdiv_rn(1.0f, ts);
+  const int64_t n = rows * k;
+  const int64_t nblocks = (n + 15) / 16;
+  const int64_t sfk = k / 16;
+  const int64_t row_blocks = (rows + 127) / 128;
+  const int64_t sf_blocks = (sfk + 3) / 4;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && ts_out) *ts_out = ts;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < nblocks;
+       b += stride) {
+    float v[16];
+    if ((b + 1) * 16 <= n) {
+      load16<kBf16>(x, b * 16, v);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = (b * 16 + i < n) ? load1<kBf16>(x, b * 16 + i) : 0.0f;
+    }
+    float bmax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
+    // max|x*inv_ts| == RN(max|x| * inv_ts): RN is monotonic.
+    const float namax = __fmul_rn(bmax, inv_ts);
+    const uint32_t sbits = e4m3_round_up(__fdiv_rn(namax, 6.0f));
+    const float bs = e4m3_decode_positive(sbits);
+    const float mult = bs > 0.0f ? __fdiv_rn(inv_ts, bs) : 0.0f;
+    uint32_t lo = 0, hi = 0;
+    const bool high_first = (layout == 0);
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const uint32_t c0 = e2m1_encode(__fmul_rn(v[i], mult));
+      const uint32_t c1 = e2m1_encode(__fmul_rn(v[i + 1], mult));
+      const uint32_t byte = high_first ? ((c0 << 4) | c1) : (c0 | (c1 << 4));
+      if (i < 8) lo |= byte << (4 * i);
+      else hi |= byte << (4 * (i - 8));
+    }
+    reinterpret_cast<uint2*>(q)[b] = make_uint2(lo, hi);
+    if (layout == 0) {
+      sf[b] = static_cast<uint8_t>(sbits);
+    } else {
+      const int64_t row = b / sfk, sc = b - row * sfk;
+      sf[mma_scale_offset(row, sc, row_blocks, sf_blocks, layout)] = static_cast<uint8_t>(sbits);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ MXFP8
+// One thread per 32-element block: ue8m0 exponent floor(log2(amax)) - 8,
+// elements RN-satfinite e4m3 of x * 2^-e.
+__device__ __forceinline__ int floor_log2_positive(float a) {
+  const uint32_t b = __float_as_uint(a);
+  const int e = static_cast<int>((b >> 23) & 0xffu);
+  if (e != 0) return e - 127;
+  return -149 + (31 - __clz(static_cast<int>(b & 0x7fffffu)));
+}
+
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+template <bool kBf16>
+__global__ void __launch_bounds__(256)
+    mxfp8_quantize_kernel(const void* x, int64_t rows, int64_t k, int layout, uint8_t* q,
+                          uint8_t* sf) {
+  const int64_t sfk = k / 32;
+  const int64_t nblocks = rows * sfk;
+  const int64_t row_blocks = (rows + 127) / 128;
+  const int64_t sf_blocks = (sfk + 3) / 4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < nblocks;
+       b += stride) {
+    float v[32];
+    load16<kBf16>(x, b * 32, *reinterpret_cast<float(*)[16]>(&v[0]));
+    load16<kBf16>(x, b * 32 + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    int e = -127;
+    if (amax > 0.0f) e = max(-127, min(127, floor_log2_positive(amax) - 8));
+    const float mul = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);  // 2^-e, normal
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t p0 = cvt_e4m3x2(__fmul_rn(v[4 * i], mul), __fmul_rn(v[4 * i + 1], mul));
+      const uint32_t p1 = cvt_e4m3x2(__fmul_rn(v[4 * i + 2], mul), __fmul_rn(v[4 * i + 3], mul));
+      w[i] = p0 | (p1 << 16);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(q + b * 32);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    const uint8_t code = static_cast<uint8_t>(e + 127);
+    if (layout == 0) {
+      sf[b] = code;
+    } else {
+      const int64_t row = b / sfk, sc = b - row * sfk;
+      sf[mma_scale_offset(row, sc, row_blocks, sf_blocks, layout)] = code;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ repack
+__global__ void __launch_bounds__(256)
+    nvfp4_repack_kernel(const uint8_t* sq, const uint8_t* ssf, int src_layout, uint8_t* dq,
+                        uint8_t* dsf, int dst_layout, int64_t rows, int64_t k) {
+  const int64_t sfk = k / 16;
+  const int64_t nblocks = rows * sfk;
+  const int64_t row_blocks = (rows + 127) / 128;
+  const int64_t sf_blocks = (sfk + 3) / 4;
+  const bool swap = (src_layout == 0) != (dst_layout == 0);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < nblocks;
+       b += stride) {
+    uint2 w = reinterpret_cast<const uint2*>(sq)[b];
+    if (swap) {
+      w.x = ((w.x >> 4) & 0x0f0f0f0fu) | ((w.x << 4) & 0xf0f0f0f0u);
+      w.y = ((w.y >> 4) & 0x0f0f0f0fu) | ((w.y << 4) & 0xf0f0f0f0u);
+    }
+    reinterpret_cast<uint2*>(dq)[b] = w;
+    const int64_t row = b / sfk, sc = b - row * sfk;
+    const int64_t so =
+        src_layout == 0 ? b : mma_scale_offset(row, sc, row_blocks, sf_blocks, src_layout);
+    const int64_t d =
+        dst_layout == 0 ? b : mma_scale_offset(row, sc, row_blocks, sf_blocks, dst_layout);
+    dsf[d] = ssf[so];
+  }
+}
+
+// ------------------------------------------------------------------ self test
+__global__ void wait_timeout_selftest_kernel(uint64_t timeout_ns, uint32_t* status) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0u;
+    fence_barrier_init();
+    // Nobody arrives: phase 0 never completes, the bounded wait must expire.
+    mbar_wait_bounded(&bar, 0u, timeout_ns, &abort_flag, status, kDevTimeoutTest);
+  }
+}
+
+// ------------------------------------------------------------------ launches
+static int grid_for(int64_t work_items, int threads) {
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 8;
+  int64_t g = (work_items + threads - 1) / threads;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+cudaError_t launch_amax(const void* x, bool bf16, int64_t n, uint32_t* amax_bits,
+                        cudaStream_t stream) {
+  const int grid = grid_for(n / 16 + 1, 256);
+  if (bf16) amax_kernel<true><<<grid, 256, 0, stream>>>(x, n, amax_bits);
+  else amax_kernel<false><<<grid, 256, 0, stream>>>(x, n, amax_bits);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_nvfp4(const void* x, bool bf16, int64_t rows, int64_t k, int layout,
+                                  uint8_t* q, uint8_t* sf, float* ts, const uint32_t* amax_bits,
+                                  cudaStream_t stream) {
+  const int64_t nblocks = (rows * k + 15) / 16;
+  const int grid = grid_for(nblocks, 256);
+  if (bf16)
+    nvfp4_quantize_kernel<true><<<grid, 256, 0, stream>>>(x, rows, k, layout, q, sf, ts, amax_bits);
+  else
+    nvfp4_quantize_kernel<false><<<grid, 256, 0, stream>>>(x, rows, k, layout, q, sf, ts,
+                                                           amax_bits);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_mxfp8(const void* x, bool bf16, int64_t rows, int64_t k, int layout,
+                                  uint8_t* q, uint8_t* sf, cudaStream_t stream) {
+  const int grid = grid_for(rows * (k / 32), 256);
+  if (bf16) mxfp8_quantize_kernel<true><<<grid, 256, 0, stream>>>(x, rows, k, layout, q, sf);
+  else mxfp8_quantize_kernel<false><<<grid, 256, 0, stream>>>(x, rows, k, layout, q, sf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_repack_nvfp4(const uint8_t* sq, const uint8_t* ssf, int src_layout,
+                                uint8_t* dq, uint8_t* dsf, int dst_layout, int64_t rows,
+                                int64_t k, cudaStream_t stream) {
+  const int grid = grid_for(rows * (k / 16), 256);
+  nvfp4_repack_kernel<<<grid, 256, 0, stream>>>(sq, ssf, src_layout, dq, dsf, dst_layout, rows,
+                                                k);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_wait_timeout_selftest(uint64_t timeout_ns, uint32_t* status,
+                                         cudaStream_t stream) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(timeout_ns, status);
+  return cudaGetLastError();
+}
+
+}  // namespace qg

@@ -1,0 +1,149 @@
+/* qgemm.h -- C ABI of the B200 (sm_100a) block-scaled quantized GEMM library.
+ *
+ * This is the drop-in boundary for the reference's quant-GEMM path
+ * (hibouwu/CUDA_optimazation).  The reference has no in-process API: its
+ * operator surface is the NVFP4 host quantizer
+ * (GEMMsm110/include/requant/nvfp4_reference.cuh:76-112), the device requant
+ * primitives (GEMMsm110/include/requant/sm110_tcgen05_epilogue.cuh:75-160),
+ * the tc6 runner (GEMMsm110/include/backends/tc6_nvfp4.cuh:561-619) and the
+ * CUTLASS 72b NVFP4 backend the harness shells out to
+ * (GEMMquant_sm110/build_and_run.sh:38-75).  Each entry point below names the
+ * reference interface it replaces.
+ *
+ * Conventions
+ *  - Every pointer is caller-owned DEVICE memory unless stated otherwise.
+ *    No entry point allocates device memory.
+ *  - Calls are stream-ordered and asynchronous: a QG_OK return means the
+ *    work was enqueued on `stream`.  Device-side failures (a bounded wait that
+ *    timed out) are reported through `status` words read by qg_read_status().
+ *  - Nothing here calls exit() or abort().
+ *  - Operands are K-major: A is M x K row-major, B is N x K row-major
+ *    ("B^T" layout), C = A * B^T is M x N row-major with leading dimension ldc.
+ */
+#ifndef QGEMM_B200_H
+#define QGEMM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* qg_stream_t; /* == cudaStream_t; NULL = legacy stream */
+
+typedef enum {
+  QG_OK = 0,
+  QG_ERR_SHAPE = 1,       /* M, N or K out of the supported range          */
+  QG_ERR_ALIGN = 2,       /* pointer / leading dimension not 16-B aligned   */
+  QG_ERR_LAYOUT = 3,      /* layout not accepted by this entry point        */
+  QG_ERR_DTYPE = 4,       /* unknown dtype code                             */
+  QG_ERR_CUDA = 5,        /* a CUDA runtime / driver call failed            */
+  QG_ERR_TIMEOUT = 6,     /* a device wait exceeded its bound (status word) */
+  QG_ERR_ARG = 7,         /* null pointer or bad argument                   */
+  QG_ERR_UNSUPPORTED = 8  /* device is not sm_100                           */
+} qg_status;
+
+typedef enum { QG_DTYPE_F32 = 0, QG_DTYPE_BF16 = 1 } qg_dtype;
+
+/* Operand layouts.
+ *  QG_LAYOUT_REF_LINEAR : the reference quantizer's byte order
+ *      (nvfp4_reference.cuh:76-112): the tensor is flattened row-major, value
+ *      2i goes to the HIGH nibble of byte i (pack_fp4.cuh:11-15), and one
+ *      scale byte per 16 flattened elements in linear order.
+ *  QG_LAYOUT_MMA : the tensor-core operand order: row-major, value 2i in
+ *      the LOW nibble, scales in 512-byte chunks of 128 rows x 4 scale columns
+ *      at cutlass-gemm-cpp-guide/include/guide/scale_layout.hpp:11-26
+ *      (chunk index = scale_block * row_blocks + row_block).
+ *  QG_LAYOUT_MMA_KMAJOR : as QG_LAYOUT_MMA, but chunks of one 128-row block
+ *      are contiguous along K (chunk index = row_block * scale_blocks +
+ *      scale_block), the order CUTLASS's Sm1xxBlockScaledConfig
+ *      tile_to_shape(..., Step<_2,_1>) produces.  The two MMA orders coincide
+ *      when either block count is 1.
+ */
+typedef enum {
+  QG_LAYOUT_REF_LINEAR = 0,
+  QG_LAYOUT_MMA = 1,
+  QG_LAYOUT_MMA_KMAJOR = 2
+} qg_layout;
+
+/* Human-readable name of a qg_status code. */
+const char* qg_status_string(int status);
+
+/* Library version string. */
+const char* qg_version(void);
+
+/* Bytes of the scale-factor buffer for an MN x K operand with one scale per
+ * `sv` K elements (16 for NVFP4, 32 for MXFP8) in an MMA layout:
+ * ceil(MN/128) * ceil(ceil(K/sv)/4) * 512.
+ * Replaces guide::sm1xx_scale_storage_size (scale_layout.hpp:28-34). */
+int64_t qg_scale_bytes(int64_t mn, int64_t k, int sv);
+
+/* Workspace bytes qg_quantize_nvfp4 needs (one amax word, padded). */
+size_t qg_quantize_workspace_bytes(void);
+
+/* NVFP4 quantizer: x (rows x k, fp32 or bf16, row-major) -> e2m1 values `q`
+ * (rows*k/2 bytes), e4m3 block scales `sf` (one per 16 K elements; in
+ * QG_LAYOUT_REF_LINEAR rows*k/16 bytes, else qg_scale_bytes(rows, k, 16)
+ * bytes) and the fp32 tensor scale *ts = amax / (448 * 6) (1 if amax == 0).
+ * Bit-exact to make_nvfp4_reference (nvfp4_reference.cuh:76-112), which this
+ * replaces together with the device twins sm110_make_nvfp4_block_scale /
+ * sm110_requant_nvfp4_e2m1x2 (sm110_tcgen05_epilogue.cuh:75-160).
+ * REF_LINEAR accepts any rows*k; the MMA layouts need k % 16 == 0.
+ * `workspace` (device, qg_quantize_workspace_bytes()) holds the amax scratch
+ * word and is cleared on `stream` by the call. */
+int qg_quantize_nvfp4(const void* x, int x_dtype, int64_t rows, int64_t k, int layout, void* q,
+                      void* sf, float* ts, void* workspace, qg_stream_t stream);
+
+/* MXFP8 quantizer (OCP MX v1.0; the reference has none): x (rows x k) ->
+ * e4m3 values `q` (rows*k bytes) and ue8m0 scales per 32 K elements, scale
+ * exponent floor(log2(block amax)) - 8 clamped to [-127, 127] (all-zero
+ * blocks get code 0).  k % 32 == 0.  Layout REF_LINEAR writes the scales as
+ * [rows][k/32]; the MMA layouts as qg_scale_bytes(rows, k, 32) bytes. */
+int qg_quantize_mxfp8(const void* x, int x_dtype, int64_t rows, int64_t k, int layout, void* q,
+                      void* sf, qg_stream_t stream);
+
+/* Re-lay an NVFP4 operand between layouts (rows x k, k % 16 == 0).  Source
+ * and destination must not alias. */
+int qg_repack_nvfp4(const void* src_q, const void* src_sf, int src_layout, void* dst_q,
+                    void* dst_sf, int dst_layout, int64_t rows, int64_t k, qg_stream_t stream);
+
+/* NVFP4 x NVFP4 block-scaled GEMM on tcgen05 (kind::mxf4nvf4, block16):
+ *   C[m, n] = (a_ts * b_ts) * sum_k a(m,k) sfa(m,k/16) b(n,k) sfb(n,k/16)
+ * a_q / b_q in the MMA nibble order (M*K/2 and N*K/2 bytes), scales in
+ * `sf_layout` (QG_LAYOUT_MMA or QG_LAYOUT_MMA_KMAJOR); a_ts / b_ts point at
+ * one device float each (NULL = 1.0).  c_dtype fp32 or bf16, ldc >= n
+ * (elements).  K % 32 == 0; M, N >= 1.  `status` (device uint32, may be
+ * NULL) receives a nonzero QG device code if a bounded wait expired.
+ * Replaces the CUTLASS 72b NVFP4 GEMM backend (build_and_run.sh:38-75) and
+ * the planned nvfp4_q1_native_fp4_mainloop slot
+ * (GEMMquant_sm110/scripts/run_quant_gemm_1024.py:37-43). */
+int qg_gemm_nvfp4(const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
+                  const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
+                  int64_t k, int64_t ldc, int sf_layout, uint32_t* status, qg_stream_t stream);
+
+/* MXFP8 x MXFP8 block-scaled GEMM on tcgen05 (kind::mxf8f6f4, ue8m0 per 32
+ * K): C = sum_k a*sfa*b*sfb.  a_q / b_q are e4m3 bytes (M*K, N*K), K % 32
+ * == 0.  Replaces the unscaled FP8 stages fp8_q0..q8
+ * (GEMMquant_sm110/src/quant_gemm_bench.cu:285-662, :1314-1373) with the
+ * scaled format of cutlass-gemm-cpp-guide/cases/bs_mxfp8_1sm_p128. */
+int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, void* c,
+                  int c_dtype, int64_t m, int64_t n, int64_t k, int64_t ldc, int sf_layout,
+                  uint32_t* status, qg_stream_t stream);
+
+/* Read and clear a device status word (synchronises `stream`).  Returns
+ * QG_OK, QG_ERR_TIMEOUT or QG_ERR_CUDA; *device_code (may be NULL) gets the
+ * raw device code. */
+int qg_read_status(uint32_t* status, uint32_t* device_code, qg_stream_t stream);
+
+/* Failure-path self test: launches one CTA that waits on an mbarrier no one
+ * arrives on, bounded by `timeout_ns`, and records the timeout in *status.
+ * Exists so tests can prove the bounded-wait path returns QG_ERR_TIMEOUT
+ * without hanging the GPU.  No reference counterpart (its waits are
+ * unbounded, GEMMsm110/include/sm110_ptx_helpers.cuh:77-91). */
+int qg_selftest_wait_timeout(uint64_t timeout_ns, uint32_t* status, qg_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QGEMM_B200_H */

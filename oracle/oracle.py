@@ -1,0 +1,176 @@
+"""ctypes view of the CPU parity checker (TEST INFRASTRUCTURE ONLY).
+
+Loads oracle/_build/libqg_oracle.so (this repo's restatement, qg_oracle.cpp)
+and, when present, oracle/_ref/libqg_ref.so (the reference's own host headers
+behind ref_shim.cpp).  Only tests/, __graft_entry__.smoke() and bench.py's CPU
+baseline legs import this module.
+"""
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "_build" / "libqg_oracle.so"
+REF_SO = HERE / "_ref" / "libqg_ref.so"
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C")
+_I64, _I32, _U32, _U64, _F32, _U8 = (ctypes.c_int64, ctypes.c_int, ctypes.c_uint32,
+                                     ctypes.c_uint64, ctypes.c_float, ctypes.c_uint8)
+_fp = ctypes.POINTER(ctypes.c_float)
+
+DISTRIBUTIONS = ["uniform", "normal", "laplace", "outlier", "lognormal", "constant"]
+
+
+def build() -> None:
+    """Compile the oracle (and the reference shim when a reference checkout exists)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+
+
+def _load(path: Path) -> ctypes.CDLL:
+    if not path.exists():
+        build()
+    return ctypes.CDLL(str(path))
+
+
+class Oracle:
+    def __init__(self) -> None:
+        L = _load(ORACLE_SO)
+        sig = {
+            "qgo_encode_e2m1": (_U8, [_F32]),
+            "qgo_decode_e2m1": (_F32, [_U8]),
+            "qgo_decode_e4m3_positive": (_F32, [_U8]),
+            "qgo_encode_e4m3_round_up": (_U8, [_F32]),
+            "qgo_encode_e4m3_rn": (_U8, [_F32]),
+            "qgo_decode_e4m3": (_F32, [_U8]),
+            "qgo_decode_ue8m0": (_F32, [_U8]),
+            "qgo_pack_e2m1x2": (_U8, [_U8, _U8]),
+            "qgo_scale_offset": (_I64, [_I64, _I64, _I64, _I64, _I32, _I32]),
+            "qgo_scale_storage_size": (_I64, [_I64, _I64, _I32]),
+            "qgo_nvfp4_reference": (None, [_f32p, _I64, _u8p, _u8p, _fp]),
+            "qgo_nvfp4_quantize_mma": (None, [_f32p, _I64, _I64, _I32, _u8p, _u8p, _fp]),
+            "qgo_mxfp8_quantize": (None, [_f32p, _I64, _I64, _I32, _u8p, _u8p]),
+            "qgo_block_scaled_gemm": (None, [_f32p, _f32p, _f32p, _f32p, _I64, _I64, _I64, _I32,
+                                             _I64, _I64, _I32, _f32p]),
+            "qgo_nvfp4_decode_mma": (None, [_u8p, _u8p, _I64, _I64, _I32, _f32p, _f32p]),
+            "qgo_mxfp8_decode": (None, [_u8p, _u8p, _I64, _I64, _I32, _f32p, _f32p]),
+            "qgo_fill_normal": (None, [_f32p, _I64, _U64, _F32, _F32]),
+            "qgo_fill_requant_dist": (None, [_f32p, _I64, _U32, _I32]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        self.L = L
+
+    # -- inputs
+    def normal(self, n: int, seed: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        self.L.qgo_fill_normal(out, n, seed, mean, std)
+        return out
+
+    def requant_dist(self, n: int, dist: str, seed: int = 1234) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        self.L.qgo_fill_requant_dist(out, n, seed, DISTRIBUTIONS.index(dist))
+        return out
+
+    # -- NVFP4
+    def nvfp4_reference(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        nb = (x.size + 15) // 16
+        q = np.zeros(nb * 8, np.uint8)
+        sf = np.zeros(nb, np.uint8)
+        ts = ctypes.c_float(0)
+        self.L.qgo_nvfp4_reference(x, x.size, q, sf, ctypes.byref(ts))
+        return q, sf, ts.value
+
+    def nvfp4_mma(self, x: np.ndarray, order: int = 0):
+        rows, k = x.shape
+        x = np.ascontiguousarray(x, np.float32)
+        q = np.zeros(rows * k // 2, np.uint8)
+        sf = np.zeros(self.L.qgo_scale_storage_size(rows, k, 16), np.uint8)
+        ts = ctypes.c_float(0)
+        self.L.qgo_nvfp4_quantize_mma(x, rows, k, order, q, sf, ctypes.byref(ts))
+        return q, sf, ts.value
+
+    def nvfp4_decode(self, q, sf, rows, k, order=0):
+        v = np.empty(rows * k, np.float32)
+        s = np.empty(rows * (k // 16), np.float32)
+        self.L.qgo_nvfp4_decode_mma(np.ascontiguousarray(q), np.ascontiguousarray(sf), rows, k,
+                                    order, v, s)
+        return v, s
+
+    # -- MXFP8
+    def mxfp8(self, x: np.ndarray, order: int = 0):
+        rows, k = x.shape
+        x = np.ascontiguousarray(x, np.float32)
+        q = np.zeros(rows * k, np.uint8)
+        nsf = rows * (k // 32) if order < 0 else self.L.qgo_scale_storage_size(rows, k, 32)
+        sf = np.zeros(nsf, np.uint8)
+        self.L.qgo_mxfp8_quantize(x, rows, k, order, q, sf)
+        return q, sf
+
+    def mxfp8_decode(self, q, sf, rows, k, order=0):
+        v = np.empty(rows * k, np.float32)
+        s = np.empty(rows * (k // 32), np.float32)
+        self.L.qgo_mxfp8_decode(np.ascontiguousarray(q), np.ascontiguousarray(sf), rows, k, order,
+                                v, s)
+        return v, s
+
+    # -- O2
+    def gemm(self, a, b, sfa, sfb, m, n, k, sv, rows=None, threads=8) -> np.ndarray:
+        r0, r1 = (0, m) if rows is None else rows
+        d = np.empty((r1 - r0) * n, np.float32)
+        self.L.qgo_block_scaled_gemm(a, b, sfa, sfb, m, n, k, sv, r0, r1, threads, d)
+        return d.reshape(r1 - r0, n)
+
+
+class Reference:
+    """The reference's own host oracles (built from its headers)."""
+
+    def __init__(self) -> None:
+        if not REF_SO.exists():
+            build()
+        if not REF_SO.exists():
+            raise FileNotFoundError(f"{REF_SO} (needs the reference checkout to build)")
+        L = ctypes.CDLL(str(REF_SO))
+        sig = {
+            "qgr_encode_e2m1": (_U8, [_F32]),
+            "qgr_encode_e4m3_round_up": (_U8, [_F32]),
+            "qgr_decode_e4m3_positive": (_F32, [_U8]),
+            "qgr_nvfp4_reference": (None, [_f32p, _I64, _u8p, _u8p, _fp]),
+            "qgr_scale_offset": (_I64, [_I32, _I32, _I32, _I32, _I32]),
+            "qgr_scale_storage_size": (_I64, [_I32, _I32, _I32]),
+            "qgr_block_scaled_gemm": (None, [_f32p, _f32p, _f32p, _f32p, _I32, _I32, _I32, _I32,
+                                             _I32, _I32, _I32, _f32p]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        self.L = L
+
+    def nvfp4_reference(self, x: np.ndarray):
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        nb = (x.size + 15) // 16
+        q = np.zeros(nb * 8, np.uint8)
+        sf = np.zeros(nb, np.uint8)
+        ts = ctypes.c_float(0)
+        self.L.qgr_nvfp4_reference(x, x.size, q, sf, ctypes.byref(ts))
+        return q, sf, ts.value
+
+    def gemm(self, a, b, sfa, sfb, m, n, k, sv, rows=None, threads=1) -> np.ndarray:
+        r0, r1 = (0, m) if rows is None else rows
+        d = np.empty((r1 - r0) * n, np.float32)
+        self.L.qgr_block_scaled_gemm(a, b, sfa, sfb, m, n, k, sv, r0, r1, threads, d)
+        return d.reshape(r1 - r0, n)
+
+
+def reference_available() -> bool:
+    try:
+        Reference()
+        return True
+    except (FileNotFoundError, OSError, subprocess.CalledProcessError):
+        return False
