@@ -41,7 +41,9 @@ struct TileCfg {
   static constexpr int kBBytes = kBN * kBKBytes;
   static constexpr int kSfaBytes = kSfChunks * 512 * (kBM / 128);
   static constexpr int kSfbBytes = kSfChunks * 512 * (kBN / 128);
-  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr int kStageTx = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  // Stage bases stay 1024-byte aligned (SWIZZLE_128B atom).
+  static constexpr int kStageBytes = (kStageTx + 1023) / 1024 * 1024;
   static constexpr int kSmemBytes = kStages * kStageBytes + 256 /*barriers*/ + 1024 /*align*/;
   // TMEM columns: accumulator [0, kBN), then per-stage scale slots.
   static constexpr int kSfaCols = kSfChunks * 4;
@@ -57,6 +59,44 @@ struct TileCfg {
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Store 32 consecutive accumulator columns of one output row.
+template <bool kOutBf16>
+__device__ __forceinline__ void store_run(const GemmParams& p, int row, int col0,
+                                          const uint32_t (&r)[32], float alpha) {
+  if (kOutBf16) {
+    __nv_bfloat16* crow = reinterpret_cast<__nv_bfloat16*>(p.c) + row * p.ldc;
+    if (p.vec_ok && col0 + 32 <= p.n) {
+      uint4* dst = reinterpret_cast<uint4*>(crow + col0);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        uint4 w;
+        w.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]) * alpha, __uint_as_float(r[v * 8 + 1]) * alpha);
+        w.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]) * alpha, __uint_as_float(r[v * 8 + 3]) * alpha);
+        w.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]) * alpha, __uint_as_float(r[v * 8 + 5]) * alpha);
+        w.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]) * alpha, __uint_as_float(r[v * 8 + 7]) * alpha);
+        dst[v] = w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.n) crow[col0 + j] = __float2bfloat16_rn(__uint_as_float(r[j]) * alpha);
+    }
+  } else {
+    float* crow = reinterpret_cast<float*>(p.c) + row * p.ldc;
+    if (p.vec_ok && col0 + 32 <= p.n) {
+      float4* dst = reinterpret_cast<float4*>(crow + col0);
+#pragma unroll
+      for (int v = 0; v < 8; ++v)
+        dst[v] = make_float4(__uint_as_float(r[v * 4 + 0]) * alpha, __uint_as_float(r[v * 4 + 1]) * alpha,
+                             __uint_as_float(r[v * 4 + 2]) * alpha, __uint_as_float(r[v * 4 + 3]) * alpha);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.n) crow[col0 + j] = __uint_as_float(r[j]) * alpha;
+    }
+  }
 }
 
 template <bool kFp4, bool kOutBf16>
@@ -126,7 +166,7 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* sb = sa + Cfg::kABytes;
           uint8_t* ssfa = sb + Cfg::kBBytes;
           uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
-          mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageTx);
           tma_load_2d(sa, &p.tm_a, &full_bar[stage], kb * Cfg::kBKBytes, mt * Cfg::kBM, pol_a);
           tma_load_2d(sb, &p.tm_b, &full_bar[stage], kb * Cfg::kBKBytes, nt * Cfg::kBN, pol_a);
           tma_load_3d(ssfa, &p.tm_sfa, &full_bar[stage], 0, mt * (Cfg::kBM / 128),
@@ -246,6 +286,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
       for (int cc = 0; cc < Cfg::kBN / 32; ++cc) {
         uint32_t r[32];
+        __syncwarp();
         tmem_ld_32x32b_x32(t_row + cc * 32, r);
         tmem_wait_ld();
         if (cc == Cfg::kBN / 32 - 1) {
@@ -255,47 +296,8 @@ __global__ void __launch_bounds__(192, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(acc_empty);
         }
-        if (row >= p.m) continue;
         const int col0 = nt * Cfg::kBN + cc * 32;
-        if (col0 >= p.n) continue;
-        if (kOutBf16) {
-          __nv_bfloat16* crow = reinterpret_cast<__nv_bfloat16*>(p.c) + row * p.ldc;
-          if (p.vec_ok && col0 + 32 <= p.n) {
-            uint4* dst = reinterpret_cast<uint4*>(crow + col0);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]) * alpha,
-                                __uint_as_float(r[v * 8 + 1]) * alpha);
-              w.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]) * alpha,
-                                __uint_as_float(r[v * 8 + 3]) * alpha);
-              w.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]) * alpha,
-                                __uint_as_float(r[v * 8 + 5]) * alpha);
-              w.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]) * alpha,
-                                __uint_as_float(r[v * 8 + 7]) * alpha);
-              dst[v] = w;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.n) crow[col0 + j] = __float2bfloat16_rn(__uint_as_float(r[j]) * alpha);
-          }
-        } else {
-          float* crow = reinterpret_cast<float*>(p.c) + row * p.ldc;
-          if (p.vec_ok && col0 + 32 <= p.n) {
-            float4* dst = reinterpret_cast<float4*>(crow + col0);
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              dst[v] = make_float4(
-                  __uint_as_float(r[v * 4 + 0]) * alpha, __uint_as_float(r[v * 4 + 1]) * alpha,
-                  __uint_as_float(r[v * 4 + 2]) * alpha, __uint_as_float(r[v * 4 + 3]) * alpha);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < p.n) crow[col0 + j] = __uint_as_float(r[j]) * alpha;
-          }
-        }
+        if (row < p.m && col0 < p.n) store_run<kOutBf16>(p, row, col0, r, alpha);
       }
     }
   }
