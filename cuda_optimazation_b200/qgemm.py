@@ -42,6 +42,8 @@ SIGNATURES = {
     "qg_scale_bytes": (_I64, [_I64, _I64, _I32]),
     "qg_quantize_workspace_bytes": (ctypes.c_size_t, []),
     "qg_quantize_nvfp4": (_I32, [_VP, _I32, _I64, _I64, _I32, _VP, _VP, _VP, _VP, _VP]),
+    "qg_quantize_nvfp4_noalloc": (_I32, [_VP, _I32, _I64, _I64, _I32, _VP, _VP, _VP, _VP]),
+    "qg_quantize_nvfp4_noalloc_max_elements": (_I64, []),
     "qg_quantize_mxfp8": (_I32, [_VP, _I32, _I64, _I64, _I32, _VP, _VP, _VP]),
     "qg_repack_nvfp4": (_I32, [_VP, _VP, _I32, _VP, _VP, _I32, _I64, _I64, _VP]),
     "qg_gemm_nvfp4": (_I32, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64, _I64,

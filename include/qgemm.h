@@ -95,6 +95,26 @@ size_t qg_quantize_workspace_bytes(void);
 int qg_quantize_nvfp4(const void* x, int x_dtype, int64_t rows, int64_t k, int layout, void* q,
                       void* sf, float* ts, void* workspace, qg_stream_t stream);
 
+/* qg_quantize_nvfp4 without the workspace argument, for callers that cannot
+ * allocate device memory: plugins hosted by a framework that owns every
+ * device allocation and hands over only the call's tensors, allocator-free
+ * embedded runtimes, code called back from inside a memory allocator, and
+ * latency-critical loops that cannot afford cudaMalloc's implicit device
+ * synchronisation.  No counterpart in the reference.  Same outputs as
+ * qg_quantize_nvfp4, bit for bit.  Its scratch is a fixed 64.25 KiB array in
+ * the library's device memory (held by every GPU that loads the library until
+ * exit), which bounds the input to qg_quantize_nvfp4_noalloc_max_elements()
+ * = 2^28 elements; larger inputs return QG_ERR_SHAPE.  The array's device
+ * address is looked up on the first call on each device, so make that first
+ * call before any stream capture.  All calls share the array: calls that may
+ * overlap on the GPU race and must be ordered by the caller.  Allocates
+ * nothing (no cudaMalloc / cudaFree, no allocating library routine). */
+int qg_quantize_nvfp4_noalloc(const void* x, int x_dtype, int64_t rows, int64_t k, int layout,
+                              void* q, void* sf, float* ts, qg_stream_t stream);
+
+/* Largest rows * k qg_quantize_nvfp4_noalloc accepts. */
+int64_t qg_quantize_nvfp4_noalloc_max_elements(void);
+
 /* MXFP8 quantizer (OCP MX v1.0; the reference has none): x (rows x k) ->
  * e4m3 values `q` (rows*k bytes) and ue8m0 scales per 32 K elements, scale
  * exponent floor(log2(block amax)) - 8 clamped to [-127, 127] (all-zero
