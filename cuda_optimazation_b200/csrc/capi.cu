@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -95,6 +96,32 @@ uint64_t default_timeout_ns() {
   return t;
 }
 
+// QG_DIAG_FLAGS: diagnostic switches of the pair kernel (see GemmParams).
+uint32_t diag_flags() {
+  static const uint32_t f = [] {
+    const char* e = std::getenv("QG_DIAG_FLAGS");
+    return e ? static_cast<uint32_t>(std::strtoul(e, nullptr, 0)) : 0u;
+  }();
+  return f;
+}
+
+// GEMM kernel variant: 0 = single CTA with tcgen05.st scale staging,
+// 1 = CTA pair, 2 = single CTA with tcgen05.cp scale copies.  Measured on
+// B200: NVFP4 (12 scale copies per stage) is fastest with 0, MXFP8 (3 per
+// stage) with 2; QG_GEMM_VARIANT=solo|pair|1cta overrides for A/B runs.
+int gemm_variant(bool fp4) {
+  static const int forced = [] {
+    const char* e = std::getenv("QG_GEMM_VARIANT");
+    if (!e) return -1;
+    if (std::strcmp(e, "solo") == 0) return 0;
+    if (std::strcmp(e, "pair") == 0) return 1;
+    if (std::strcmp(e, "1cta") == 0) return 2;
+    return -1;
+  }();
+  if (forced >= 0) return forced;
+  return fp4 ? 0 : 2;
+}
+
 int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
                 const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
                 int64_t k, int64_t ldc, int sf_layout, uint32_t* status, cudaStream_t stream) {
@@ -110,31 +137,47 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
   if (int d = check_device()) return d;
   if (!encode_fn()) return QG_ERR_CUDA;
   const int sv = fp4 ? 16 : 32;
-  const int bm = gemm_tile_m(), bn = gemm_tile_n();
+  const int variant = gemm_variant(fp4);
+  const bool pair = variant == 1;
+  // Tile of one scheduling unit (a CTA pair: 256 x 256; one CTA: 128 x 256)
+  // and the rows each CTA's TMA boxes cover.
+  const int tm = pair ? pair_tile_m() : gemm_tile_m();
+  const int tn = pair ? pair_tile_n() : gemm_tile_n();
+  const int box_a = pair ? tm / 2 : tm;
+  const int box_b = pair ? tn / 2 : tn;
   const int chunks = gemm_sf_chunks_per_stage(fp4);
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
-  if (!make_operand_map(&p.tm_a, a_q, m, row_bytes, bm)) return QG_ERR_CUDA;
-  if (!make_operand_map(&p.tm_b, b_q, n, row_bytes, bn)) return QG_ERR_CUDA;
-  if (!make_scale_map(&p.tm_sfa, a_sf, m, k, sv, sf_layout, bm / 128, chunks)) return QG_ERR_CUDA;
-  if (!make_scale_map(&p.tm_sfb, b_sf, n, k, sv, sf_layout, bn / 128, chunks)) return QG_ERR_CUDA;
+  if (!make_operand_map(&p.tm_a, a_q, m, row_bytes, box_a)) return QG_ERR_CUDA;
+  if (!make_operand_map(&p.tm_b, b_q, n, row_bytes, box_b)) return QG_ERR_CUDA;
+  if (!make_scale_map(&p.tm_sfa, a_sf, m, k, sv, sf_layout, box_a / 128, chunks)) return QG_ERR_CUDA;
+  if (!make_scale_map(&p.tm_sfb, b_sf, n, k, sv, sf_layout, tn / 128, chunks)) return QG_ERR_CUDA;
   const int esize = c_dtype == QG_DTYPE_BF16 ? 2 : 4;
   p.c = c;
   p.ldc = ldc;
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
-  p.num_m_tiles = static_cast<int>((m + bm - 1) / bm);
-  p.num_n_tiles = static_cast<int>((n + bn - 1) / bn);
+  p.num_m_tiles = static_cast<int>((m + tm - 1) / tm);
+  p.num_n_tiles = static_cast<int>((n + tn - 1) / tn);
   p.num_k_blocks = static_cast<int>((row_bytes + gemm_stage_k_bytes() - 1) / gemm_stage_k_bytes());
   p.vec_ok = aligned16(c) && ((ldc * esize) % 16 == 0);
   p.a_ts = fp4 ? a_ts : nullptr;
   p.b_ts = fp4 ? b_ts : nullptr;
   p.status = status;
   p.timeout_ns = default_timeout_ns();
+  p.diag = diag_flags();
   const int64_t tiles = static_cast<int64_t>(p.num_m_tiles) * p.num_n_tiles;
-  const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  cudaError_t e = launch_gemm_blockscaled(p, fp4, c_dtype == QG_DTYPE_BF16, grid, stream);
+  cudaError_t e;
+  if (pair) {
+    const int64_t pairs = num_sms() / 2;
+    const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
+    e = launch_gemm_pair(p, fp4, c_dtype == QG_DTYPE_BF16, grid, stream);
+  } else {
+    const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
+    e = variant == 2 ? launch_gemm_blockscaled(p, fp4, c_dtype == QG_DTYPE_BF16, grid, stream)
+                            : launch_gemm_solo(p, fp4, c_dtype == QG_DTYPE_BF16, grid, stream);
+  }
   return e == cudaSuccess ? QG_OK : QG_ERR_CUDA;
 }
 

@@ -21,10 +21,20 @@ struct GemmParams {
   const float* b_ts;
   uint32_t* status;
   uint64_t timeout_ns;
+  // Diagnostics only (QG_DIAG_FLAGS; results are wrong when set): bit 0
+  // skips scale staging, bit 1 the MMAs, bit 2 the TMA loads, bit 3 the
+  // epilogue stores.  Used to attribute kernel time to its parts.
+  uint32_t diag;
 };
 
 cudaError_t launch_gemm_blockscaled(const GemmParams& p, bool fp4, bool out_bf16, int grid,
                                     cudaStream_t stream);
+cudaError_t launch_gemm_pair(const GemmParams& p, bool fp4, bool out_bf16, int grid,
+                             cudaStream_t stream);
+cudaError_t launch_gemm_solo(const GemmParams& p, bool fp4, bool out_bf16, int grid,
+                             cudaStream_t stream);
+int pair_tile_m();
+int pair_tile_n();
 int gemm_tile_m();
 int gemm_tile_n();
 int gemm_stage_k_bytes();
