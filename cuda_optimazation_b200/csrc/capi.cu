@@ -106,10 +106,13 @@ uint32_t diag_flags() {
 }
 
 // GEMM kernel variant: 0 = single CTA with tcgen05.st scale staging,
-// 1 = CTA pair, 2 = single CTA with tcgen05.cp scale copies.  Measured on
-// B200: NVFP4 (12 scale copies per stage) is fastest with 0, MXFP8 (3 per
-// stage) with 2; QG_GEMM_VARIANT=solo|pair|1cta overrides for A/B runs.
-int gemm_variant(bool fp4) {
+// 1 = CTA pair with tcgen05.st staging, 2 = single CTA with tcgen05.cp scale
+// copies.  Measured on B200 (8192^3 NVFP4 / 4096x14336x4096 MXFP8): NVFP4 is
+// fastest on the pair (4.0 PF/s vs 3.9 single, 3.1 with copies), MXFP8, with
+// only 3 scale copies per stage, on 2 (2.1 PF/s vs 2.0 pair).  Problems of
+// at most 128 rows use the single CTA (the pair's 256-row tile would be half
+// empty).  QG_GEMM_VARIANT=solo|pair|1cta overrides for A/B runs.
+int gemm_variant(bool fp4, int64_t m) {
   static const int forced = [] {
     const char* e = std::getenv("QG_GEMM_VARIANT");
     if (!e) return -1;
@@ -119,7 +122,8 @@ int gemm_variant(bool fp4) {
     return -1;
   }();
   if (forced >= 0) return forced;
-  return fp4 ? 0 : 2;
+  if (!fp4) return 2;
+  return m > 128 ? 1 : 0;
 }
 
 int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
@@ -137,7 +141,7 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
   if (int d = check_device()) return d;
   if (!encode_fn()) return QG_ERR_CUDA;
   const int sv = fp4 ? 16 : 32;
-  const int variant = gemm_variant(fp4);
+  const int variant = gemm_variant(fp4, m);
   const bool pair = variant == 1;
   // Tile of one scheduling unit (a CTA pair: 256 x 256; one CTA: 128 x 256)
   // and the rows each CTA's TMA boxes cover.

@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t phase = static_cast<uint32_t>((g / Cfg::kStages) & 1);
       bool ok = true;
       if (lane == 0)
-        ok = mbar_wait_bounded<false, 32>(&full_bar[stage], phase, p.timeout_ns, abort_flag,
+        ok = mbar_wait_bounded(&full_bar[stage], phase, p.timeout_ns, abort_flag,
                                           p.status, kDevTimeoutMma);
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
       mbar_try_wait(&full_bar[stage], phase);  // acquire for every lane

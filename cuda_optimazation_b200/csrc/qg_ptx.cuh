@@ -447,3 +447,12 @@ __device__ __forceinline__ void tmem_cp_pair_32x128b_warpx4(uint32_t taddr, uint
                : "memory");
 }
 }  // namespace qg
+
+namespace qg {
+// Remote arrive without the release fence (relaxed); ordering of prior TMEM
+// writes comes from tcgen05.wait::st + tcgen05.fence::before_thread_sync.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+}  // namespace qg
