@@ -311,6 +311,68 @@ int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void
                      sf_layout, status, reinterpret_cast<cudaStream_t>(stream));
 }
 
+// Workspace of qg_gemm_nvfp4_skinny: fp32 partial sums [m][n], then the
+// quantised activations (values, scales, tensor scale, amax word), each
+// 256-byte aligned.
+static int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+size_t qg_gemm_nvfp4_skinny_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  if (m < 1 || n < 1 || k < 1) return 0;
+  return static_cast<size_t>(align256(m * n * 4) + align256(m * k / 2) +
+                             align256(qg_scale_bytes(m, k, 16)) + 512);
+}
+
+int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q, const void* w_sf,
+                         const float* w_ts, void* c, int c_dtype, int64_t n, int64_t k,
+                         int64_t ldc, int sf_layout, void* workspace, size_t workspace_bytes,
+                         uint32_t* status, qg_stream_t stream) {
+  if (!x || !w_q || !w_sf || !c || !workspace) return QG_ERR_ARG;
+  if (x_dtype != QG_DTYPE_F32 && x_dtype != QG_DTYPE_BF16) return QG_ERR_DTYPE;
+  if (c_dtype != QG_DTYPE_F32 && c_dtype != QG_DTYPE_BF16) return QG_ERR_DTYPE;
+  if (sf_layout != QG_LAYOUT_MMA && sf_layout != QG_LAYOUT_MMA_KMAJOR) return QG_ERR_LAYOUT;
+  if (m < 1 || m > 128 || n < 1 || k < 32 || (k % 32) != 0 || ldc < n) return QG_ERR_SHAPE;
+  if (n > (1ll << 31) - 1 || k > (1ll << 31) - 1) return QG_ERR_SHAPE;
+  if (workspace_bytes < qg_gemm_nvfp4_skinny_workspace_bytes(m, n, k)) return QG_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w_q) || !aligned16(w_sf) || !aligned16(workspace))
+    return QG_ERR_ALIGN;
+  if (int d = check_device()) return d;
+  if (!encode_fn()) return QG_ERR_CUDA;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  float* ws = reinterpret_cast<float*>(base);
+  uint8_t* xq = base + align256(m * n * 4);
+  uint8_t* xsf = xq + align256(m * k / 2);
+  float* xts = reinterpret_cast<float*>(xsf + align256(qg_scale_bytes(m, k, 16)));
+  void* amax_ws = xts + 64;  // 256 bytes past the tensor scale
+  // 1. zero the partial sums; 2. quantise the activations (fused into this
+  // call); 3. stream-K GEMM; 4. scale + convert.
+  if (cudaMemsetAsync(ws, 0, static_cast<size_t>(m * n * 4), s) != cudaSuccess) return QG_ERR_CUDA;
+  if (int r = qg_quantize_nvfp4(x, x_dtype, m, k, QG_LAYOUT_MMA, xq, xsf, xts, amax_ws, stream))
+    return r;
+  const int mma_n = skinny_mma_n(m);
+  SkinnyParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int64_t row_bytes = k / 2;
+  if (!make_operand_map(&p.tm_w, w_q, n, row_bytes, 128)) return QG_ERR_CUDA;
+  if (!make_operand_map(&p.tm_x, xq, m, row_bytes, mma_n)) return QG_ERR_CUDA;
+  if (!make_scale_map(&p.tm_sfw, w_sf, n, k, 16, sf_layout, 1, 4)) return QG_ERR_CUDA;
+  if (!make_scale_map(&p.tm_sfx, xsf, m, k, 16, QG_LAYOUT_MMA, 1, 4)) return QG_ERR_CUDA;
+  p.ws = ws;
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.num_tiles = static_cast<int>((n + 127) / 128);
+  p.num_k_blocks = static_cast<int>((row_bytes + 127) / 128);
+  p.status = status;
+  p.timeout_ns = default_timeout_ns();
+  const int64_t units = static_cast<int64_t>(p.num_tiles) * p.num_k_blocks;
+  const int grid = static_cast<int>(units < num_sms() ? units : num_sms());
+  if (launch_gemm_skinny(p, grid, s) != cudaSuccess) return QG_ERR_CUDA;
+  if (launch_skinny_finish(ws, c, c_dtype == QG_DTYPE_BF16, m, n, ldc, xts, w_ts, s) !=
+      cudaSuccess)
+    return QG_ERR_CUDA;
+  return QG_OK;
+}
+
 int qg_read_status(uint32_t* status, uint32_t* device_code, qg_stream_t stream) {
   if (!status) return QG_ERR_ARG;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

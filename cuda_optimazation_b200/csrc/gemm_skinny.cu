@@ -1,0 +1,331 @@
+// gemm_skinny.cu -- decode-shaped NVFP4 GEMM (few activation rows, large
+// weight matrix), HBM-bound.
+//
+// C[m, n] = (ts_x * ts_w) * sum_k x(m,k) w(n,k), m <= 128, computed as
+// C^T = W . X^T so the weight rows fill the tensor core's M = 128 side and the
+// activation rows its N side (16 / 32 / 64 / 128).  The reference has no
+// kernel for this shape (its harness only runs square problems,
+// GEMMquant_sm110/src/quant_gemm_bench.cu:3038-3079); BASELINE config 4 names
+// it.  The weights are streamed once from HBM; every CTA takes an equal,
+// contiguous range of (weight-tile, K-block) units ("stream-K"), so the
+// 224 x 32 units of N = 28672, K = 8192 spread evenly over 148 SMs.  A tile
+// split between CTAs is summed with fp32 reductions into a zeroed workspace;
+// a finishing kernel applies the tensor scales and writes bf16 / fp32.
+//
+// Roles (10 warps): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
+// warps 2..5 epilogue (one TMEM quadrant each: lane = weight row), warps 6..9
+// scale stagers (tcgen05.st, as in gemm_solo.cu).  The accumulator is double
+// buffered so a segment's reduction overlaps the next segment's mainloop.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "qg_gemm.h"
+#include "qg_ptx.cuh"
+
+namespace qg {
+
+template <int kN>
+struct SkinnyCfg {
+  static constexpr int kBM = 128;       // weight rows per tile
+  static constexpr int kBKBytes = 128;  // 256 fp4 of K per stage
+  static constexpr int kStages = kN >= 128 ? 6 : 8;
+  static constexpr int kMmaPerStage = 4;
+  static constexpr int kSfChunks = 4;
+  static constexpr int kWBytes = kBM * kBKBytes;
+  static constexpr int kXBytes = kN * kBKBytes;
+  static constexpr int kSfwBytes = kSfChunks * 512;
+  static constexpr int kSfxBytes = kSfChunks * 512;
+  static constexpr int kStageTx = kWBytes + kXBytes + kSfwBytes + kSfxBytes;
+  static constexpr int kStageBytes = (kStageTx + 1023) / 1024 * 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 512 + 1024;
+  static constexpr int kSfStageCols = 32;  // 16 weight + 16 activation
+  static constexpr int kTmemSfBase = 256;
+  static constexpr int kTmemCols = 512;
+  static_assert(2 * kN <= kTmemSfBase, "accumulators");
+  static_assert(kTmemSfBase + kStages * kSfStageCols <= kTmemCols, "TMEM budget");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static constexpr int kThreads = 320;
+};
+
+// Walk of one CTA's unit range: a "segment" is a run of K-blocks of one tile.
+struct UnitRange {
+  int u0, u1, nkb;
+  __device__ __forceinline__ bool seg_start(int u) const { return u == u0 || (u % nkb) == 0; }
+  __device__ __forceinline__ bool seg_end(int u) const {
+    return u == u1 - 1 || (u % nkb) == nkb - 1;
+  }
+};
+
+template <int kN>
+__global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_constant__ SkinnyParams p) {
+  using Cfg = SkinnyCfg<kN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  uint64_t* full_bar = bars;
+  uint64_t* sf_ready = bars + Cfg::kStages;
+  uint64_t* empty_bar = bars + 2 * Cfg::kStages;
+  uint64_t* acc_full = bars + 3 * Cfg::kStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;            // [2]
+  uint64_t* drain_bar = acc_full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 5);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&sf_ready[s], 4);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0u;
+    fence_barrier_init();
+    tma_prefetch_desc(&p.tm_w);
+    tma_prefetch_desc(&p.tm_x);
+    tma_prefetch_desc(&p.tm_sfw);
+    tma_prefetch_desc(&p.tm_sfx);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int64_t units = static_cast<int64_t>(p.num_tiles) * p.num_k_blocks;
+  UnitRange ur;
+  ur.u0 = static_cast<int>(units * blockIdx.x / gridDim.x);
+  ur.u1 = static_cast<int>(units * (blockIdx.x + 1) / gridDim.x);
+  ur.nkb = p.num_k_blocks;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();  // weights: streamed once
+      const uint64_t pol_x = l2_policy_evict_last();   // activations: reused by all CTAs
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int u = ur.u0, g = 0; u < ur.u1; ++u, ++g) {
+        const int stage = g % Cfg::kStages;
+        const uint32_t phase = static_cast<uint32_t>((g / Cfg::kStages) & 1);
+        const int tile = u / ur.nkb, kb = u % ur.nkb;
+        if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.timeout_ns, abort_flag, p.status,
+                               kDevTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sw = smem + stage * Cfg::kStageBytes;
+        uint8_t* sx = sw + Cfg::kWBytes;
+        uint8_t* ssfw = sx + Cfg::kXBytes;
+        uint8_t* ssfx = ssfw + Cfg::kSfwBytes;
+        mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageTx);
+        tma_load_3d(ssfw, &p.tm_sfw, &full_bar[stage], 0, tile, kb * Cfg::kSfChunks, pol_w);
+        tma_load_3d(ssfx, &p.tm_sfx, &full_bar[stage], 0, 0, kb * Cfg::kSfChunks, pol_x);
+        tma_load_2d(sx, &p.tm_x, &full_bar[stage], kb * Cfg::kBKBytes, 0, pol_x);
+        tma_load_2d(sw, &p.tm_w, &full_bar[stage], kb * Cfg::kBKBytes, tile * Cfg::kBM, pol_w);
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+      }
+      if (!ok) {
+        uint32_t dummy = 0;
+        for (int s = 0; s < Cfg::kStages; ++s)
+          if (issued_mask & (1u << s))
+            mbar_wait_bounded(&full_bar[s], (issued_parity >> s) & 1u, p.timeout_ns, &dummy,
+                              nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_block_scaled(Cfg::kBM, kN, 1u, 0u, 0u, 0u);
+      bool ok = true;
+      int seg = 0;
+      uint32_t acc = 0;
+      for (int u = ur.u0, g = 0; u < ur.u1 && ok; ++u, ++g) {
+        const int stage = g % Cfg::kStages;
+        const uint32_t phase = static_cast<uint32_t>((g / Cfg::kStages) & 1);
+        const int buf = seg & 1;
+        if (ur.seg_start(u)) {
+          if (!mbar_wait_bounded(&acc_empty[buf], ((seg >> 1) & 1) ^ 1u, p.timeout_ns, abort_flag,
+                                 p.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          acc = 0;
+        }
+        if (!mbar_wait_bounded(&sf_ready[stage], phase, p.timeout_ns, abort_flag, p.status,
+                               kDevTimeoutMma) ||
+            !mbar_wait_bounded(&full_bar[stage], phase, p.timeout_ns, abort_flag, p.status,
+                               kDevTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint8_t* sw = smem + stage * Cfg::kStageBytes;
+        uint8_t* sx = sw + Cfg::kWBytes;
+        const uint32_t sfw_col = tmem_base + Cfg::kTmemSfBase + stage * Cfg::kSfStageCols;
+        const uint32_t sfx_col = sfw_col + 16;
+        const uint64_t wdesc = make_smem_desc(smem_u32(sw), 16, 1024, kSwizzle128B);
+        const uint64_t xdesc = make_smem_desc(smem_u32(sx), 16, 1024, kSwizzle128B);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kN);
+#pragma unroll
+        for (int j = 0; j < Cfg::kMmaPerStage; ++j) {
+          const uint64_t koff = static_cast<uint64_t>(j * 2);
+          mma_mxf4nvf4(d_tmem, wdesc + koff, xdesc + koff, idesc, sfw_col + j * 4,
+                       sfx_col + j * 4, acc);
+          acc = 1;
+        }
+        tc_commit(&empty_bar[stage]);
+        if (ur.seg_end(u)) {
+          tc_commit(&acc_full[buf]);
+          ++seg;
+        }
+      }
+      tc_commit(drain_bar);
+      uint32_t dummy = 0;
+      mbar_wait_bounded(drain_bar, 0, p.timeout_ns, &dummy, nullptr, 0);
+    }
+  } else if (warp >= 6) {
+    // ---------------------------------------------------------------- scale stagers
+    const int quad = warp % 4;
+    const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    for (int u = ur.u0, g = 0; u < ur.u1; ++u, ++g) {
+      const int stage = g % Cfg::kStages;
+      const uint32_t phase = static_cast<uint32_t>((g / Cfg::kStages) & 1);
+      bool ok = true;
+      if (lane == 0)
+        ok = mbar_wait_bounded(&full_bar[stage], phase, p.timeout_ns, abort_flag, p.status,
+                               kDevTimeoutMma);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      mbar_try_wait(&full_bar[stage], phase);
+      const uint8_t* ssfw = smem + stage * Cfg::kStageBytes + Cfg::kWBytes + Cfg::kXBytes;
+      const uint8_t* ssfx = ssfw + Cfg::kSfwBytes;
+      uint32_t a[16], b[16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 v = lds128(ssfw + c * 512 + lane * 16);
+        const uint4 w = lds128(ssfx + c * 512 + lane * 16);
+        a[4 * c] = v.x; a[4 * c + 1] = v.y; a[4 * c + 2] = v.z; a[4 * c + 3] = v.w;
+        b[4 * c] = w.x; b[4 * c + 1] = w.y; b[4 * c + 2] = w.z; b[4 * c + 3] = w.w;
+      }
+      const uint32_t col = Cfg::kTmemSfBase + stage * Cfg::kSfStageCols;
+      tmem_st_32x32b<16>(t_quad + col, a);
+      tmem_st_32x32b<16>(t_quad + col + 16, b);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sf_ready[stage]);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int quad = warp % 4;
+    const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    int seg = 0;
+    for (int u = ur.u0; u < ur.u1; ++u) {
+      if (!ur.seg_end(u)) continue;
+      const int buf = seg & 1;
+      bool ok = true;
+      if (lane == 0)
+        ok = mbar_wait_bounded<false, 128>(&acc_full[buf], (seg >> 1) & 1, p.timeout_ns,
+                                           abort_flag, p.status, kDevTimeoutEpilogue);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      mbar_try_wait(&acc_full[buf], (seg >> 1) & 1);
+      tc_fence_after();
+      const int n = (u / ur.nkb) * Cfg::kBM + quad * 32 + lane;  // weight row = output column
+      const bool n_ok = n < p.n;
+#pragma unroll
+      for (int cc = 0; cc < kN / 16; ++cc) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(t_quad + static_cast<uint32_t>(buf * kN + cc * 16), r);
+        tmem_wait_ld();
+        if (cc == kN / 16 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = cc * 16 + j;
+          if (n_ok && m < p.m)
+            atomicAdd(p.ws + static_cast<int64_t>(m) * p.n + n, __uint_as_float(r[j]));
+        }
+      }
+      ++seg;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// C[m, n] = alpha * ws[m, n] (bf16 or fp32), alpha = product of the tensor
+// scales read from the device.
+template <bool kOutBf16>
+__global__ void __launch_bounds__(256)
+    skinny_finish_kernel(const float* ws, void* c, int64_t m, int64_t n, int64_t ldc,
+                         const float* a_ts, const float* b_ts) {
+  const float alpha = (a_ts ? *a_ts : 1.0f) * (b_ts ? *b_ts : 1.0f);
+  const int64_t total = m * n;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = e / n, col = e - r * n;
+    const float v = ws[e] * alpha;
+    if (kOutBf16) reinterpret_cast<__nv_bfloat16*>(c)[r * ldc + col] = __float2bfloat16_rn(v);
+    else reinterpret_cast<float*>(c)[r * ldc + col] = v;
+  }
+}
+
+template <int kN>
+static cudaError_t launch_skinny_n(const SkinnyParams& p, int grid, cudaStream_t stream) {
+  using Cfg = SkinnyCfg<kN>;
+  auto kern = gemm_skinny_kernel<kN>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+int skinny_mma_n(int64_t m) { return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128; }
+
+cudaError_t launch_gemm_skinny(const SkinnyParams& p, int grid, cudaStream_t stream) {
+  switch (skinny_mma_n(p.m)) {
+    case 16: return launch_skinny_n<16>(p, grid, stream);
+    case 32: return launch_skinny_n<32>(p, grid, stream);
+    case 64: return launch_skinny_n<64>(p, grid, stream);
+    default: return launch_skinny_n<128>(p, grid, stream);
+  }
+}
+
+cudaError_t launch_skinny_finish(const float* ws, void* c, bool out_bf16, int64_t m, int64_t n,
+                                 int64_t ldc, const float* a_ts, const float* b_ts,
+                                 cudaStream_t stream) {
+  const int64_t blocks = (m * n + 255) / 256;
+  const int64_t cap = 4ll * num_sms();
+  const int grid = static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+  if (out_bf16) skinny_finish_kernel<true><<<grid, 256, 0, stream>>>(ws, c, m, n, ldc, a_ts, b_ts);
+  else skinny_finish_kernel<false><<<grid, 256, 0, stream>>>(ws, c, m, n, ldc, a_ts, b_ts);
+  return cudaGetLastError();
+}
+
+}  // namespace qg

@@ -27,6 +27,26 @@ struct GemmParams {
   uint32_t diag;
 };
 
+// Decode-shaped NVFP4 GEMM (gemm_skinny.cu): weights W [n][k] on the MMA's M
+// side, activations X [m][k] (m <= 128) on its N side, stream-K over
+// (weight tile, K block) units with fp32 reductions into ws [m][n].
+struct SkinnyParams {
+  CUtensorMap tm_w;    // uint8 [n][k/2], box 128 B x 128 rows, SWIZZLE_128B
+  CUtensorMap tm_x;    // uint8 [m][k/2], box 128 B x mma_n rows, SWIZZLE_128B
+  CUtensorMap tm_sfw;  // uint32 chunks, box (128, 1, 4)
+  CUtensorMap tm_sfx;
+  float* ws;
+  int m, n, k;
+  int num_tiles, num_k_blocks;
+  uint32_t* status;
+  uint64_t timeout_ns;
+};
+cudaError_t launch_gemm_skinny(const SkinnyParams& p, int grid, cudaStream_t stream);
+cudaError_t launch_skinny_finish(const float* ws, void* c, bool out_bf16, int64_t m, int64_t n,
+                                 int64_t ldc, const float* a_ts, const float* b_ts,
+                                 cudaStream_t stream);
+int skinny_mma_n(int64_t m);
+
 cudaError_t launch_gemm_blockscaled(const GemmParams& p, bool fp4, bool out_bf16, int grid,
                                     cudaStream_t stream);
 cudaError_t launch_gemm_pair(const GemmParams& p, bool fp4, bool out_bf16, int grid,

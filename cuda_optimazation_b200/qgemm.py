@@ -50,6 +50,9 @@ SIGNATURES = {
                              _I32, _VP, _VP]),
     "qg_gemm_mxfp8": (_I32, [_VP, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64, _I64, _I32, _VP,
                              _VP]),
+    "qg_gemm_nvfp4_skinny": (_I32, [_VP, _I32, _I64, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64,
+                                    _I32, _VP, ctypes.c_size_t, _VP, _VP]),
+    "qg_gemm_nvfp4_skinny_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64]),
     "qg_read_status": (_I32, [_VP, _VP, _VP]),
     "qg_selftest_wait_timeout": (_I32, [_U64, _VP, _VP]),
 }
@@ -219,6 +222,30 @@ def block_scaled_gemm(a, b, out_dtype: torch.dtype = torch.bfloat16,
     else:
         gemm_mxfp8_raw(a.quantized, a.block_scales, b.quantized, b.block_scales, out, m, n, k,
                        a.layout, status, stream)
+    return out
+
+
+def gemm_nvfp4_skinny(x: torch.Tensor, w: "Nvfp4Result", out_dtype: torch.dtype = torch.bfloat16,
+                      out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
+                      status: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Decode GEMM C = x . w^T with the activation quantisation fused in:
+    x is an (m <= 128) x k fp32/bf16 CUDA tensor, w pre-quantised NVFP4
+    weights (n x k, MMA layout)."""
+    m, k = x.shape
+    n = w.rows
+    if w.k != k:
+        raise ValueError("K mismatch")
+    if out is None:
+        out = torch.empty(m, n, dtype=out_dtype, device=x.device)
+    need = int(lib().qg_gemm_nvfp4_skinny_workspace_bytes(m, n, k))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    rc = lib().qg_gemm_nvfp4_skinny(x.data_ptr(), _dtype_code(x), m, w.quantized.data_ptr(),
+                                    w.block_scales.data_ptr(), w.tensor_scale.data_ptr(),
+                                    out.data_ptr(), _dtype_code(out), n, k, out.stride(0),
+                                    w.layout, workspace.data_ptr(), workspace.numel(),
+                                    _ptr(status), _stream(stream))
+    _check(rc, "qg_gemm_nvfp4_skinny")
     return out
 
 

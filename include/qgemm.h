@@ -151,6 +151,24 @@ int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void
                   int c_dtype, int64_t m, int64_t n, int64_t k, int64_t ldc, int sf_layout,
                   uint32_t* status, qg_stream_t stream);
 
+/* Decode-shaped NVFP4 GEMM with the activation quantisation fused into the
+ * call: x (m x k, bf16 or fp32, m <= 128) is quantised to NVFP4 exactly as
+ * qg_quantize_nvfp4 would, then C[m, n] = (ts_x * w_ts) * x_q . w_q^T with the
+ * pre-quantised weights w_q (n x k, MMA layout, scales in sf_layout).  The
+ * weights are streamed once at HBM rate (stream-K over 128-row weight tiles
+ * on every SM).  `workspace` (device, qg_gemm_nvfp4_skinny_workspace_bytes)
+ * holds the fp32 partial sums and the quantised activations.  K % 32 == 0.
+ * No reference counterpart kernel: the reference harness runs square
+ * problems only (GEMMquant_sm110/src/quant_gemm_bench.cu:3038-3079); this is
+ * the decode configuration of its quant-GEMM path. */
+int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q, const void* w_sf,
+                         const float* w_ts, void* c, int c_dtype, int64_t n, int64_t k,
+                         int64_t ldc, int sf_layout, void* workspace, size_t workspace_bytes,
+                         uint32_t* status, qg_stream_t stream);
+
+/* Workspace bytes qg_gemm_nvfp4_skinny needs. */
+size_t qg_gemm_nvfp4_skinny_workspace_bytes(int64_t m, int64_t n, int64_t k);
+
 /* Read and clear a device status word (synchronises `stream`).  Returns
  * QG_OK, QG_ERR_TIMEOUT or QG_ERR_CUDA; *device_code (may be NULL) gets the
  * raw device code. */

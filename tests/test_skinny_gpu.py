@@ -1,0 +1,67 @@
+"""GPU parity: decode-shaped NVFP4 GEMM with fused activation quantisation
+(qg_gemm_nvfp4_skinny) vs the oracle's quantiser + O2."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import check_gemm
+
+pytestmark = pytest.mark.gpu
+
+
+def activations(oracle, m, k, seed):
+    """N(0,1) with 0.1% outliers x50 (every 1000th element), bf16-rounded."""
+    x = oracle.normal(m * k, seed).reshape(m, k)
+    x.reshape(-1)[::1000] *= 50.0
+    return torch.from_numpy(x).to(torch.bfloat16)
+
+
+def run_case(qlib, oracle, m, n, k, out_dtype=torch.float32, cols=None):
+    xb = activations(oracle, m, k, 100 + m)
+    xw = oracle.normal(n * k, 7, 0.0, 0.02).reshape(n, k)
+    W = qlib.make_nvfp4(torch.from_numpy(xw).cuda())
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    c = qlib.gemm_nvfp4_skinny(xb.cuda(), W, out_dtype, status=status)
+    rc, code = qlib.read_status(status)
+    assert rc == qlib.OK, code
+    got = c.float().cpu().numpy()
+    # Oracle: quantise the (bf16-exact) activations and the weights, O2.
+    xa = xb.float().numpy()
+    qa, sa, ta = oracle.nvfp4_mma(xa, 0)
+    qw, sw, tw = oracle.nvfp4_mma(xw, 0)
+    av, asf = oracle.nvfp4_decode(qa, sa, m, k)
+    wv, wsf = oracle.nvfp4_decode(qw, sw, n, k)
+    if cols is not None:
+        wv = wv.reshape(n, k)[cols].ravel()
+        wsf = wsf.reshape(n, k // 16)[cols].ravel()
+        got = got[:, cols]
+    nn = n if cols is None else len(cols)
+    ref = oracle.gemm(av, np.ascontiguousarray(wv), asf, np.ascontiguousarray(wsf), m, nn, k, 16)
+    ref = ref * np.float32(np.float32(ta) * np.float32(tw))
+    return check_gemm(got, ref, bf16=(out_dtype == torch.bfloat16))
+
+
+@pytest.mark.parametrize("m", [1, 16, 37, 64, 128])
+def test_skinny_fp32(qlib, oracle, m):
+    run_case(qlib, oracle, m, 1000, 1024)
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 4096, 544), (64, 384, 8192), (128, 2048, 256)])
+def test_skinny_shapes_bf16(qlib, oracle, m, n, k):
+    run_case(qlib, oracle, m, n, k, torch.bfloat16)
+
+
+def test_skinny_decode_config_sampled_columns(qlib, oracle):
+    """BASELINE config 4 shape (M=16, N=28672, K=8192) with the oracle on a
+    deterministic subset of output columns spread over every weight tile."""
+    cols = np.unique(np.concatenate([np.arange(0, 28672, 97), np.arange(28544, 28672)]))
+    run_case(qlib, oracle, 16, 28672, 8192, torch.float32, cols=cols)
+
+
+def test_skinny_rejects_large_m(qlib):
+    L = qlib.lib()
+    d = torch.empty(16, dtype=torch.uint8, device="cuda")
+    rc = L.qg_gemm_nvfp4_skinny(d.data_ptr(), 1, 129, d.data_ptr(), d.data_ptr(), None,
+                                d.data_ptr(), 1, 256, 256, 256, 1, d.data_ptr(), 1 << 30, None,
+                                None)
+    assert rc == qlib.ERR_SHAPE
