@@ -28,7 +28,7 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC",
     "-Xptxas", "-v",
     f"-I{ROOT / 'include'}",
-]
+] + os.environ.get("QG_EXTRA_NVCC", "").split()
 
 
 def nvcc() -> str:

@@ -364,6 +364,7 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   p.num_k_blocks = static_cast<int>((row_bytes + 127) / 128);
   p.status = status;
   p.timeout_ns = default_timeout_ns();
+  p.diag = diag_flags();
   const int64_t units = static_cast<int64_t>(p.num_tiles) * p.num_k_blocks;
   const int grid = static_cast<int>(units < num_sms() ? units : num_sms());
   if (launch_gemm_skinny(p, grid, s) != cudaSuccess) return QG_ERR_CUDA;

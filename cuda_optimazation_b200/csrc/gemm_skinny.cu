@@ -57,6 +57,13 @@ struct UnitRange {
   }
 };
 
+// Diagnostic stamp (QG_DIAG_FLAGS bit 6): CTA 0 writes %globaltimer into
+// slot `i` of the workspace.
+__device__ __forceinline__ void trace(const SkinnyParams& p, int i) {
+  if ((p.diag & 64u) && blockIdx.x == 0 && i < 512)
+    reinterpret_cast<unsigned long long*>(p.ws)[i] = globaltimer_ns();
+}
+
 template <int kN>
 __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_constant__ SkinnyParams p) {
   using Cfg = SkinnyCfg<kN>;
@@ -103,6 +110,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  if (threadIdx.x == 0) trace(p, 0);
   const int64_t units = static_cast<int64_t>(p.num_tiles) * p.num_k_blocks;
   UnitRange ur;
   ur.u0 = static_cast<int>(units * blockIdx.x / gridDim.x);
@@ -129,6 +137,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
         uint8_t* sx = sw + Cfg::kWBytes;
         uint8_t* ssfw = sx + Cfg::kXBytes;
         uint8_t* ssfx = ssfw + Cfg::kSfwBytes;
+        trace(p, 16 + g);
         mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageTx);
         tma_load_3d(ssfw, &p.tm_sfw, &full_bar[stage], 0, tile, kb * Cfg::kSfChunks, pol_w);
         tma_load_3d(ssfx, &p.tm_sfx, &full_bar[stage], 0, 0, kb * Cfg::kSfChunks, pol_x);
@@ -173,6 +182,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
           break;
         }
         tc_fence_after();
+        trace(p, 144 + g);
         uint8_t* sw = smem + stage * Cfg::kStageBytes;
         uint8_t* sx = sw + Cfg::kWBytes;
         const uint32_t sfw_col = tmem_base + Cfg::kTmemSfBase + stage * Cfg::kSfStageCols;
@@ -210,6 +220,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
                                kDevTimeoutMma);
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
       mbar_try_wait(&full_bar[stage], phase);
+      if (lane == 0 && quad == 0) trace(p, 272 + g);
       const uint8_t* ssfw = smem + stage * Cfg::kStageBytes + Cfg::kWBytes + Cfg::kXBytes;
       const uint8_t* ssfx = ssfw + Cfg::kSfwBytes;
       uint32_t a[16], b[16];
@@ -258,7 +269,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int m = cc * 16 + j;
-          if (n_ok && m < p.m)
+          if (n_ok && m < p.m && !(p.diag & 64u))
             atomicAdd(p.ws + static_cast<int64_t>(m) * p.n + n, __uint_as_float(r[j]));
         }
       }
@@ -268,6 +279,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace(p, 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);

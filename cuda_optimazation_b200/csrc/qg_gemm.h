@@ -40,6 +40,9 @@ struct SkinnyParams {
   int num_tiles, num_k_blocks;
   uint32_t* status;
   uint64_t timeout_ns;
+  // Diagnostics (QG_DIAG_FLAGS): bit 6 writes %globaltimer stamps of CTA 0's
+  // roles into the workspace instead of results.
+  uint32_t diag;
 };
 cudaError_t launch_gemm_skinny(const SkinnyParams& p, int grid, cudaStream_t stream);
 cudaError_t launch_skinny_finish(const float* ws, void* c, bool out_bf16, int64_t m, int64_t n,
