@@ -1,0 +1,84 @@
+"""Column-parallel (N-sharded) block-scaled GEMM over several GPUs of one box.
+
+The reference is single-GPU; BASELINE config 5 asks for the quant GEMM
+C = A . B^T at M = 16384, N = 53248, K = 8192 sharded along N over 1/2/4/8
+B200s.  The scheme:
+
+* rank r owns B rows ``shard_range(N, world, r)`` and their scale rows
+  (weights are sharded once, at load time);
+* A (quantised once) is broadcast from rank 0 with NCCL;
+* every rank runs its local GEMM with no communication;
+* optionally the bf16 output shards are all-gathered over NVLink and laid out
+  as the full M x N matrix.
+
+Shards are multiples of ``align`` rows (256, the CTA-pair tile) so every rank
+runs full tiles; the last rank takes the remainder.  ``local_gemm`` is
+injectable so the partition / gather logic can be exercised on CPU ranks.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+ALIGN = 256
+
+
+def shard_range(n: int, world: int, rank: int, align: int = ALIGN) -> tuple[int, int]:
+    """[start, stop) of the B rows (output columns) owned by `rank`."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad world / rank")
+    blocks = (n + align - 1) // align
+    per = blocks // world
+    extra = blocks % world
+    b0 = rank * per + min(rank, extra)
+    b1 = b0 + per + (1 if rank < extra else 0)
+    return min(n, b0 * align), min(n, b1 * align)
+
+
+def shard_sizes(n: int, world: int, align: int = ALIGN) -> list[int]:
+    return [b - a for a, b in (shard_range(n, world, r, align) for r in range(world))]
+
+
+def broadcast_operand(tensors, src: int = 0, group=None) -> None:
+    """Broadcast the tensors of a quantised operand (values, scales, tensor
+    scale) from `src` to every rank, in place."""
+    for t in tensors:
+        dist.broadcast(t, src, group=group)
+
+
+def gather_columns(c_local: torch.Tensor, n: int, group=None, align: int = ALIGN) -> torch.Tensor:
+    """All-gather the column shards [M, n_r] of every rank into the full
+    [M, N] matrix (rank-major shards padded to the largest, then placed)."""
+    world = dist.get_world_size(group)
+    sizes = shard_sizes(n, world, align)
+    m = c_local.shape[0]
+    width = max(sizes)
+    if c_local.shape[1] != width:
+        pad = torch.zeros(m, width, dtype=c_local.dtype, device=c_local.device)
+        pad[:, : c_local.shape[1]] = c_local
+        c_local = pad
+    buf = torch.empty(world, m, width, dtype=c_local.dtype, device=c_local.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(buf, c_local.contiguous(), group=group)
+    else:  # gloo (CPU ranks) has only the list form
+        dist.all_gather(list(buf.unbind(0)), c_local.contiguous(), group=group)
+    out = torch.empty(m, n, dtype=c_local.dtype, device=c_local.device)
+    for r in range(world):
+        a, b = shard_range(n, world, r, align)
+        out[:, a:b] = buf[r, :, : b - a]
+    return out
+
+
+def colpar_gemm(a, b_local, n_total: int, local_gemm: Optional[Callable] = None,
+                gather: bool = True, group=None, **gemm_kwargs) -> torch.Tensor:
+    """One column-parallel GEMM step: local C shard = A . B_local^T, then
+    (optionally) the all-gather to the full matrix.  `local_gemm(a, b, **kw)`
+    defaults to the tcgen05 ``block_scaled_gemm``."""
+    if local_gemm is None:
+        from .qgemm import block_scaled_gemm as local_gemm
+    c_local = local_gemm(a, b_local, **gemm_kwargs)
+    if not gather or dist.get_world_size(group) == 1:
+        return c_local
+    return gather_columns(c_local, n_total, group=group)
