@@ -46,7 +46,9 @@ def needs_build() -> bool:
     if not OUT.exists():
         return True
     t = OUT.stat().st_mtime
-    deps = list(CSRC.glob("*")) + [ROOT / "include" / "qgemm.h", Path(__file__)]
+    deps = list(CSRC.glob("*")) + [ROOT / "include" / "qgemm.h", Path(__file__), HARNESS_SRC]
+    if not HARNESS_BIN.exists():
+        return True
     return any(d.stat().st_mtime > t for d in deps if d.is_file())
 
 
@@ -75,7 +77,26 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         sys.stderr.write(r.stdout + r.stderr)
         raise RuntimeError("link failed")
     os.replace(tmp, OUT)
+    build_harness()
     return OUT
+
+
+HARNESS_SRC = PKG / "harness" / "quant_gemm_bench.cpp"
+HARNESS_BIN = PKG / "bin" / "quant_gemm_sm110_bench"
+
+
+def build_harness() -> Path:
+    """The drop-in quant_gemm_sm110_bench binary, linked against the library
+    (rpath $ORIGIN/..)."""
+    HARNESS_BIN.parent.mkdir(exist_ok=True)
+    cmd = [nvcc(), "-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
+           f"-I{ROOT / 'include'}", str(HARNESS_SRC), "-o", str(HARNESS_BIN),
+           f"-L{PKG}", "-lqgemm_b200", "-Xlinker", "-rpath=$ORIGIN/.."]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError("harness build failed")
+    return HARNESS_BIN
 
 
 if __name__ == "__main__":

@@ -1,0 +1,447 @@
+// quant_gemm_bench.cpp -- drop-in benchmark binary for the reference's
+// quant-GEMM harness, running this library's B200 kernels.
+//
+// Reference surface it mirrors (GEMMquant_sm110/src/quant_gemm_bench.cu):
+//   quant_gemm_sm110_bench [N] [backend]          (:3038-3079)
+//   writes ./quant_sm110_benchmark.csv with the header
+//   BackendId,Version,N,Precision,Reference,TimeMs,GFLOPS,RatioToReference,Matched
+//   (:3092-3095) -- new columns only after Matched -- and prints
+//   backend_id=... time_ms=... work_unit=flop rate_per_second=...
+//   reference_rate_per_second=... matched=...  (:1522-1530);
+//   3 warm-up + 10 timed launches between CUDA events (:43-44, :1282-1304);
+//   exit status non-zero on a mismatch or a CUDA error (:17-27).
+// Added forms:
+//   quant_gemm_sm110_bench M N K backend [--seed S] [--out-dtype bf16|fp32]
+//   quant_gemm_sm110_bench --m=M --n=N --k=K [--iterations=I] [--swizzle=S]
+//     -- the CUTLASS example 72b command line the sweep runner shells out to
+//     (GEMMquant_sm110/build_and_run.sh:151-176); prints "Disposition:",
+//     "Avg runtime: <ms> ms" and "GFLOPS: <x>" for parse_cutlass_fp4_stdout
+//     (GEMMquant_sm110/scripts/run_quant_gemm_1024.py:404-410).
+// Backends: nvfp4_q1_native_fp4_mainloop (the reference's planned slot,
+// run_quant_gemm_1024.py:37-43), mxfp8_q0_tcgen05_block_scaled,
+// nvfp4_skinny_q0 (decode GEMM, fused activation quantisation), all.
+//
+// Inputs are seeded N(0,1) (std::mt19937_64, A: seed, B: seed ^ 0xbb67ae85),
+// quantised on the device by the library.  The check recomputes sampled
+// output rows on the host from the quantised operands the device produced
+// (double accumulation, as guide::block_scaled_reference_mnk does) and
+// applies the north-star tolerance: relative Frobenius error <= 1e-5 and
+// |err| <= 1e-3 * ||row||_2 for fp32 output, plus the bf16 rounding bound
+// for bf16 output.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <iomanip>
+#include <iostream>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "qgemm.h"
+
+namespace {
+
+constexpr int kWarmup = 3;
+constexpr int kRepeat = 10;
+
+#define CHECK_CUDA(call)                                                                   \
+  do {                                                                                     \
+    cudaError_t e_ = (call);                                                               \
+    if (e_ != cudaSuccess) {                                                               \
+      std::cerr << "CUDA error at " << __FILE__ << ":" << __LINE__ << " "                  \
+                << cudaGetErrorString(e_) << "\n";                                          \
+      std::exit(EXIT_FAILURE);                                                              \
+    }                                                                                      \
+  } while (0)
+#define CHECK_QG(call)                                                                     \
+  do {                                                                                     \
+    int s_ = (call);                                                                       \
+    if (s_ != QG_OK) {                                                                     \
+      std::cerr << "qgemm error at " << __FILE__ << ":" << __LINE__ << " "                 \
+                << qg_status_string(s_) << "\n";                                            \
+      std::exit(EXIT_FAILURE);                                                              \
+    }                                                                                      \
+  } while (0)
+
+struct Options {
+  int64_t m = 1024, n = 1024, k = 1024;
+  std::string backend = "all";
+  uint64_t seed = 20260817ull;
+  bool out_bf16 = false;
+  bool cutlass_cli = false;
+  int iterations = kRepeat;
+  bool square = true;  // N form: CSV column N = n
+};
+
+std::vector<float> normal(size_t count, uint64_t seed, float stddev = 1.0f) {
+  std::mt19937_64 rng(seed);
+  std::normal_distribution<float> d(0.0f, stddev);
+  std::vector<float> v(count);
+  for (auto& x : v) x = d(rng);
+  return v;
+}
+
+// Decoders of the device formats (format definitions: e2m1 grid, e4m3 with
+// bias 7, ue8m0 with bias 127).
+float e2m1(uint8_t c) {
+  static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  return (c & 8) ? -mag[c & 7] : mag[c & 7];
+}
+float e4m3(uint8_t b) {
+  const int e = (b >> 3) & 15, m = b & 7;
+  const float v = e == 0 ? std::ldexp(static_cast<float>(m), -9)
+                         : std::ldexp(1.0f + m / 8.0f, e - 7);
+  return (b & 0x80) ? -v : v;
+}
+float ue8m0(uint8_t b) { return std::ldexp(1.0f, static_cast<int>(b) - 127); }
+size_t scale_offset(int64_t row, int64_t sfc, int64_t rows, int64_t sf_cols) {
+  const int64_t row_blocks = (rows + 127) / 128;
+  (void)sf_cols;
+  const int64_t chunk = (sfc / 4) * row_blocks + row / 128;  // QG_LAYOUT_MMA
+  const int64_t w = row % 128;
+  return static_cast<size_t>(chunk * 512 + (w % 32) * 16 + (w / 32) * 4 + sfc % 4);
+}
+
+struct HostOperand {  // logical values and scales of one quantised operand
+  std::vector<float> v, s;
+  int64_t rows = 0, k = 0, sv = 16;
+  float ts = 1.0f;
+};
+
+HostOperand fetch_nvfp4(const void* dq, const void* dsf, const float* dts, int64_t rows,
+                        int64_t k) {
+  std::vector<uint8_t> q(rows * k / 2), sf(qg_scale_bytes(rows, k, 16));
+  CHECK_CUDA(cudaMemcpy(q.data(), dq, q.size(), cudaMemcpyDeviceToHost));
+  CHECK_CUDA(cudaMemcpy(sf.data(), dsf, sf.size(), cudaMemcpyDeviceToHost));
+  HostOperand o;
+  o.rows = rows, o.k = k, o.sv = 16;
+  CHECK_CUDA(cudaMemcpy(&o.ts, dts, 4, cudaMemcpyDeviceToHost));
+  o.v.resize(rows * k);
+  o.s.resize(rows * (k / 16));
+  for (int64_t i = 0; i < rows * k; ++i) {
+    const uint8_t b = q[i / 2];
+    o.v[i] = e2m1((i & 1) ? (b >> 4) : (b & 15));  // low nibble first
+  }
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t c = 0; c < k / 16; ++c) o.s[r * (k / 16) + c] = e4m3(sf[scale_offset(r, c, rows, k / 16)]);
+  return o;
+}
+
+HostOperand fetch_mxfp8(const void* dq, const void* dsf, int64_t rows, int64_t k) {
+  std::vector<uint8_t> q(rows * k), sf(qg_scale_bytes(rows, k, 32));
+  CHECK_CUDA(cudaMemcpy(q.data(), dq, q.size(), cudaMemcpyDeviceToHost));
+  CHECK_CUDA(cudaMemcpy(sf.data(), dsf, sf.size(), cudaMemcpyDeviceToHost));
+  HostOperand o;
+  o.rows = rows, o.k = k, o.sv = 32;
+  o.v.resize(rows * k);
+  o.s.resize(rows * (k / 32));
+  for (int64_t i = 0; i < rows * k; ++i) o.v[i] = e4m3(q[i]);
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t c = 0; c < k / 32; ++c) o.s[r * (k / 32) + c] = ue8m0(sf[scale_offset(r, c, rows, k / 32)]);
+  return o;
+}
+
+// Sampled-row check of C (m x n, fp32 copy of the device output).
+bool check_rows(const HostOperand& a, const HostOperand& b, const std::vector<float>& c,
+                int64_t m, int64_t n, bool bf16, double* frob_out) {
+  const int64_t k = a.k, sfk = k / a.sv;
+  const int samples = static_cast<int>(std::min<int64_t>(m, 16));
+  double err2 = 0.0, ref2 = 0.0;
+  bool ok = true;
+  const float alpha = a.ts * b.ts;
+  std::vector<double> row(n);
+  for (int s = 0; s < samples; ++s) {
+    const int64_t r = (static_cast<int64_t>(s) * 131) % m;  // gemm_benchmark.cuh:51-53 pattern
+    double norm2 = 0.0;
+    for (int64_t col = 0; col < n; ++col) {
+      double sum = 0.0;
+      for (int64_t kk = 0; kk < k; ++kk)
+        sum += (static_cast<double>(a.v[r * k + kk]) * a.s[r * sfk + kk / a.sv]) *
+               (static_cast<double>(b.v[col * k + kk]) * b.s[col * sfk + kk / b.sv]);
+      row[col] = static_cast<double>(static_cast<float>(sum) * alpha);
+      norm2 += row[col] * row[col];
+    }
+    const double tol_row = 1e-3 * std::sqrt(norm2);
+    for (int64_t col = 0; col < n; ++col) {
+      const double got = c[r * n + col], ref = row[col];
+      const double e = std::fabs(got - ref);
+      const double tol = tol_row + (bf16 ? std::ldexp(1.0, -8) * std::fabs(ref) : 0.0);
+      if (!std::isfinite(got) || e > tol) ok = false;
+      err2 += e * e;
+      ref2 += ref * ref;
+    }
+  }
+  const double frob = std::sqrt(err2 / std::max(ref2, 1e-300));
+  *frob_out = frob;
+  return ok && frob <= 1e-5 + (bf16 ? std::ldexp(1.0, -8) : 0.0);
+}
+
+}  // namespace
+
+namespace {
+
+struct Row {
+  std::string backend, version, precision;
+  double ms = 0, gflops = 0;
+  bool matched = false;
+  double frob = 0;
+};
+
+template <typename Launch>
+float time_launches(Launch launch, int repeat) {
+  for (int i = 0; i < kWarmup; ++i) launch();
+  CHECK_CUDA(cudaDeviceSynchronize());
+  cudaEvent_t e0, e1;
+  CHECK_CUDA(cudaEventCreate(&e0));
+  CHECK_CUDA(cudaEventCreate(&e1));
+  CHECK_CUDA(cudaEventRecord(e0));
+  for (int i = 0; i < repeat; ++i) launch();
+  CHECK_CUDA(cudaEventRecord(e1));
+  CHECK_CUDA(cudaEventSynchronize(e1));
+  float ms = 0;
+  CHECK_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+  CHECK_CUDA(cudaEventDestroy(e0));
+  CHECK_CUDA(cudaEventDestroy(e1));
+  return ms / repeat;
+}
+
+void* dalloc(size_t bytes) {
+  void* p = nullptr;
+  CHECK_CUDA(cudaMalloc(&p, bytes > 0 ? bytes : 16));
+  return p;
+}
+
+std::vector<float> fetch_c(const void* dc, int64_t count, bool bf16) {
+  std::vector<float> c(count);
+  if (bf16) {
+    std::vector<uint16_t> h(count);
+    CHECK_CUDA(cudaMemcpy(h.data(), dc, count * 2, cudaMemcpyDeviceToHost));
+    for (int64_t i = 0; i < count; ++i) {
+      const uint32_t w = static_cast<uint32_t>(h[i]) << 16;
+      std::memcpy(&c[i], &w, 4);
+    }
+  } else {
+    CHECK_CUDA(cudaMemcpy(c.data(), dc, count * 4, cudaMemcpyDeviceToHost));
+  }
+  return c;
+}
+
+// NVFP4 x NVFP4 GEMM (nvfp4_q1_native_fp4_mainloop).
+Row run_nvfp4(const Options& o) {
+  const int64_t m = o.m, n = o.n, k = o.k;
+  auto ha = normal(m * k, o.seed), hb = normal(n * k, o.seed ^ 0xbb67ae85ull);
+  float *da = static_cast<float*>(dalloc(m * k * 4)), *db = static_cast<float*>(dalloc(n * k * 4));
+  CHECK_CUDA(cudaMemcpy(da, ha.data(), m * k * 4, cudaMemcpyHostToDevice));
+  CHECK_CUDA(cudaMemcpy(db, hb.data(), n * k * 4, cudaMemcpyHostToDevice));
+  void *aq = dalloc(m * k / 2), *asf = dalloc(qg_scale_bytes(m, k, 16));
+  void *bq = dalloc(n * k / 2), *bsf = dalloc(qg_scale_bytes(n, k, 16));
+  float *ats = static_cast<float*>(dalloc(4)), *bts = static_cast<float*>(dalloc(4));
+  void* ws = dalloc(qg_quantize_workspace_bytes());
+  CHECK_QG(qg_quantize_nvfp4(da, QG_DTYPE_F32, m, k, QG_LAYOUT_MMA, aq, asf, ats, ws, nullptr));
+  CHECK_QG(qg_quantize_nvfp4(db, QG_DTYPE_F32, n, k, QG_LAYOUT_MMA, bq, bsf, bts, ws, nullptr));
+  const int cdt = o.out_bf16 ? QG_DTYPE_BF16 : QG_DTYPE_F32;
+  void* dc = dalloc(m * n * (o.out_bf16 ? 2 : 4));
+  uint32_t* status = static_cast<uint32_t*>(dalloc(4));
+  CHECK_CUDA(cudaMemset(status, 0, 4));
+  Row r;
+  r.backend = "nvfp4_q1_native_fp4_mainloop";
+  r.version = "tcgen05 mxf4nvf4 block16 (B200)";
+  r.precision = o.out_bf16 ? "nvfp4->bf16" : "nvfp4->fp32";
+  r.ms = time_launches([&] {
+    CHECK_QG(qg_gemm_nvfp4(aq, asf, ats, bq, bsf, bts, dc, cdt, m, n, k, n, QG_LAYOUT_MMA, status,
+                           nullptr));
+  }, o.iterations);
+  CHECK_QG(qg_read_status(status, nullptr, nullptr));
+  r.gflops = 2.0 * m * n * k / (r.ms * 1e6);
+  auto A = fetch_nvfp4(aq, asf, ats, m, k), B = fetch_nvfp4(bq, bsf, bts, n, k);
+  r.matched = check_rows(A, B, fetch_c(dc, m * n, o.out_bf16), m, n, o.out_bf16, &r.frob);
+  for (void* p : {static_cast<void*>(da), static_cast<void*>(db), aq, asf, bq, bsf,
+                  static_cast<void*>(ats), static_cast<void*>(bts), ws, dc,
+                  static_cast<void*>(status)})
+    cudaFree(p);
+  return r;
+}
+
+// MXFP8 x MXFP8 GEMM (mxfp8_q0_tcgen05_block_scaled); B ~ N(0, 0.02).
+Row run_mxfp8(const Options& o) {
+  const int64_t m = o.m, n = o.n, k = o.k;
+  auto ha = normal(m * k, o.seed), hb = normal(n * k, o.seed ^ 0xbb67ae85ull, 0.02f);
+  float *da = static_cast<float*>(dalloc(m * k * 4)), *db = static_cast<float*>(dalloc(n * k * 4));
+  CHECK_CUDA(cudaMemcpy(da, ha.data(), m * k * 4, cudaMemcpyHostToDevice));
+  CHECK_CUDA(cudaMemcpy(db, hb.data(), n * k * 4, cudaMemcpyHostToDevice));
+  void *aq = dalloc(m * k), *asf = dalloc(qg_scale_bytes(m, k, 32));
+  void *bq = dalloc(n * k), *bsf = dalloc(qg_scale_bytes(n, k, 32));
+  CHECK_QG(qg_quantize_mxfp8(da, QG_DTYPE_F32, m, k, QG_LAYOUT_MMA, aq, asf, nullptr));
+  CHECK_QG(qg_quantize_mxfp8(db, QG_DTYPE_F32, n, k, QG_LAYOUT_MMA, bq, bsf, nullptr));
+  const int cdt = o.out_bf16 ? QG_DTYPE_BF16 : QG_DTYPE_F32;
+  void* dc = dalloc(m * n * (o.out_bf16 ? 2 : 4));
+  uint32_t* status = static_cast<uint32_t*>(dalloc(4));
+  CHECK_CUDA(cudaMemset(status, 0, 4));
+  Row r;
+  r.backend = "mxfp8_q0_tcgen05_block_scaled";
+  r.version = "tcgen05 mxf8f6f4 ue8m0/32 (B200)";
+  r.precision = o.out_bf16 ? "mxfp8->bf16" : "mxfp8->fp32";
+  r.ms = time_launches([&] {
+    CHECK_QG(qg_gemm_mxfp8(aq, asf, bq, bsf, dc, cdt, m, n, k, n, QG_LAYOUT_MMA, status, nullptr));
+  }, o.iterations);
+  CHECK_QG(qg_read_status(status, nullptr, nullptr));
+  r.gflops = 2.0 * m * n * k / (r.ms * 1e6);
+  auto A = fetch_mxfp8(aq, asf, m, k), B = fetch_mxfp8(bq, bsf, n, k);
+  r.matched = check_rows(A, B, fetch_c(dc, m * n, o.out_bf16), m, n, o.out_bf16, &r.frob);
+  for (void* p : {static_cast<void*>(da), static_cast<void*>(db), aq, asf, bq, bsf, dc,
+                  static_cast<void*>(status)})
+    cudaFree(p);
+  return r;
+}
+
+// Decode GEMM with fused activation quantisation (nvfp4_skinny_q0): m <= 128
+// bf16-rounded activations, NVFP4 weights N(0, 0.02).
+Row run_skinny(const Options& o) {
+  const int64_t m = std::min<int64_t>(o.m, 128), n = o.n, k = o.k;
+  auto hx = normal(m * k, o.seed), hw = normal(n * k, o.seed ^ 0xbb67ae85ull, 0.02f);
+  float* dx = static_cast<float*>(dalloc(m * k * 4));
+  float* dw = static_cast<float*>(dalloc(n * k * 4));
+  CHECK_CUDA(cudaMemcpy(dx, hx.data(), m * k * 4, cudaMemcpyHostToDevice));
+  CHECK_CUDA(cudaMemcpy(dw, hw.data(), n * k * 4, cudaMemcpyHostToDevice));
+  void *wq = dalloc(n * k / 2), *wsf = dalloc(qg_scale_bytes(n, k, 16));
+  float* wts = static_cast<float*>(dalloc(4));
+  void* qws = dalloc(qg_quantize_workspace_bytes());
+  CHECK_QG(qg_quantize_nvfp4(dw, QG_DTYPE_F32, n, k, QG_LAYOUT_MMA, wq, wsf, wts, qws, nullptr));
+  const size_t wsb = qg_gemm_nvfp4_skinny_workspace_bytes(m, n, k);
+  void* ws = dalloc(wsb);
+  const int cdt = o.out_bf16 ? QG_DTYPE_BF16 : QG_DTYPE_F32;
+  void* dc = dalloc(m * n * (o.out_bf16 ? 2 : 4));
+  Row r;
+  r.backend = "nvfp4_skinny_q0";
+  r.version = "stream-K tcgen05 decode GEMM, fused act quant (B200)";
+  r.precision = o.out_bf16 ? "nvfp4->bf16" : "nvfp4->fp32";
+  r.ms = time_launches([&] {
+    CHECK_QG(qg_gemm_nvfp4_skinny(dx, QG_DTYPE_F32, m, wq, wsf, wts, dc, cdt, n, k, n,
+                                  QG_LAYOUT_MMA, ws, wsb, nullptr, nullptr));
+  }, o.iterations);
+  r.gflops = 2.0 * m * n * k / (r.ms * 1e6);
+  // The quantised activations live in the workspace after the fp32 sums.
+  auto al = [](int64_t v) { return (v + 255) / 256 * 256; };
+  const uint8_t* base = static_cast<const uint8_t*>(ws);
+  const uint8_t* xq = base + al(m * n * 4);
+  const uint8_t* xsf = xq + al(m * k / 2);
+  const float* xts = reinterpret_cast<const float*>(xsf + al(qg_scale_bytes(m, k, 16)));
+  auto A = fetch_nvfp4(xq, xsf, xts, m, k), W = fetch_nvfp4(wq, wsf, wts, n, k);
+  r.matched = check_rows(A, W, fetch_c(dc, m * n, o.out_bf16), m, n, o.out_bf16, &r.frob);
+  for (void* p : {static_cast<void*>(dx), static_cast<void*>(dw), wq, wsf,
+                  static_cast<void*>(wts), qws, ws, dc})
+    cudaFree(p);
+  return r;
+}
+
+void write_row(std::ofstream& csv, const Row& r, const Options& o) {
+  const double peak_tflops = r.precision.rfind("mxfp8", 0) == 0 ? 4500.0 : 9000.0;
+  std::cout << r.backend << ": " << r.ms << " ms, " << r.gflops << " GFLOP/s, matched="
+            << r.matched << " (relative Frobenius " << r.frob << ")\n";
+  std::cout << "backend_id=" << r.backend << std::setprecision(17) << " time_ms=" << r.ms
+            << " work_unit=flop rate_per_second=" << r.gflops * 1e9
+            << " reference_rate_per_second=0 matched=" << r.matched << "\n";
+  csv << std::setprecision(17) << r.backend << ',' << r.version << ','
+      << (o.square ? o.n : o.m) << ',' << r.precision << ",host block-scaled reference (sampled rows),"
+      << r.ms << ',' << r.gflops << ",0," << (r.matched ? 1 : 0) << ',' << r.gflops / 1e3 << ','
+      << 100.0 * r.gflops / 1e3 / peak_tflops << ",1," << o.m << ',' << o.n << ',' << o.k << '\n';
+}
+
+void usage(const char* p) {
+  std::cerr << "Usage: " << p << " [N] [backend]\n"
+            << "       " << p << " M N K backend [--seed S] [--out-dtype bf16|fp32]\n"
+            << "       " << p << " --m=M --n=N --k=K [--iterations=I] [--swizzle=S]\n"
+            << "backends: all|nvfp4_q1_native_fp4_mainloop|mxfp8_q0_tcgen05_block_scaled|"
+               "nvfp4_skinny_q0\n";
+}
+
+bool parse(int argc, char** argv, Options* o) {
+  std::vector<std::string> pos;
+  for (int i = 1; i < argc; ++i) {
+    std::string a = argv[i];
+    auto val = [&](const char* key) { return a.substr(std::strlen(key)); };
+    if (a.rfind("--m=", 0) == 0) { o->m = std::atoll(val("--m=").c_str()); o->cutlass_cli = true; }
+    else if (a.rfind("--n=", 0) == 0) { o->n = std::atoll(val("--n=").c_str()); o->cutlass_cli = true; }
+    else if (a.rfind("--k=", 0) == 0) { o->k = std::atoll(val("--k=").c_str()); o->cutlass_cli = true; }
+    else if (a.rfind("--iterations=", 0) == 0) o->iterations = std::max(1, std::atoi(val("--iterations=").c_str()));
+    else if (a.rfind("--swizzle=", 0) == 0) {}  // raster hint of the CUTLASS CLI; not used
+    else if (a == "--seed" && i + 1 < argc) o->seed = std::strtoull(argv[++i], nullptr, 10);
+    else if (a == "--out-dtype" && i + 1 < argc) o->out_bf16 = std::string(argv[++i]) == "bf16";
+    else if (a == "-h" || a == "--help") return false;
+    else pos.push_back(a);
+  }
+  if (o->cutlass_cli) {
+    o->backend = "nvfp4_q1_native_fp4_mainloop";
+    o->out_bf16 = true;
+    o->square = false;
+    return o->m > 0 && o->n > 0 && o->k > 0;
+  }
+  if (pos.size() <= 2) {
+    if (!pos.empty()) o->m = o->n = o->k = std::atoll(pos[0].c_str());
+    if (pos.size() == 2) o->backend = pos[1];
+  } else if (pos.size() == 4) {
+    o->m = std::atoll(pos[0].c_str());
+    o->n = std::atoll(pos[1].c_str());
+    o->k = std::atoll(pos[2].c_str());
+    o->backend = pos[3];
+    o->square = false;
+  } else {
+    return false;
+  }
+  const std::string& b = o->backend;
+  return o->m > 0 && o->n > 0 && o->k > 0 &&
+         (b == "all" || b == "nvfp4_q1_native_fp4_mainloop" ||
+          b == "mxfp8_q0_tcgen05_block_scaled" || b == "nvfp4_skinny_q0");
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  Options o;
+  if (!parse(argc, argv, &o)) {
+    usage(argv[0]);
+    return EXIT_FAILURE;
+  }
+  int dev = 0;
+  CHECK_CUDA(cudaGetDevice(&dev));
+  cudaDeviceProp prop{};
+  CHECK_CUDA(cudaGetDeviceProperties(&prop, dev));
+  if (o.cutlass_cli) {
+    Row r = run_nvfp4(o);
+    std::cout << "  Problem Size: " << o.m << 'x' << o.n << 'x' << o.k << "\n"
+              << "  Disposition: " << (r.matched ? "Passed" : "Failed") << "\n"
+              << "  Avg runtime: " << r.ms << " ms\n"
+              << "  GFLOPS: " << r.gflops << "\n";
+    return r.matched ? EXIT_SUCCESS : EXIT_FAILURE;
+  }
+  std::cout << "GPU: " << prop.name << " (sm_" << prop.major << prop.minor << ")\n"
+            << "M=" << o.m << " N=" << o.n << " K=" << o.k << ", backend=" << o.backend << '\n'
+            << "Benchmark policy: warmup=" << kWarmup << ", timed repeats=" << o.iterations << '\n';
+  std::ofstream csv("quant_sm110_benchmark.csv");
+  csv << "BackendId,Version,N,Precision,Reference,TimeMs,GFLOPS,RatioToReference,Matched,"
+         "TFLOPS,PctPeak,GPUs,M,NCols,K\n";
+  bool all_ok = true;
+  auto want = [&](const char* b) { return o.backend == "all" || o.backend == b; };
+  if (want("nvfp4_q1_native_fp4_mainloop")) {
+    Row r = run_nvfp4(o);
+    write_row(csv, r, o);
+    all_ok &= r.matched;
+  }
+  if (want("mxfp8_q0_tcgen05_block_scaled")) {
+    Row r = run_mxfp8(o);
+    write_row(csv, r, o);
+    all_ok &= r.matched;
+  }
+  if (want("nvfp4_skinny_q0")) {
+    Row r = run_skinny(o);
+    write_row(csv, r, o);
+    all_ok &= r.matched;
+  }
+  return all_ok ? EXIT_SUCCESS : EXIT_FAILURE;
+}

@@ -1,0 +1,53 @@
+"""The drop-in quant_gemm_sm110_bench binary: CLI, CSV contract and exit codes
+of GEMMquant_sm110/src/quant_gemm_bench.cu (:3038-3095, :1512-1534) and the
+CUTLASS 72b output the sweep runner parses
+(GEMMquant_sm110/scripts/run_quant_gemm_1024.py:404-410)."""
+import csv
+import re
+import subprocess
+
+import pytest
+
+HEADER = ["BackendId", "Version", "N", "Precision", "Reference", "TimeMs", "GFLOPS",
+          "RatioToReference", "Matched"]
+
+
+@pytest.fixture(scope="module")
+def binary(qlib):
+    from cuda_optimazation_b200 import build
+    return build.build_harness()
+
+
+def test_bad_arguments_exit_nonzero(binary):
+    r = subprocess.run([str(binary), "256", "no_such_backend"], capture_output=True, text=True)
+    assert r.returncode != 0 and "Usage" in r.stderr
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("args", [["256", "all"], ["1024", "all"],
+                                  ["512", "1024", "768", "nvfp4_q1_native_fp4_mainloop",
+                                   "--out-dtype", "bf16"],
+                                  ["64", "4096", "2048", "nvfp4_skinny_q0"]])
+def test_csv_rows_matched(binary, tmp_path, args):
+    r = subprocess.run([str(binary), *args], capture_output=True, text=True, cwd=tmp_path,
+                       timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    rows = list(csv.DictReader(open(tmp_path / "quant_sm110_benchmark.csv")))
+    with open(tmp_path / "quant_sm110_benchmark.csv") as f:
+        assert f.readline().strip().split(",")[:9] == HEADER
+    assert rows and all(row["Matched"] == "1" for row in rows)
+    assert all(float(row["GFLOPS"]) > 0 for row in rows)
+    assert re.search(r"backend_id=\S+ time_ms=\S+ work_unit=flop rate_per_second=\S+ "
+                     r"reference_rate_per_second=\S+ matched=1", r.stdout)
+
+
+@pytest.mark.gpu
+def test_cutlass_cli_form(binary, tmp_path):
+    r = subprocess.run([str(binary), "--m=1024", "--n=1024", "--k=1024", "--iterations=20",
+                        "--swizzle=2"], capture_output=True, text=True, cwd=tmp_path, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    # parse_cutlass_fp4_stdout
+    assert "Disposition: Passed" in r.stdout
+    t = re.search(r"Avg runtime:\s*([0-9.eE+-]+)\s*ms", r.stdout)
+    g = re.search(r"GFLOPS:\s*([0-9.eE+-]+)", r.stdout)
+    assert t and g and float(t.group(1)) > 0 and float(g.group(1)) > 0
