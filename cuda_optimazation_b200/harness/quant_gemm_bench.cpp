@@ -319,7 +319,7 @@ Row run_skinny(const Options& o) {
   void* dc = dalloc(m * n * (o.out_bf16 ? 2 : 4));
   Row r;
   r.backend = "nvfp4_skinny_q0";
-  r.version = "stream-K tcgen05 decode GEMM, fused act quant (B200)";
+  r.version = "stream-K tcgen05 decode GEMM with fused act quant (B200)";
   r.precision = o.out_bf16 ? "nvfp4->bf16" : "nvfp4->fp32";
   r.ms = time_launches([&] {
     CHECK_QG(qg_gemm_nvfp4_skinny(dx, QG_DTYPE_F32, m, wq, wsf, wts, dc, cdt, n, k, n,
