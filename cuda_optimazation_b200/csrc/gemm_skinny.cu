@@ -124,10 +124,9 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       const uint64_t pol_x = l2_policy_evict_last();   // activations: reused by all CTAs
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
+      int stage = 0, tile = ur.u0 / ur.nkb, kb = ur.u0 % ur.nkb;
+      uint32_t phase = 0;
       for (int u = ur.u0, g = 0; u < ur.u1; ++u, ++g) {
-        const int stage = g % Cfg::kStages;
-        const uint32_t phase = static_cast<uint32_t>((g / Cfg::kStages) & 1);
-        const int tile = u / ur.nkb, kb = u % ur.nkb;
         if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.timeout_ns, abort_flag, p.status,
                                kDevTimeoutProducer)) {
           ok = false;
@@ -145,6 +144,14 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
         tma_load_2d(sw, &p.tm_w, &full_bar[stage], kb * Cfg::kBKBytes, tile * Cfg::kBM, pol_w);
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++kb == ur.nkb) {
+          kb = 0;
+          ++tile;
+        }
+        if (++stage == Cfg::kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
       if (!ok) {
         uint32_t dummy = 0;
@@ -157,15 +164,19 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
+      // The issue loop is the kernel's serial path: counters are stepped
+      // incrementally and descriptors offset by constants, so no division or
+      // modulo runs per unit.
       const uint32_t idesc = make_idesc_block_scaled(Cfg::kBM, kN, 1u, 0u, 0u, 0u);
+      const uint64_t wdesc0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
+      const uint64_t xdesc0 = make_smem_desc(smem_u32(smem + Cfg::kWBytes), 16, 1024, kSwizzle128B);
+      constexpr uint64_t kStageDesc = Cfg::kStageBytes >> 4;
       bool ok = true;
-      int seg = 0;
-      uint32_t acc = 0;
-      for (int u = ur.u0, g = 0; u < ur.u1 && ok; ++u, ++g) {
-        const int stage = g % Cfg::kStages;
-        const uint32_t phase = static_cast<uint32_t>((g / Cfg::kStages) & 1);
+      int seg = 0, stage = 0, kb = ur.u0 % ur.nkb;
+      uint32_t phase = 0, acc = 0;
+      for (int u = ur.u0; u < ur.u1 && ok; ++u) {
         const int buf = seg & 1;
-        if (ur.seg_start(u)) {
+        if (u == ur.u0 || kb == 0) {
           if (!mbar_wait_bounded(&acc_empty[buf], ((seg >> 1) & 1) ^ 1u, p.timeout_ns, abort_flag,
                                  p.status, kDevTimeoutMma)) {
             ok = false;
@@ -182,25 +193,26 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
           break;
         }
         tc_fence_after();
-        trace(p, 144 + g);
-        uint8_t* sw = smem + stage * Cfg::kStageBytes;
-        uint8_t* sx = sw + Cfg::kWBytes;
         const uint32_t sfw_col = tmem_base + Cfg::kTmemSfBase + stage * Cfg::kSfStageCols;
-        const uint32_t sfx_col = sfw_col + 16;
-        const uint64_t wdesc = make_smem_desc(smem_u32(sw), 16, 1024, kSwizzle128B);
-        const uint64_t xdesc = make_smem_desc(smem_u32(sx), 16, 1024, kSwizzle128B);
+        const uint64_t wdesc = wdesc0 + stage * kStageDesc;
+        const uint64_t xdesc = xdesc0 + stage * kStageDesc;
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kN);
 #pragma unroll
         for (int j = 0; j < Cfg::kMmaPerStage; ++j) {
           const uint64_t koff = static_cast<uint64_t>(j * 2);
           mma_mxf4nvf4(d_tmem, wdesc + koff, xdesc + koff, idesc, sfw_col + j * 4,
-                       sfx_col + j * 4, acc);
+                       sfw_col + 16 + j * 4, acc);
           acc = 1;
         }
         tc_commit(&empty_bar[stage]);
-        if (ur.seg_end(u)) {
+        if (u == ur.u1 - 1 || kb == ur.nkb - 1) {
           tc_commit(&acc_full[buf]);
           ++seg;
+        }
+        if (++kb == ur.nkb) kb = 0;
+        if (++stage == Cfg::kStages) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
       tc_commit(drain_bar);
@@ -211,16 +223,15 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
     // ---------------------------------------------------------------- scale stagers
     const int quad = warp % 4;
     const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
-    for (int u = ur.u0, g = 0; u < ur.u1; ++u, ++g) {
-      const int stage = g % Cfg::kStages;
-      const uint32_t phase = static_cast<uint32_t>((g / Cfg::kStages) & 1);
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int u = ur.u0; u < ur.u1; ++u) {
       bool ok = true;
       if (lane == 0)
         ok = mbar_wait_bounded(&full_bar[stage], phase, p.timeout_ns, abort_flag, p.status,
                                kDevTimeoutMma);
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
       mbar_try_wait(&full_bar[stage], phase);
-      if (lane == 0 && quad == 0) trace(p, 272 + g);
       const uint8_t* ssfw = smem + stage * Cfg::kStageBytes + Cfg::kWBytes + Cfg::kXBytes;
       const uint8_t* ssfx = ssfw + Cfg::kSfwBytes;
       uint32_t a[16], b[16];
@@ -238,6 +249,10 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sf_ready[stage]);
+      if (++stage == Cfg::kStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
     }
   } else {
     // ---------------------------------------------------------------- epilogue
