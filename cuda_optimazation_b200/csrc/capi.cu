@@ -311,14 +311,27 @@ int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void
                      sf_layout, status, reinterpret_cast<cudaStream_t>(stream));
 }
 
-// Workspace of qg_gemm_nvfp4_skinny: fp32 partial sums [m][n], then the
-// quantised activations (values, scales, tensor scale, amax word), each
-// 256-byte aligned.
+// Workspace of qg_gemm_nvfp4_skinny, each part 256-byte aligned: the
+// per-CTA partial tiles [max_ctas][2][m][128] fp32, the tile counters
+// [tiles][4], the quantised activations (values, scales) and the tensor
+// scale.
 static int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+struct SkinnyWs {
+  int64_t part, cnt, xq, xsf, xts, total;
+};
+static SkinnyWs skinny_ws_layout(int64_t m, int64_t n, int64_t k) {
+  SkinnyWs w;
+  w.part = 0;
+  w.cnt = w.part + align256(static_cast<int64_t>(skinny_max_ctas()) * 2 * m * 128 * 4);
+  w.xq = w.cnt + align256((n + 127) / 128 * 4 * 4);
+  w.xsf = w.xq + align256(m * k / 2);
+  w.xts = w.xsf + align256(qg_scale_bytes(m, k, 16));
+  w.total = w.xts + 256;
+  return w;
+}
 size_t qg_gemm_nvfp4_skinny_workspace_bytes(int64_t m, int64_t n, int64_t k) {
   if (m < 1 || n < 1 || k < 1) return 0;
-  return static_cast<size_t>(align256(m * n * 4) + align256(m * k / 2) +
-                             align256(qg_scale_bytes(m, k, 16)) + 512);
+  return static_cast<size_t>(skinny_ws_layout(m, n, k).total);
 }
 
 int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q, const void* w_sf,
@@ -338,16 +351,17 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   if (!encode_fn()) return QG_ERR_CUDA;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   uint8_t* base = static_cast<uint8_t*>(workspace);
-  float* ws = reinterpret_cast<float*>(base);
-  uint8_t* xq = base + align256(m * n * 4);
-  uint8_t* xsf = xq + align256(m * k / 2);
-  float* xts = reinterpret_cast<float*>(xsf + align256(qg_scale_bytes(m, k, 16)));
-  void* amax_ws = xts + 64;  // 256 bytes past the tensor scale
-  // 1. zero the partial sums; 2. quantise the activations (fused into this
-  // call); 3. stream-K GEMM; 4. scale + convert.
-  if (cudaMemsetAsync(ws, 0, static_cast<size_t>(m * n * 4), s) != cudaSuccess) return QG_ERR_CUDA;
-  if (int r = qg_quantize_nvfp4(x, x_dtype, m, k, QG_LAYOUT_MMA, xq, xsf, xts, amax_ws, stream))
-    return r;
+  const SkinnyWs wl = skinny_ws_layout(m, n, k);
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(base + wl.cnt);
+  uint8_t* xq = base + wl.xq;
+  uint8_t* xsf = base + wl.xsf;
+  float* xts = reinterpret_cast<float*>(base + wl.xts);
+  const int64_t tiles = (n + 127) / 128;
+  // 1. quantise the activations (one cluster; also zeroes the counters);
+  // 2. stream-K GEMM, launched as its programmatic dependent.
+  if (launch_skinny_quantize(x, x_dtype == QG_DTYPE_BF16, m, k, xq, xsf, xts, cnt, tiles * 4, s) !=
+      cudaSuccess)
+    return QG_ERR_CUDA;
   const int mma_n = skinny_mma_n(m);
   SkinnyParams p;
   std::memset(&p, 0, sizeof(p));
@@ -356,7 +370,13 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   if (!make_operand_map(&p.tm_x, xq, m, row_bytes, mma_n)) return QG_ERR_CUDA;
   if (!make_scale_map(&p.tm_sfw, w_sf, n, k, 16, sf_layout, 1, 4)) return QG_ERR_CUDA;
   if (!make_scale_map(&p.tm_sfx, xsf, m, k, 16, QG_LAYOUT_MMA, 1, 4)) return QG_ERR_CUDA;
-  p.ws = ws;
+  p.part = reinterpret_cast<float*>(base + wl.part);
+  p.cnt = cnt;
+  p.c = c;
+  p.ldc = ldc;
+  p.x_ts = xts;
+  p.w_ts = w_ts;
+  p.out_bf16 = c_dtype == QG_DTYPE_BF16 ? 1 : 0;
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
@@ -366,11 +386,9 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   p.timeout_ns = default_timeout_ns();
   p.diag = diag_flags();
   const int64_t units = static_cast<int64_t>(p.num_tiles) * p.num_k_blocks;
-  const int grid = static_cast<int>(units < num_sms() ? units : num_sms());
-  if (launch_gemm_skinny(p, grid, s) != cudaSuccess) return QG_ERR_CUDA;
-  if (launch_skinny_finish(ws, c, c_dtype == QG_DTYPE_BF16, m, n, ldc, xts, w_ts, s) !=
-      cudaSuccess)
-    return QG_ERR_CUDA;
+  int64_t grid = units < num_sms() ? units : num_sms();
+  if (grid > skinny_max_ctas()) grid = skinny_max_ctas();
+  if (launch_gemm_skinny(p, static_cast<int>(grid), s) != cudaSuccess) return QG_ERR_CUDA;
   return QG_OK;
 }
 

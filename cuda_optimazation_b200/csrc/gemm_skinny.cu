@@ -9,8 +9,10 @@
 // it.  The weights are streamed once from HBM; every CTA takes an equal,
 // contiguous range of (weight-tile, K-block) units ("stream-K"), so the
 // 224 x 32 units of N = 28672, K = 8192 spread evenly over 148 SMs.  A tile
-// split between CTAs is summed with fp32 reductions into a zeroed workspace;
-// a finishing kernel applies the tensor scales and writes bf16 / fp32.
+// that one CTA owns is scaled and written to C by that CTA; a tile split
+// between CTAs is summed by the last of them to finish (see the epilogue).
+// The grid is a programmatic dependent of the activation quantizer
+// (skinny_quant.cu), so no memset, reduction or finishing launch is needed.
 //
 // Roles (10 warps): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
 // warps 2..5 epilogue (one TMEM quadrant each: lane = weight row), warps 6..9
@@ -24,6 +26,9 @@
 #include "qg_ptx.cuh"
 
 namespace qg {
+
+// Upper bound of the GEMM grid; sizes the partial-tile workspace.
+constexpr int kSkinnyMaxCtas = 256;
 
 template <int kN>
 struct SkinnyCfg {
@@ -51,17 +56,13 @@ struct SkinnyCfg {
 // Walk of one CTA's unit range: a "segment" is a run of K-blocks of one tile.
 struct UnitRange {
   int u0, u1, nkb;
-  __device__ __forceinline__ bool seg_start(int u) const { return u == u0 || (u % nkb) == 0; }
-  __device__ __forceinline__ bool seg_end(int u) const {
-    return u == u1 - 1 || (u % nkb) == nkb - 1;
-  }
 };
 
 // Diagnostic stamp (QG_DIAG_FLAGS bit 6): CTA 0 writes %globaltimer into
-// slot `i` of the workspace.
+// slot `i` of the last (never used by a launched CTA) partial slice pair.
 __device__ __forceinline__ void trace(const SkinnyParams& p, int i) {
   if ((p.diag & 64u) && blockIdx.x == 0 && i < 512)
-    reinterpret_cast<unsigned long long*>(p.ws)[i] = globaltimer_ns();
+    reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * 2 * p.m * 128)[i] = globaltimer_ns();
 }
 
 template <int kN>
@@ -126,22 +127,42 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       bool ok = true;
       int stage = 0, tile = ur.u0 / ur.nkb, kb = ur.u0 % ur.nkb;
       uint32_t phase = 0;
+      // The first kStages stages get their weight loads at once; their
+      // activation loads wait for the quantizer grid (griddep_wait), so the
+      // weight stream starts while the activations are being quantised.
+      int deferred = 0;
+      int dkb[Cfg::kStages];
+      auto issue_x = [&](int s, int k_blk) {
+        uint8_t* sx = smem + s * Cfg::kStageBytes + Cfg::kWBytes;
+        uint8_t* ssfx = sx + Cfg::kXBytes + Cfg::kSfwBytes;
+        tma_load_3d(ssfx, &p.tm_sfx, &full_bar[s], 0, 0, k_blk * Cfg::kSfChunks, pol_x);
+        tma_load_2d(sx, &p.tm_x, &full_bar[s], k_blk * Cfg::kBKBytes, 0, pol_x);
+      };
+      bool dep_done = false;
+      auto release_deferred = [&]() {
+        griddep_wait();
+        trace(p, 2);
+        for (int s = 0; s < deferred; ++s) issue_x(s, dkb[s]);
+        dep_done = true;
+      };
       for (int u = ur.u0, g = 0; u < ur.u1; ++u, ++g) {
+        if (!dep_done && g == Cfg::kStages) release_deferred();
         if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.timeout_ns, abort_flag, p.status,
                                kDevTimeoutProducer)) {
           ok = false;
           break;
         }
         uint8_t* sw = smem + stage * Cfg::kStageBytes;
-        uint8_t* sx = sw + Cfg::kWBytes;
-        uint8_t* ssfw = sx + Cfg::kXBytes;
-        uint8_t* ssfx = ssfw + Cfg::kSfwBytes;
+        uint8_t* ssfw = sw + Cfg::kWBytes + Cfg::kXBytes;
         trace(p, 16 + g);
         mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageTx);
         tma_load_3d(ssfw, &p.tm_sfw, &full_bar[stage], 0, tile, kb * Cfg::kSfChunks, pol_w);
-        tma_load_3d(ssfx, &p.tm_sfx, &full_bar[stage], 0, 0, kb * Cfg::kSfChunks, pol_x);
-        tma_load_2d(sx, &p.tm_x, &full_bar[stage], kb * Cfg::kBKBytes, 0, pol_x);
         tma_load_2d(sw, &p.tm_w, &full_bar[stage], kb * Cfg::kBKBytes, tile * Cfg::kBM, pol_w);
+        if (dep_done) {
+          issue_x(stage, kb);
+        } else {
+          dkb[deferred++] = kb;
+        }
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
         if (++kb == ur.nkb) {
@@ -153,6 +174,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
           phase ^= 1u;
         }
       }
+      if (!dep_done) release_deferred();
       if (!ok) {
         uint32_t dummy = 0;
         for (int s = 0; s < Cfg::kStages; ++s)
@@ -256,11 +278,31 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
     }
   } else {
     // ---------------------------------------------------------------- epilogue
+    // Lane = weight row = output column n; the kN accumulator columns are the
+    // activation rows m.  A tile owned by one CTA is scaled and stored to C.
+    // A split tile: every contributor stores its partial to its own slice,
+    // then bumps the tile's counter (one per TMEM quadrant); the last to
+    // arrive sums the slices in contributor order, so the result does not
+    // depend on which CTA finished last.
     const int quad = warp % 4;
     const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
-    int seg = 0;
-    for (int u = ur.u0; u < ur.u1; ++u) {
-      if (!ur.seg_end(u)) continue;
+    griddep_wait();  // the tensor scale and the counters come from the quantizer grid
+    if (quad == 0 && lane == 0) trace(p, 3);
+    const float alpha = (p.x_ts ? *p.x_ts : 1.0f) * (p.w_ts ? *p.w_ts : 1.0f);
+    const int64_t units_all = static_cast<int64_t>(p.num_tiles) * ur.nkb;
+    const int64_t grid = gridDim.x;
+    auto contributor = [&](int64_t u) { return static_cast<int>(((u + 1) * grid - 1) / units_all); };
+    auto first_tile = [&](int c) { return static_cast<int>(units_all * c / grid / ur.nkb); };
+    auto store_c = [&](int m, int n, float v) {
+      if (p.out_bf16)
+        reinterpret_cast<__nv_bfloat16*>(p.c)[static_cast<int64_t>(m) * p.ldc + n] =
+            __float2bfloat16_rn(v);
+      else
+        reinterpret_cast<float*>(p.c)[static_cast<int64_t>(m) * p.ldc + n] = v;
+    };
+    const int tile_lo = ur.u0 / ur.nkb, tile_hi = (ur.u1 - 1) / ur.nkb;
+    const int my_first = tile_lo;
+    for (int t = tile_lo, seg = 0; t <= tile_hi; ++t, ++seg) {
       const int buf = seg & 1;
       bool ok = true;
       if (lane == 0)
@@ -269,8 +311,13 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
       mbar_try_wait(&acc_full[buf], (seg >> 1) & 1);
       tc_fence_after();
-      const int n = (u / ur.nkb) * Cfg::kBM + quad * 32 + lane;  // weight row = output column
+      const int col = quad * 32 + lane;
+      const int n = t * Cfg::kBM + col;
       const bool n_ok = n < p.n;
+      const int cf = contributor(static_cast<int64_t>(t) * ur.nkb);
+      const int cl = contributor(static_cast<int64_t>(t + 1) * ur.nkb - 1);
+      float* mine = p.part + static_cast<int64_t>(blockIdx.x * 2 + (t == my_first ? 0 : 1)) *
+                                 p.m * Cfg::kBM;
 #pragma unroll
       for (int cc = 0; cc < kN / 16; ++cc) {
         uint32_t r[16];
@@ -284,11 +331,73 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int m = cc * 16 + j;
-          if (n_ok && m < p.m && !(p.diag & 64u))
-            atomicAdd(p.ws + static_cast<int64_t>(m) * p.n + n, __uint_as_float(r[j]));
+          if (m < p.m) {
+            const float v = __uint_as_float(r[j]);
+            if (cf == cl) {
+              if (n_ok) store_c(m, n, v * alpha);
+            } else {
+              __stcg(mine + m * Cfg::kBM + col, v);
+            }
+          }
         }
       }
-      ++seg;
+      if (quad == 0 && lane == 0) trace(p, 100 + seg);
+      if (cf == cl) continue;
+      __threadfence();
+      __syncwarp();
+      uint32_t old = 0;
+      if (lane == 0) old = atomicAdd(&p.cnt[t * 4 + quad], 1u);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old != static_cast<uint32_t>(cl - cf)) continue;
+      __threadfence();
+      // Sum pass: a lane takes 4 adjacent columns of one row, a warp
+      // instruction 4 rows x 32 columns; 8 instructions x 2 contributors of
+      // 16-byte loads are in flight per warp before the adds, in order.
+      {
+        const int sub = lane >> 3, c4 = (lane & 7) * 4;
+        const int64_t slice = static_cast<int64_t>(p.m) * Cfg::kBM;
+        for (int m0 = 0; m0 < p.m; m0 += 32) {
+          float4 acc[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int c = cf; c <= cl; c += 2) {
+            const bool two = c + 1 <= cl;
+            const float* s0 = p.part + (c * 2 + (t == first_tile(c) ? 0 : 1)) * slice + quad * 32 + c4;
+            const float* s1 = two ? p.part + ((c + 1) * 2 + (t == first_tile(c + 1) ? 0 : 1)) * slice +
+                                        quad * 32 + c4
+                                  : s0;
+            float4 v0[8], v1[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int m = m0 + i * 4 + sub;
+              const bool ok = m < p.m;
+              v0[i] = ok ? __ldcg(reinterpret_cast<const float4*>(s0 + m * Cfg::kBM))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+              v1[i] = ok && two ? __ldcg(reinterpret_cast<const float4*>(s1 + m * Cfg::kBM))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              acc[i].x += v0[i].x; acc[i].y += v0[i].y; acc[i].z += v0[i].z; acc[i].w += v0[i].w;
+              if (two) {
+                acc[i].x += v1[i].x; acc[i].y += v1[i].y; acc[i].z += v1[i].z; acc[i].w += v1[i].w;
+              }
+            }
+          }
+          const int nb = t * Cfg::kBM + quad * 32 + c4;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int m = m0 + i * 4 + sub;
+            if (m >= p.m) continue;
+            const float e[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (nb + q < p.n) store_c(m, nb + q, e[q] * alpha);
+          }
+        }
+      }
+      if (lane == 0) p.cnt[t * 4 + quad] = 0u;  // ready for the next call
+      if (quad == 0 && lane == 0) trace(p, 200 + seg);
     }
   }
 
@@ -298,23 +407,6 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
-  }
-}
-
-// C[m, n] = alpha * ws[m, n] (bf16 or fp32), alpha = product of the tensor
-// scales read from the device.
-template <bool kOutBf16>
-__global__ void __launch_bounds__(256)
-    skinny_finish_kernel(const float* ws, void* c, int64_t m, int64_t n, int64_t ldc,
-                         const float* a_ts, const float* b_ts) {
-  const float alpha = (a_ts ? *a_ts : 1.0f) * (b_ts ? *b_ts : 1.0f);
-  const int64_t total = m * n;
-  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = e / n, col = e - r * n;
-    const float v = ws[e] * alpha;
-    if (kOutBf16) reinterpret_cast<__nv_bfloat16*>(c)[r * ldc + col] = __float2bfloat16_rn(v);
-    else reinterpret_cast<float*>(c)[r * ldc + col] = v;
   }
 }
 
@@ -329,9 +421,20 @@ static cudaError_t launch_skinny_n(const SkinnyParams& p, int grid, cudaStream_t
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
 }
+
+int skinny_max_ctas() { return kSkinnyMaxCtas; }
 
 int skinny_mma_n(int64_t m) { return m <= 16 ? 16 : m <= 32 ? 32 : m <= 64 ? 64 : 128; }
 
@@ -342,17 +445,6 @@ cudaError_t launch_gemm_skinny(const SkinnyParams& p, int grid, cudaStream_t str
     case 64: return launch_skinny_n<64>(p, grid, stream);
     default: return launch_skinny_n<128>(p, grid, stream);
   }
-}
-
-cudaError_t launch_skinny_finish(const float* ws, void* c, bool out_bf16, int64_t m, int64_t n,
-                                 int64_t ldc, const float* a_ts, const float* b_ts,
-                                 cudaStream_t stream) {
-  const int64_t blocks = (m * n + 255) / 256;
-  const int64_t cap = 4ll * num_sms();
-  const int grid = static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
-  if (out_bf16) skinny_finish_kernel<true><<<grid, 256, 0, stream>>>(ws, c, m, n, ldc, a_ts, b_ts);
-  else skinny_finish_kernel<false><<<grid, 256, 0, stream>>>(ws, c, m, n, ldc, a_ts, b_ts);
-  return cudaGetLastError();
 }
 
 }  // namespace qg

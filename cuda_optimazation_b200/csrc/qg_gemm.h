@@ -29,25 +29,39 @@ struct GemmParams {
 
 // Decode-shaped NVFP4 GEMM (gemm_skinny.cu): weights W [n][k] on the MMA's M
 // side, activations X [m][k] (m <= 128) on its N side, stream-K over
-// (weight tile, K block) units with fp32 reductions into ws [m][n].
+// (weight tile, K block) units.  A tile split between CTAs is summed by the
+// last contributor to finish it (per-tile counters), in a fixed order, from
+// per-CTA partial slices; whole tiles are written straight to C.
 struct SkinnyParams {
   CUtensorMap tm_w;    // uint8 [n][k/2], box 128 B x 128 rows, SWIZZLE_128B
   CUtensorMap tm_x;    // uint8 [m][k/2], box 128 B x mma_n rows, SWIZZLE_128B
   CUtensorMap tm_sfw;  // uint32 chunks, box (128, 1, 4)
   CUtensorMap tm_sfx;
-  float* ws;
+  float* part;         // [grid][2][m][128] fp32 partial tiles
+  uint32_t* cnt;       // [num_tiles][4] arrival counters, zero between calls
+  void* c;
+  int64_t ldc;
+  const float* x_ts;   // activation tensor scale (written by the quantizer)
+  const float* w_ts;   // weight tensor scale (may be null)
+  int out_bf16;
   int m, n, k;
   int num_tiles, num_k_blocks;
   uint32_t* status;
   uint64_t timeout_ns;
   // Diagnostics (QG_DIAG_FLAGS): bit 6 writes %globaltimer stamps of CTA 0's
-  // roles into the workspace instead of results.
+  // roles into the partial buffer instead of results.
   uint32_t diag;
 };
+// The GEMM is launched as a programmatic dependent of the activation
+// quantizer: its prologue and first weight loads overlap the quantizer.
 cudaError_t launch_gemm_skinny(const SkinnyParams& p, int grid, cudaStream_t stream);
-cudaError_t launch_skinny_finish(const float* ws, void* c, bool out_bf16, int64_t m, int64_t n,
-                                 int64_t ldc, const float* a_ts, const float* b_ts,
-                                 cudaStream_t stream);
+// One thread-block cluster quantises X [m][k] (m <= 128) to NVFP4 in the MMA
+// scale layout (padding scale slots zeroed), writes the tensor scale, and
+// zeroes `ncnt` counters.
+cudaError_t launch_skinny_quantize(const void* x, bool bf16, int64_t m, int64_t k, uint8_t* q,
+                                   uint8_t* sf, float* ts, uint32_t* cnt, int64_t ncnt,
+                                   cudaStream_t stream);
+int skinny_max_ctas();
 int skinny_mma_n(int64_t m);
 
 cudaError_t launch_gemm_blockscaled(const GemmParams& p, bool fp4, bool out_bf16, int grid,

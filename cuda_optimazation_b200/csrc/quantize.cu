@@ -22,85 +22,9 @@
 
 #include "qg_gemm.h"
 #include "qg_ptx.cuh"
+#include "qg_codec.cuh"
 
 namespace qg {
-
-// ------------------------------------------------------------------ codecs
-// fp32 -> e2m1 nibble, round to nearest even, sign kept on zero, NaN -> +0,
-// saturating at 6.  The seven thresholds are the fp32 bit patterns of the
-// rounding boundaries of the e2m1 grid {0, .5, 1, 1.5, 2, 3, 4, 6}: a tie
-// that must round to the even lower code starts one ulp above the midpoint.
-__device__ __forceinline__ uint32_t e2m1_encode(float v) {
-  const uint32_t raw = __float_as_uint(v);
-  const uint32_t mag = raw & 0x7fffffffu;
-  if (mag > 0x7f800000u) return 0u;
-  const uint32_t code = (mag >= 0x3e800001u) + (mag >= 0x3f400000u) + (mag >= 0x3fa00001u) +
-                        (mag >= 0x3fe00000u) + (mag >= 0x40200001u) + (mag >= 0x40600000u) +
-                        (mag >= 0x40a00001u);
-  return ((raw >> 28) & 0x8u) | code;
-}
-
-// Smallest positive finite e4m3 code whose value is >= v (0 for v <= 0,
-// 0x7e = 448 above the range).  Normal range: truncate the fp32 mantissa to
-// 3 bits and bump by one code when any dropped bit is set; subnormal range
-// (v < 2^-6): ceil(v * 2^9) subnormal steps.
-__device__ __forceinline__ uint32_t e4m3_round_up(float v) {
-  if (!(v > 0.0f)) return 0u;
-  if (v >= 448.0f) return 0x7eu;
-  if (v < 0.015625f) return static_cast<uint32_t>(ceilf(v * 512.0f));
-  const uint32_t b = __float_as_uint(v);
-  const uint32_t e = ((b >> 23) & 0xffu) - 127u + 7u;
-  uint32_t code = (e << 3) | ((b >> 20) & 7u);
-  if (b & 0xfffffu) code += 1u;
-  return code;
-}
-
-__device__ __forceinline__ float e4m3_decode_positive(uint32_t c) {
-  const uint32_t e = (c >> 3) & 0xfu, m = c & 7u;
-  if (e == 0u) return static_cast<float>(m) * 0.001953125f;  // m * 2^-9
-  return __uint_as_float(((e + 120u) << 23) | (m << 20));
-}
-
-// Byte offset of scale (row, scale column) in an MMA scale layout.
-__device__ __forceinline__ int64_t mma_scale_offset(int64_t row, int64_t sfc, int64_t row_blocks,
-                                                    int64_t sf_blocks, int layout) {
-  const int64_t br = row >> 7, bs = sfc >> 2, w = row & 127;
-  const int64_t chunk = (layout == 1) ? bs * row_blocks + br : br * sf_blocks + bs;
-  return chunk * 512 + (w & 31) * 16 + (w >> 5) * 4 + (sfc & 3);
-}
-
-template <bool kBf16>
-__device__ __forceinline__ void load16(const void* x, int64_t elem, float (&v)[16]) {
-  if (kBf16) {
-    const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(x) + elem);
-    const uint4 a = __ldg(p), b = __ldg(p + 1);
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      v[2 * i] = __uint_as_float(w[i] << 16);
-      v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-    }
-  } else {
-    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + elem);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 f = __ldg(p + i);
-      v[4 * i] = f.x;
-      v[4 * i + 1] = f.y;
-      v[4 * i + 2] = f.z;
-      v[4 * i + 3] = f.w;
-    }
-  }
-}
-
-template <bool kBf16>
-__device__ __forceinline__ float load1(const void* x, int64_t i) {
-  if (kBf16) {
-    const uint16_t h = reinterpret_cast<const uint16_t*>(x)[i];
-    return __uint_as_float(static_cast<uint32_t>(h) << 16);
-  }
-  return reinterpret_cast<const float*>(x)[i];
-}
 
 // ------------------------------------------------------------------ amax
 template <bool kBf16>
