@@ -374,8 +374,7 @@ def run_skinny(args, w, rank, world, dist, torch):
         x.view(-1)[::1000] *= 50.0
         sets.append((x.to(torch.bfloat16), W))
     out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-    ws = torch.empty(int(q.lib().qg_gemm_nvfp4_skinny_workspace_bytes(m, n, k)),
-                     dtype=torch.uint8, device=dev)
+    ws = q.skinny_workspace(m, n, k, dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def call(i):

@@ -313,11 +313,13 @@ int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void
 
 // Workspace of qg_gemm_nvfp4_skinny, each part 256-byte aligned: the
 // per-CTA partial tiles [max_ctas][2][m][128] fp32, the tile counters
-// [tiles][4], the quantised activations (values, scales) and the tensor
-// scale.
+// [tiles][4], the quantised activations (values, scales), the tensor scale,
+// the quantiser's per-CTA amax slots and its grid arrival counters.  The
+// counters must be zero before the first call (zero-filled workspace); every
+// call that completes leaves them zero.
 static int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 struct SkinnyWs {
-  int64_t part, cnt, xq, xsf, xts, total;
+  int64_t part, cnt, xq, xsf, xts, amax, sync, total;
 };
 static SkinnyWs skinny_ws_layout(int64_t m, int64_t n, int64_t k) {
   SkinnyWs w;
@@ -326,7 +328,9 @@ static SkinnyWs skinny_ws_layout(int64_t m, int64_t n, int64_t k) {
   w.xq = w.cnt + align256((n + 127) / 128 * 4 * 4);
   w.xsf = w.xq + align256(m * k / 2);
   w.xts = w.xsf + align256(qg_scale_bytes(m, k, 16));
-  w.total = w.xts + 256;
+  w.amax = w.xts + 256;
+  w.sync = w.amax + align256(skinny_max_ctas() * 4);
+  w.total = w.sync + 256;
   return w;
 }
 size_t qg_gemm_nvfp4_skinny_workspace_bytes(int64_t m, int64_t n, int64_t k) {
@@ -356,32 +360,34 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   uint8_t* xq = base + wl.xq;
   uint8_t* xsf = base + wl.xsf;
   float* xts = reinterpret_cast<float*>(base + wl.xts);
-  const int64_t tiles = (n + 127) / 128;
-  // 1. quantise the activations (one cluster; also zeroes the counters);
-  // 2. stream-K GEMM, launched as its programmatic dependent.
-  if (launch_skinny_quantize(x, x_dtype == QG_DTYPE_BF16, m, k, xq, xsf, xts, cnt, tiles * 4, s) !=
-      cudaSuccess)
-    return QG_ERR_CUDA;
   const int mma_n = skinny_mma_n(m);
   SkinnyParams p;
   std::memset(&p, 0, sizeof(p));
   const int64_t row_bytes = k / 2;
   if (!make_operand_map(&p.tm_w, w_q, n, row_bytes, 128)) return QG_ERR_CUDA;
   if (!make_operand_map(&p.tm_x, xq, m, row_bytes, mma_n)) return QG_ERR_CUDA;
-  if (!make_scale_map(&p.tm_sfw, w_sf, n, k, 16, sf_layout, 1, 4)) return QG_ERR_CUDA;
-  if (!make_scale_map(&p.tm_sfx, xsf, m, k, 16, QG_LAYOUT_MMA, 1, 4)) return QG_ERR_CUDA;
+  if (!make_scale_map(&p.tm_sfw, w_sf, n, k, 16, sf_layout, 1, 8)) return QG_ERR_CUDA;
+  if (!make_scale_map(&p.tm_sfx, xsf, m, k, 16, QG_LAYOUT_MMA, 1, 8)) return QG_ERR_CUDA;
   p.part = reinterpret_cast<float*>(base + wl.part);
   p.cnt = cnt;
   p.c = c;
   p.ldc = ldc;
+  p.x = x;
+  p.x_bf16 = x_dtype == QG_DTYPE_BF16 ? 1 : 0;
+  p.xq = xq;
+  p.xsf = xsf;
   p.x_ts = xts;
+  p.amax_part = reinterpret_cast<float*>(base + wl.amax);
+  p.sync = reinterpret_cast<uint32_t*>(base + wl.sync);
   p.w_ts = w_ts;
   p.out_bf16 = c_dtype == QG_DTYPE_BF16 ? 1 : 0;
+  p.vec_ok = (reinterpret_cast<uintptr_t>(c) % 16 == 0) &&
+             ((ldc * (c_dtype == QG_DTYPE_BF16 ? 2 : 4)) % 16 == 0);
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
   p.num_tiles = static_cast<int>((n + 127) / 128);
-  p.num_k_blocks = static_cast<int>((row_bytes + 127) / 128);
+  p.num_k_blocks = static_cast<int>((row_bytes + 255) / 256);  // 512 of K per stage
   p.status = status;
   p.timeout_ns = default_timeout_ns();
   p.diag = diag_flags();

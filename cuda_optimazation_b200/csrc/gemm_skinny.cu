@@ -11,42 +11,59 @@
 // 224 x 32 units of N = 28672, K = 8192 spread evenly over 148 SMs.  A tile
 // that one CTA owns is scaled and written to C by that CTA; a tile split
 // between CTAs is summed by the last of them to finish (see the epilogue).
-// The grid is a programmatic dependent of the activation quantizer
-// (skinny_quant.cu), so no memset, reduction or finishing launch is needed.
+// The activation quantisation runs in the same cooperative grid (see
+// quantize_phase), so a call is one launch: no memset, quantiser, reduction
+// or finishing kernel.
 //
 // Roles (10 warps): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
-// warps 2..5 epilogue (one TMEM quadrant each: lane = weight row), warps 6..9
+// warps 2..9 first quantise the activations, then warps 2..5 are the
+// epilogue (one TMEM quadrant each: lane = weight row) and warps 6..9 the
 // scale stagers (tcgen05.st, as in gemm_solo.cu).  The accumulator is double
 // buffered so a segment's reduction overlaps the next segment's mainloop.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include "qg_codec.cuh"
 #include "qg_gemm.h"
 #include "qg_ptx.cuh"
 
 namespace qg {
+
+#ifndef QG_SKINNY_L2_AHEAD
+#define QG_SKINNY_L2_AHEAD 8
+#endif
 
 // Upper bound of the GEMM grid; sizes the partial-tile workspace.
 constexpr int kSkinnyMaxCtas = 256;
 
 template <int kN>
 struct SkinnyCfg {
-  static constexpr int kBM = 128;       // weight rows per tile
-  static constexpr int kBKBytes = 128;  // 256 fp4 of K per stage
-  static constexpr int kStages = kN >= 128 ? 6 : 8;
-  static constexpr int kMmaPerStage = 4;
-  static constexpr int kSfChunks = 4;
-  static constexpr int kWBytes = kBM * kBKBytes;
-  static constexpr int kXBytes = kN * kBKBytes;
+  static constexpr int kBM = 128;        // weight rows per tile
+  static constexpr int kBoxBytes = 128;  // one SWIZZLE_128B box: 256 fp4 of K
+  static constexpr int kBoxes = 2;       // boxes per stage: 512 of K
+  static constexpr int kBKBytes = kBoxes * kBoxBytes;
+  // A stage carries 8 MMAs: the serial per-stage cost of the issue loops
+  // (barrier waits, commit) is paid once per 32 KB of weights.
+  static constexpr int kMmaPerStage = 4 * kBoxes;
+  static constexpr int kSfChunks = 4 * kBoxes;  // 512-byte chunks, 64 of K each
+  static constexpr int kWBox = kBM * kBoxBytes;
+  static constexpr int kXBox = kN * kBoxBytes;
+  static constexpr int kWBytes = kWBox * kBoxes;
+  static constexpr int kXBytes = kXBox * kBoxes;
   static constexpr int kSfwBytes = kSfChunks * 512;
   static constexpr int kSfxBytes = kSfChunks * 512;
   static constexpr int kStageTx = kWBytes + kXBytes + kSfwBytes + kSfxBytes;
   static constexpr int kStageBytes = (kStageTx + 1023) / 1024 * 1024;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 512 + 1024;
-  static constexpr int kSfStageCols = 32;  // 16 weight + 16 activation
-  static constexpr int kTmemSfBase = 256;
+  static constexpr int kSfStageCols = 8 * kSfChunks;  // 4 weight + 4 activation per chunk
+  static constexpr int kTmemSfBase = 2 * kN < 64 ? 64 : 2 * kN;
   static constexpr int kTmemCols = 512;
+  static constexpr int kSmemStages = (232448 - 512 - 1024) / kStageBytes;
+  static constexpr int kTmemStages = (kTmemCols - kTmemSfBase) / kSfStageCols;
+  static constexpr int kStages0 = kSmemStages < kTmemStages ? kSmemStages : kTmemStages;
+  static constexpr int kStages = kStages0 < 8 ? kStages0 : 8;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 512 + 1024;
+  static_assert(kStages >= 2, "pipeline depth");
   static_assert(2 * kN <= kTmemSfBase, "accumulators");
   static_assert(kTmemSfBase + kStages * kSfStageCols <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -58,11 +75,195 @@ struct UnitRange {
   int u0, u1, nkb;
 };
 
+// Order in which a CTA walks its range: the segment of its LAST tile first,
+// then the segment of its first tile, then the whole tiles between.  Both
+// segments a CTA shares with a neighbour are therefore finished early by
+// both neighbours, so the fixup of a split tile overlaps the streaming of
+// whole tiles instead of trailing the kernel.
+struct SegCursor {
+  int tile_lo, tile_hi, u0, u1, nkb;
+  int i, t, kb, kb_end;  // segment index, its tile, current / end K block
+  __device__ __forceinline__ void init(const UnitRange& r) {
+    u0 = r.u0;
+    u1 = r.u1;
+    nkb = r.nkb;
+    tile_lo = u0 / nkb;
+    tile_hi = (u1 - 1) / nkb;
+    i = 0;
+    enter();
+  }
+  __device__ __forceinline__ int nseg() const { return tile_hi - tile_lo + 1; }
+  __device__ __forceinline__ int tile_of(int s) const {
+    if (tile_hi == tile_lo) return tile_lo;
+    return s == 0 ? tile_hi : (s == 1 ? tile_lo : tile_lo + s - 1);
+  }
+  __device__ __forceinline__ void enter() {
+    t = tile_of(i);
+    kb = (t == tile_lo) ? u0 - t * nkb : 0;
+    kb_end = (t == tile_hi) ? u1 - t * nkb : nkb;
+  }
+  __device__ __forceinline__ bool seg_first() const {
+    return kb == ((t == tile_lo) ? u0 - t * nkb : 0);
+  }
+  __device__ __forceinline__ bool seg_last() const { return kb + 1 == kb_end; }
+  // Step to the next unit; false past the end of the range.
+  __device__ __forceinline__ bool next() {
+    if (++kb < kb_end) return true;
+    if (++i >= nseg()) return false;
+    enter();
+    return true;
+  }
+};
+
 // Diagnostic stamp (QG_DIAG_FLAGS bit 6): CTA 0 writes %globaltimer into
 // slot `i` of the last (never used by a launched CTA) partial slice pair.
+__device__ __forceinline__ void trace_cta(const SkinnyParams& p, int i) {
+  if (p.diag & 64u)
+    reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * 2 * p.m * 128)[i] = globaltimer_ns();
+}
 __device__ __forceinline__ void trace(const SkinnyParams& p, int i) {
   if ((p.diag & 64u) && blockIdx.x == 0 && i < 512)
     reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * 2 * p.m * 128)[i] = globaltimer_ns();
+}
+
+// ------------------------------------------------------------------ activation quantiser
+// Run by the 256 threads of warps 2..9 of every CTA before their GEMM roles,
+// while warp 0 already streams the first weight stages.  make_nvfp4_reference
+// (GEMMsm110/include/requant/nvfp4_reference.cuh:76-112) bit for bit, MMA
+// layout:
+//   1. each CTA reduces the amax of its contiguous range of 16-element
+//      blocks into amax_part[cta]; grid arrival #1;
+//   2. every CTA reduces amax_part, quantises its range into xq / xsf,
+//      zeroes its share of the padding scale slots and of the tile counters;
+//      grid arrival #2, after which x_ready lets the producer issue the
+//      activation loads.
+// The last CTA to leave resets the arrival counters for the next call.
+// Returns false when a grid arrival timed out (status recorded).
+constexpr int kQuantThreads = 256;
+constexpr uint32_t kQuantBar = 1;  // named barrier id of warps 2..9
+
+template <bool kBf16>
+__device__ bool quantize_phase(const SkinnyParams& p, int qt, float* red,
+                               volatile uint32_t* abort_flag, uint64_t* x_loaded,
+                               uint64_t* x_ready) {
+  constexpr int kFly = kBf16 ? 4 : 2;  // blocks in flight per thread
+  const int G = gridDim.x, c = blockIdx.x;
+  const int64_t sfk = p.k / 16;
+  const int64_t nblocks = static_cast<int64_t>(p.m) * sfk;
+  const int64_t b0 = nblocks * c / G, b1 = nblocks * (c + 1) / G;
+
+  // The first kFly blocks of a thread stay in registers for the second pass
+  // (decode-sized x: usually all of them), later ones are read again.
+  float mx = 0.0f;
+  RawBlock<kBf16> keep[kFly];
+  const int64_t chunk = static_cast<int64_t>(kFly) * kQuantThreads;
+#pragma unroll
+  for (int f = 0; f < kFly; ++f)
+    if (b0 + qt + f * kQuantThreads < b1) keep[f].load(p.x, b0 + qt + f * kQuantThreads);
+#pragma unroll
+  for (int f = 0; f < kFly; ++f) {
+    if (b0 + qt + f * kQuantThreads >= b1) break;
+    float v[16];
+    keep[f].decode(v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(v[i]));
+  }
+  for (int64_t base = b0 + qt + chunk; base < b1; base += chunk) {
+    RawBlock<kBf16> r[kFly];
+#pragma unroll
+    for (int f = 0; f < kFly; ++f)
+      if (base + f * kQuantThreads < b1) r[f].load(p.x, base + f * kQuantThreads);
+#pragma unroll
+    for (int f = 0; f < kFly; ++f) {
+      if (base + f * kQuantThreads >= b1) break;
+      float v[16];
+      r[f].decode(v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(v[i]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((qt & 31) == 0) red[qt >> 5] = mx;
+  named_bar_sync(kQuantBar, kQuantThreads);
+  if (qt == 0) {
+    trace(p, 4);
+    mbar_arrive(x_loaded);
+    float a = 0.0f;
+    for (int w = 0; w < kQuantThreads / 32; ++w) a = fmaxf(a, red[w]);
+    p.amax_part[c] = a;
+    const bool ok = grid_arrive_wait(&p.sync[0], G, p.timeout_ns, abort_flag, p.status,
+                                     kDevTimeoutGridSync);
+    red[8] = ok ? 1.0f : 0.0f;
+    trace(p, 5);
+  }
+  named_bar_sync(kQuantBar, kQuantThreads);
+  if (red[8] == 0.0f) return false;
+  if (qt < 32) {
+    float a = 0.0f;
+    for (int r = qt; r < G; r += 32) a = fmaxf(a, __ldcg(p.amax_part + r));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if (qt == 0) red[9] = a;
+  }
+  named_bar_sync(kQuantBar, kQuantThreads);
+  const float amax = red[9];
+  const float ts = amax > 0.0f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
+  const float inv_ts = __fdiv_rn(1.0f, ts);
+  if (c == 0 && qt == 0) *p.x_ts = ts;
+
+  const int64_t sf_blocks = (sfk + 3) / 4;  // one 128-row block: m <= 128
+  auto encode = [&](const RawBlock<kBf16>& r, int64_t b) {
+    float v[16];
+    r.decode(v);
+    uint32_t lo, hi;
+    const uint32_t sbits = nvfp4_encode_block(v, inv_ts, lo, hi);
+    reinterpret_cast<uint2*>(p.xq)[b] = make_uint2(lo, hi);
+    const int64_t row = b / sfk, sc = b - row * sfk;
+    p.xsf[mma_scale_offset(row, sc, 1, sf_blocks, 1)] = static_cast<uint8_t>(sbits);
+  };
+#pragma unroll
+  for (int f = 0; f < kFly; ++f)
+    if (b0 + qt + f * kQuantThreads < b1) encode(keep[f], b0 + qt + f * kQuantThreads);
+  for (int64_t base = b0 + qt + chunk; base < b1; base += chunk) {
+    RawBlock<kBf16> r[kFly];
+#pragma unroll
+    for (int f = 0; f < kFly; ++f)
+      if (base + f * kQuantThreads < b1) r[f].load(p.x, base + f * kQuantThreads);
+#pragma unroll
+    for (int f = 0; f < kFly; ++f)
+      if (base + f * kQuantThreads < b1) encode(r[f], base + f * kQuantThreads);
+  }
+  if (qt == 0) trace(p, 6);
+  // Padding scale slots (rows >= m, scale columns >= k/16) read as zero.
+  const int64_t cols_pad = sf_blocks * 4, npad = 128 * cols_pad;
+  const int64_t gt = static_cast<int64_t>(c) * kQuantThreads + qt, gstride = static_cast<int64_t>(G) * kQuantThreads;
+  if (npad != nblocks) {
+    for (int64_t i = gt; i < npad; i += gstride) {
+      const int64_t row = i / cols_pad, sc = i - row * cols_pad;
+      if (row >= p.m || sc >= sfk) p.xsf[mma_scale_offset(row, sc, 1, sf_blocks, 1)] = 0u;
+    }
+  }
+  for (int64_t i = gt; i < static_cast<int64_t>(p.num_tiles) * 4; i += gstride) p.cnt[i] = 0u;
+  asm volatile("fence.proxy.async.global;" ::: "memory");  // xq / xsf are read by TMA
+  named_bar_sync(kQuantBar, kQuantThreads);
+  if (qt == 0) trace(p, 7);
+  if (qt == 0) {
+    const bool ok = grid_arrive_wait(&p.sync[1], G, p.timeout_ns, abort_flag, p.status,
+                                     kDevTimeoutGridSync);
+    red[8] = ok ? 1.0f : 0.0f;
+    trace(p, 8);
+    if (ok) {
+      mbar_arrive(x_ready);
+      if (atomicAdd(&p.sync[2], 1u) == static_cast<uint32_t>(G - 1)) {
+        p.sync[0] = 0u;
+        p.sync[1] = 0u;
+        p.sync[2] = 0u;
+      }
+    }
+  }
+  named_bar_sync(kQuantBar, kQuantThreads);
+  return red[8] != 0.0f;
 }
 
 template <int kN>
@@ -78,8 +279,11 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
   uint64_t* acc_full = bars + 3 * Cfg::kStages;  // [2]
   uint64_t* acc_empty = acc_full + 2;            // [2]
   uint64_t* drain_bar = acc_full + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 5);
+  uint64_t* x_ready = acc_full + 5;   // quantised activations visible grid-wide
+  uint64_t* x_loaded = acc_full + 6;  // this CTA's quantiser has read its activations
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 7);
   volatile uint32_t* abort_flag = tmem_slot + 1;
+  float* qred = reinterpret_cast<float*>(tmem_slot + 2);  // [10] quantiser scratch
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -95,6 +299,8 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       mbar_init(&acc_empty[b], 4);
     }
     mbar_init(drain_bar, 1);
+    mbar_init(x_ready, 1);
+    mbar_init(x_loaded, 1);
     *abort_flag = 0u;
     fence_barrier_init();
     tma_prefetch_desc(&p.tm_w);
@@ -112,11 +318,19 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
   const uint32_t tmem_base = *tmem_slot;
 
   if (threadIdx.x == 0) trace(p, 0);
+  if (threadIdx.x == 0) trace_cta(p, 768 + blockIdx.x);
   const int64_t units = static_cast<int64_t>(p.num_tiles) * p.num_k_blocks;
   UnitRange ur;
   ur.u0 = static_cast<int>(units * blockIdx.x / gridDim.x);
   ur.u1 = static_cast<int>(units * (blockIdx.x + 1) / gridDim.x);
   ur.nkb = p.num_k_blocks;
+
+  bool quant_ok = true;
+  if (warp >= 2) {
+    const int qt = threadIdx.x - 64;
+    quant_ok = p.x_bf16 ? quantize_phase<true>(p, qt, qred, abort_flag, x_loaded, x_ready)
+                        : quantize_phase<false>(p, qt, qred, abort_flag, x_loaded, x_ready);
+  }
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA
@@ -125,28 +339,57 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       const uint64_t pol_x = l2_policy_evict_last();   // activations: reused by all CTAs
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      int stage = 0, tile = ur.u0 / ur.nkb, kb = ur.u0 % ur.nkb;
+      int stage = 0;
       uint32_t phase = 0;
-      // The first kStages stages get their weight loads at once; their
-      // activation loads wait for the quantizer grid (griddep_wait), so the
-      // weight stream starts while the activations are being quantised.
+      // The first kStages stages get their weight loads at once and the
+      // next kL2Ahead units' weights are prefetched into L2; the activation
+      // loads wait for the in-kernel quantiser (x_ready), so the weight
+      // stream runs while the activations are being quantised.  On a
+      // quantiser timeout the deferred loads are still issued (the buffers
+      // are valid memory) so every armed stage completes before exit.
+      constexpr int kL2Ahead = QG_SKINNY_L2_AHEAD;  // units (32 KB of weights each)
       int deferred = 0;
       int dkb[Cfg::kStages];
       auto issue_x = [&](int s, int k_blk) {
         uint8_t* sx = smem + s * Cfg::kStageBytes + Cfg::kWBytes;
         uint8_t* ssfx = sx + Cfg::kXBytes + Cfg::kSfwBytes;
         tma_load_3d(ssfx, &p.tm_sfx, &full_bar[s], 0, 0, k_blk * Cfg::kSfChunks, pol_x);
-        tma_load_2d(sx, &p.tm_x, &full_bar[s], k_blk * Cfg::kBKBytes, 0, pol_x);
+#pragma unroll
+        for (int h = 0; h < Cfg::kBoxes; ++h)
+          tma_load_2d(sx + h * Cfg::kXBox, &p.tm_x, &full_bar[s],
+                      k_blk * Cfg::kBKBytes + h * Cfg::kBoxBytes, 0, pol_x);
       };
       bool dep_done = false;
-      auto release_deferred = [&]() {
-        griddep_wait();
+      auto release_deferred = [&](SegCursor ahead, bool more) {
+        for (int i = 0; more && i < kL2Ahead; ++i) {
+          tma_prefetch_l2_3d(&p.tm_sfw, 0, ahead.t, ahead.kb * Cfg::kSfChunks);
+#pragma unroll
+          for (int h = 0; h < Cfg::kBoxes; ++h)
+            tma_prefetch_l2_2d(&p.tm_w, ahead.kb * Cfg::kBKBytes + h * Cfg::kBoxBytes,
+                               ahead.t * Cfg::kBM);
+          more = ahead.next();
+        }
+        if (!mbar_wait_bounded(x_ready, 0, p.timeout_ns, abort_flag, p.status,
+                               kDevTimeoutProducer))
+          ok = false;
+        asm volatile("fence.proxy.async.global;" ::: "memory");
         trace(p, 2);
         for (int s = 0; s < deferred; ++s) issue_x(s, dkb[s]);
         dep_done = true;
       };
-      for (int u = ur.u0, g = 0; u < ur.u1; ++u, ++g) {
-        if (!dep_done && g == Cfg::kStages) release_deferred();
+      // The weight stream starts once this CTA's quantiser has read its
+      // share of the activations, so those reads do not queue behind it.
+      if (!mbar_wait_bounded(x_loaded, 0, p.timeout_ns, abort_flag, p.status,
+                             kDevTimeoutProducer))
+        ok = false;
+      SegCursor cur;
+      cur.init(ur);
+      bool more = ok;
+      for (int g = 0; more; ++g) {
+        if (!dep_done && g == Cfg::kStages) {
+          release_deferred(cur, true);
+          if (!ok) break;
+        }
         if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.timeout_ns, abort_flag, p.status,
                                kDevTimeoutProducer)) {
           ok = false;
@@ -156,25 +399,25 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
         uint8_t* ssfw = sw + Cfg::kWBytes + Cfg::kXBytes;
         trace(p, 16 + g);
         mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageTx);
-        tma_load_3d(ssfw, &p.tm_sfw, &full_bar[stage], 0, tile, kb * Cfg::kSfChunks, pol_w);
-        tma_load_2d(sw, &p.tm_w, &full_bar[stage], kb * Cfg::kBKBytes, tile * Cfg::kBM, pol_w);
+        tma_load_3d(ssfw, &p.tm_sfw, &full_bar[stage], 0, cur.t, cur.kb * Cfg::kSfChunks, pol_w);
+#pragma unroll
+        for (int h = 0; h < Cfg::kBoxes; ++h)
+          tma_load_2d(sw + h * Cfg::kWBox, &p.tm_w, &full_bar[stage],
+                      cur.kb * Cfg::kBKBytes + h * Cfg::kBoxBytes, cur.t * Cfg::kBM, pol_w);
         if (dep_done) {
-          issue_x(stage, kb);
+          issue_x(stage, cur.kb);
         } else {
-          dkb[deferred++] = kb;
+          dkb[deferred++] = cur.kb;
         }
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-        if (++kb == ur.nkb) {
-          kb = 0;
-          ++tile;
-        }
+        more = cur.next();
         if (++stage == Cfg::kStages) {
           stage = 0;
           phase ^= 1u;
         }
       }
-      if (!dep_done) release_deferred();
+      if (!dep_done) release_deferred(cur, false);
       if (!ok) {
         uint32_t dummy = 0;
         for (int s = 0; s < Cfg::kStages; ++s)
@@ -186,56 +429,68 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
     if (lane == 0) {
-      // The issue loop is the kernel's serial path: counters are stepped
-      // incrementally and descriptors offset by constants, so no division or
-      // modulo runs per unit.
+      // The issue loop is the kernel's serial path (one thread, a dependent
+      // instruction chain): segments are walked outside, the per-unit body
+      // is a wait, eight MMAs and a commit, with descriptors and scale
+      // columns stepped by constants.
       const uint32_t idesc = make_idesc_block_scaled(Cfg::kBM, kN, 1u, 0u, 0u, 0u);
       const uint64_t wdesc0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
       const uint64_t xdesc0 = make_smem_desc(smem_u32(smem + Cfg::kWBytes), 16, 1024, kSwizzle128B);
       constexpr uint64_t kStageDesc = Cfg::kStageBytes >> 4;
       bool ok = true;
-      int seg = 0, stage = 0, kb = ur.u0 % ur.nkb;
-      uint32_t phase = 0, acc = 0;
-      for (int u = ur.u0; u < ur.u1 && ok; ++u) {
+      int stage = 0, g = 0;
+      uint32_t phase = 0;
+      uint64_t wdesc = wdesc0, xdesc = xdesc0;
+      uint32_t sfw_col = tmem_base + Cfg::kTmemSfBase;
+      SegCursor order;
+      order.init(ur);
+      for (int seg = 0; ok && seg < order.nseg(); ++seg) {
+        const int t = order.tile_of(seg);
+        const int kb_lo = (t == order.tile_lo) ? ur.u0 - t * ur.nkb : 0;
+        const int kb_hi = (t == order.tile_hi) ? ur.u1 - t * ur.nkb : ur.nkb;
         const int buf = seg & 1;
-        if (u == ur.u0 || kb == 0) {
-          if (!mbar_wait_bounded(&acc_empty[buf], ((seg >> 1) & 1) ^ 1u, p.timeout_ns, abort_flag,
-                                 p.status, kDevTimeoutMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          acc = 0;
-        }
-        if (!mbar_wait_bounded(&sf_ready[stage], phase, p.timeout_ns, abort_flag, p.status,
-                               kDevTimeoutMma) ||
-            !mbar_wait_bounded(&full_bar[stage], phase, p.timeout_ns, abort_flag, p.status,
-                               kDevTimeoutMma)) {
+        if (!mbar_wait_bounded(&acc_empty[buf], ((seg >> 1) & 1) ^ 1u, p.timeout_ns, abort_flag,
+                               p.status, kDevTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sfw_col = tmem_base + Cfg::kTmemSfBase + stage * Cfg::kSfStageCols;
-        const uint64_t wdesc = wdesc0 + stage * kStageDesc;
-        const uint64_t xdesc = xdesc0 + stage * kStageDesc;
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kN);
+        uint32_t acc = 0;
+        for (int j = kb_lo; j < kb_hi; ++j, ++g) {
+          // sf_ready is arrived by the stagers only after they observed
+          // full_bar, so it also orders the TMA data of the stage.
+          if (!mbar_wait_bounded(&sf_ready[stage], phase, p.timeout_ns, abort_flag, p.status,
+                                 kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int j = 0; j < Cfg::kMmaPerStage; ++j) {
-          const uint64_t koff = static_cast<uint64_t>(j * 2);
-          mma_mxf4nvf4(d_tmem, wdesc + koff, xdesc + koff, idesc, sfw_col + j * 4,
-                       sfw_col + 16 + j * 4, acc);
-          acc = 1;
+          for (int i = 0; i < Cfg::kMmaPerStage; ++i) {
+            // MMA i: box i / 4, 32-byte K step (i % 4) inside the 128-byte row.
+            const uint64_t wo = static_cast<uint64_t>((i / 4) * (Cfg::kWBox >> 4) + (i % 4) * 2);
+            const uint64_t xo = static_cast<uint64_t>((i / 4) * (Cfg::kXBox >> 4) + (i % 4) * 2);
+            mma_mxf4nvf4(d_tmem, wdesc + wo, xdesc + xo, idesc, sfw_col + i * 4,
+                         sfw_col + 4 * Cfg::kSfChunks + i * 4, acc);
+            acc = 1;
+          }
+          tc_commit(&empty_bar[stage]);
+          trace(p, 320 + g);
+          if (++stage == Cfg::kStages) {
+            stage = 0;
+            phase ^= 1u;
+            wdesc = wdesc0;
+            xdesc = xdesc0;
+            sfw_col = tmem_base + Cfg::kTmemSfBase;
+          } else {
+            wdesc += kStageDesc;
+            xdesc += kStageDesc;
+            sfw_col += Cfg::kSfStageCols;
+          }
         }
-        tc_commit(&empty_bar[stage]);
-        if (u == ur.u1 - 1 || kb == ur.nkb - 1) {
-          tc_commit(&acc_full[buf]);
-          ++seg;
-        }
-        if (++kb == ur.nkb) kb = 0;
-        if (++stage == Cfg::kStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (!ok) break;
+        tc_commit(&acc_full[buf]);
       }
       tc_commit(drain_bar);
       uint32_t dummy = 0;
@@ -247,7 +502,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
     const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     int stage = 0;
     uint32_t phase = 0;
-    for (int u = ur.u0; u < ur.u1; ++u) {
+    for (int u = ur.u0; quant_ok && u < ur.u1; ++u) {
       bool ok = true;
       if (lane == 0)
         ok = mbar_wait_bounded(&full_bar[stage], phase, p.timeout_ns, abort_flag, p.status,
@@ -256,17 +511,17 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       mbar_try_wait(&full_bar[stage], phase);
       const uint8_t* ssfw = smem + stage * Cfg::kStageBytes + Cfg::kWBytes + Cfg::kXBytes;
       const uint8_t* ssfx = ssfw + Cfg::kSfwBytes;
-      uint32_t a[16], b[16];
+      uint32_t a[4 * Cfg::kSfChunks], b[4 * Cfg::kSfChunks];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < Cfg::kSfChunks; ++c) {
         const uint4 v = lds128(ssfw + c * 512 + lane * 16);
         const uint4 w = lds128(ssfx + c * 512 + lane * 16);
         a[4 * c] = v.x; a[4 * c + 1] = v.y; a[4 * c + 2] = v.z; a[4 * c + 3] = v.w;
         b[4 * c] = w.x; b[4 * c + 1] = w.y; b[4 * c + 2] = w.z; b[4 * c + 3] = w.w;
       }
       const uint32_t col = Cfg::kTmemSfBase + stage * Cfg::kSfStageCols;
-      tmem_st_32x32b<16>(t_quad + col, a);
-      tmem_st_32x32b<16>(t_quad + col + 16, b);
+      tmem_st_32x32b<4 * Cfg::kSfChunks>(t_quad + col, a);
+      tmem_st_32x32b<4 * Cfg::kSfChunks>(t_quad + col + 4 * Cfg::kSfChunks, b);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -286,9 +541,8 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
     // depend on which CTA finished last.
     const int quad = warp % 4;
     const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
-    griddep_wait();  // the tensor scale and the counters come from the quantizer grid
     if (quad == 0 && lane == 0) trace(p, 3);
-    const float alpha = (p.x_ts ? *p.x_ts : 1.0f) * (p.w_ts ? *p.w_ts : 1.0f);
+    const float alpha = __ldcg(p.x_ts) * (p.w_ts ? *p.w_ts : 1.0f);
     const int64_t units_all = static_cast<int64_t>(p.num_tiles) * ur.nkb;
     const int64_t grid = gridDim.x;
     auto contributor = [&](int64_t u) { return static_cast<int>(((u + 1) * grid - 1) / units_all); };
@@ -300,9 +554,11 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       else
         reinterpret_cast<float*>(p.c)[static_cast<int64_t>(m) * p.ldc + n] = v;
     };
-    const int tile_lo = ur.u0 / ur.nkb, tile_hi = (ur.u1 - 1) / ur.nkb;
-    const int my_first = tile_lo;
-    for (int t = tile_lo, seg = 0; t <= tile_hi; ++t, ++seg) {
+    SegCursor order;
+    order.init(ur);
+    const int my_first = order.tile_lo;
+    for (int seg = 0; quant_ok && seg < order.nseg(); ++seg) {
+      const int t = order.tile_of(seg);
       const int buf = seg & 1;
       bool ok = true;
       if (lane == 0)
@@ -344,55 +600,91 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       if (quad == 0 && lane == 0) trace(p, 100 + seg);
       if (cf == cl) continue;
       __threadfence();
+      if (quad == 0 && lane == 0) trace(p, 300 + 4 * seg);
       __syncwarp();
       uint32_t old = 0;
       if (lane == 0) old = atomicAdd(&p.cnt[t * 4 + quad], 1u);
       old = __shfl_sync(0xffffffffu, old, 0);
+      if (quad == 0 && lane == 0) trace(p, 301 + 4 * seg);
       if (old != static_cast<uint32_t>(cl - cf)) continue;
       __threadfence();
-      // Sum pass: a lane takes 4 adjacent columns of one row, a warp
-      // instruction 4 rows x 32 columns; 8 instructions x 2 contributors of
-      // 16-byte loads are in flight per warp before the adds, in order.
+      if (quad == 0 && lane == 0) trace(p, 302 + 4 * seg);
+      // Sum pass: a lane takes 8 adjacent columns of one row, a warp
+      // instruction 8 rows x 32 columns; 4 steps x 2 contributors x 32 bytes
+      // are in flight per lane before the adds (in contributor order), and
+      // each step ends in one 16-byte (bf16) or two (fp32) stores per lane.
       {
-        const int sub = lane >> 3, c4 = (lane & 7) * 4;
+        const int sub = lane >> 2, c8 = (lane & 3) * 8;
         const int64_t slice = static_cast<int64_t>(p.m) * Cfg::kBM;
+        const int nb = t * Cfg::kBM + quad * 32 + c8;
+        const bool vec = p.vec_ok && nb + 8 <= p.n;
         for (int m0 = 0; m0 < p.m; m0 += 32) {
-          float4 acc[8];
+          float acc[4][8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[i][e] = 0.0f;
           for (int c = cf; c <= cl; c += 2) {
             const bool two = c + 1 <= cl;
-            const float* s0 = p.part + (c * 2 + (t == first_tile(c) ? 0 : 1)) * slice + quad * 32 + c4;
+            const float* s0 = p.part + (c * 2 + (t == first_tile(c) ? 0 : 1)) * slice + quad * 32 + c8;
             const float* s1 = two ? p.part + ((c + 1) * 2 + (t == first_tile(c + 1) ? 0 : 1)) * slice +
-                                        quad * 32 + c4
+                                        quad * 32 + c8
                                   : s0;
-            float4 v0[8], v1[8];
+            float4 v0[4][2], v1[4][2];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int m = m0 + i * 4 + sub;
+            for (int i = 0; i < 4; ++i) {
+              const int m = m0 + i * 8 + sub;
               const bool ok = m < p.m;
-              v0[i] = ok ? __ldcg(reinterpret_cast<const float4*>(s0 + m * Cfg::kBM))
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-              v1[i] = ok && two ? __ldcg(reinterpret_cast<const float4*>(s1 + m * Cfg::kBM))
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              acc[i].x += v0[i].x; acc[i].y += v0[i].y; acc[i].z += v0[i].z; acc[i].w += v0[i].w;
-              if (two) {
-                acc[i].x += v1[i].x; acc[i].y += v1[i].y; acc[i].z += v1[i].z; acc[i].w += v1[i].w;
+              for (int h = 0; h < 2; ++h) {
+                v0[i][h] = ok ? __ldcg(reinterpret_cast<const float4*>(s0 + m * Cfg::kBM) + h)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                v1[i][h] = ok && two ? __ldcg(reinterpret_cast<const float4*>(s1 + m * Cfg::kBM) + h)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
               }
             }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                acc[i][4 * h] += v0[i][h].x; acc[i][4 * h + 1] += v0[i][h].y;
+                acc[i][4 * h + 2] += v0[i][h].z; acc[i][4 * h + 3] += v0[i][h].w;
+                if (two) {
+                  acc[i][4 * h] += v1[i][h].x; acc[i][4 * h + 1] += v1[i][h].y;
+                  acc[i][4 * h + 2] += v1[i][h].z; acc[i][4 * h + 3] += v1[i][h].w;
+                }
+              }
           }
-          const int nb = t * Cfg::kBM + quad * 32 + c4;
+          if (quad == 0 && lane == 0 && m0 == 0) trace(p, 303 + 4 * seg);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int m = m0 + i * 4 + sub;
+          for (int i = 0; i < 4; ++i) {
+            const int m = m0 + i * 8 + sub;
             if (m >= p.m) continue;
-            const float e[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+            if (vec) {
+              if (p.out_bf16) {
+                uint32_t w[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              if (nb + q < p.n) store_c(m, nb + q, e[q] * alpha);
+                for (int e = 0; e < 4; ++e) {
+                  const __nv_bfloat162 h2 =
+                      __floats2bfloat162_rn(acc[i][2 * e] * alpha, acc[i][2 * e + 1] * alpha);
+                  w[e] = *reinterpret_cast<const uint32_t*>(&h2);
+                }
+                *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.c) +
+                                          static_cast<int64_t>(m) * p.ldc + nb) =
+                    make_uint4(w[0], w[1], w[2], w[3]);
+              } else {
+                float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.c) +
+                                                        static_cast<int64_t>(m) * p.ldc + nb);
+                dst[0] = make_float4(acc[i][0] * alpha, acc[i][1] * alpha, acc[i][2] * alpha,
+                                     acc[i][3] * alpha);
+                dst[1] = make_float4(acc[i][4] * alpha, acc[i][5] * alpha, acc[i][6] * alpha,
+                                     acc[i][7] * alpha);
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                if (nb + e < p.n) store_c(m, nb + e, acc[i][e] * alpha);
+            }
           }
         }
       }
@@ -404,6 +696,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) trace(p, 1);
+  if (threadIdx.x == 0) trace_cta(p, 512 + blockIdx.x);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
@@ -427,8 +720,10 @@ static cudaError_t launch_skinny_n(const SkinnyParams& p, int grid, cudaStream_t
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  // Cooperative: every CTA is resident at once (the quantiser's grid-wide
+  // arrivals rely on it), or the launch fails.
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, p);

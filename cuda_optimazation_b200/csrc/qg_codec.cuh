@@ -1,5 +1,5 @@
 // qg_codec.cuh -- NVFP4 element / scale codecs and vector loads shared by the
-// activation quantizers (quantize.cu, skinny_quant.cu).  Rounding follows
+// activation quantizers (quantize.cu, gemm_skinny.cu).  Rounding follows
 // make_nvfp4_reference (GEMMsm110/include/requant/nvfp4_reference.cuh:76-112).
 #pragma once
 #include <cuda_bf16.h>
@@ -84,6 +84,56 @@ __device__ __forceinline__ float load1(const void* x, int64_t i) {
     return __uint_as_float(static_cast<uint32_t>(h) << 16);
   }
   return reinterpret_cast<const float*>(x)[i];
+}
+
+// Raw 16-element block (bf16: 32 bytes, fp32: 64 bytes), so several blocks'
+// loads can be in flight per thread before any is decoded.
+template <bool kBf16>
+struct RawBlock {
+  uint4 w[kBf16 ? 2 : 4];
+  __device__ __forceinline__ void load(const void* x, int64_t blk) {
+    const uint4* p = reinterpret_cast<const uint4*>(x) + blk * (kBf16 ? 2 : 4);
+#pragma unroll
+    for (int i = 0; i < (kBf16 ? 2 : 4); ++i) w[i] = __ldg(p + i);
+  }
+  __device__ __forceinline__ void decode(float (&v)[16]) const {
+#pragma unroll
+    for (int i = 0; i < (kBf16 ? 2 : 4); ++i) {
+      const uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (kBf16) {
+          v[8 * i + 2 * j] = __uint_as_float(u[j] << 16);
+          v[8 * i + 2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+        } else {
+          v[4 * i + j] = __uint_as_float(u[j]);
+        }
+      }
+    }
+  }
+};
+
+// One 16-element NVFP4 block in the MMA order (low nibble first): returns the
+// ue4m3 scale code, packs the 16 e2m1 codes into lo/hi.
+__device__ __forceinline__ uint32_t nvfp4_encode_block(const float (&v)[16], float inv_ts,
+                                                       uint32_t& lo, uint32_t& hi) {
+  float bmax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
+  const float namax = __fmul_rn(bmax, inv_ts);  // == max|x * inv_ts| (RN is monotonic)
+  const uint32_t sbits = e4m3_round_up(__fdiv_rn(namax, 6.0f));
+  const float bs = e4m3_decode_positive(sbits);
+  const float mult = bs > 0.0f ? __fdiv_rn(inv_ts, bs) : 0.0f;
+  lo = 0;
+  hi = 0;
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    const uint32_t byte =
+        e2m1_encode(__fmul_rn(v[i], mult)) | (e2m1_encode(__fmul_rn(v[i + 1], mult)) << 4);
+    if (i < 8) lo |= byte << (4 * i);
+    else hi |= byte << (4 * (i - 8));
+  }
+  return sbits;
 }
 
 }  // namespace qg

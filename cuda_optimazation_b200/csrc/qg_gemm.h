@@ -29,38 +29,39 @@ struct GemmParams {
 
 // Decode-shaped NVFP4 GEMM (gemm_skinny.cu): weights W [n][k] on the MMA's M
 // side, activations X [m][k] (m <= 128) on its N side, stream-K over
-// (weight tile, K block) units.  A tile split between CTAs is summed by the
-// last contributor to finish it (per-tile counters), in a fixed order, from
+// (weight tile, K block) units.  The activation quantisation runs inside the
+// same (cooperative) grid, on the warps that are idle while the first weight
+// stages stream in.  A tile split between CTAs is summed by the last
+// contributor to finish it (per-tile counters), in a fixed order, from
 // per-CTA partial slices; whole tiles are written straight to C.
 struct SkinnyParams {
   CUtensorMap tm_w;    // uint8 [n][k/2], box 128 B x 128 rows, SWIZZLE_128B
-  CUtensorMap tm_x;    // uint8 [m][k/2], box 128 B x mma_n rows, SWIZZLE_128B
+  CUtensorMap tm_x;    // uint8 [m][k/2] (the quantised xq), box 128 B x mma_n rows
   CUtensorMap tm_sfw;  // uint32 chunks, box (128, 1, 4)
   CUtensorMap tm_sfx;
+  const void* x;       // activations, fp32 or bf16 [m][k]
+  int x_bf16;
+  uint8_t* xq;         // quantised activations [m][k/2]
+  uint8_t* xsf;        // their scales, MMA layout
+  float* x_ts;         // their tensor scale
+  float* amax_part;    // [grid] per-CTA amax
+  uint32_t* sync;      // [3] grid arrival counters, zero between calls
   float* part;         // [grid][2][m][128] fp32 partial tiles
-  uint32_t* cnt;       // [num_tiles][4] arrival counters, zero between calls
+  uint32_t* cnt;       // [num_tiles][4] tile arrival counters, zero between calls
   void* c;
   int64_t ldc;
-  const float* x_ts;   // activation tensor scale (written by the quantizer)
   const float* w_ts;   // weight tensor scale (may be null)
   int out_bf16;
+  int vec_ok;          // C rows start 16-byte aligned (16-byte stores legal)
   int m, n, k;
   int num_tiles, num_k_blocks;
   uint32_t* status;
   uint64_t timeout_ns;
   // Diagnostics (QG_DIAG_FLAGS): bit 6 writes %globaltimer stamps of CTA 0's
-  // roles into the partial buffer instead of results.
+  // roles into an unused partial slice.
   uint32_t diag;
 };
-// The GEMM is launched as a programmatic dependent of the activation
-// quantizer: its prologue and first weight loads overlap the quantizer.
 cudaError_t launch_gemm_skinny(const SkinnyParams& p, int grid, cudaStream_t stream);
-// One thread-block cluster quantises X [m][k] (m <= 128) to NVFP4 in the MMA
-// scale layout (padding scale slots zeroed), writes the tensor scale, and
-// zeroes `ncnt` counters.
-cudaError_t launch_skinny_quantize(const void* x, bool bf16, int64_t m, int64_t k, uint8_t* q,
-                                   uint8_t* sf, float* ts, uint32_t* cnt, int64_t ncnt,
-                                   cudaStream_t stream);
 int skinny_max_ctas();
 int skinny_mma_n(int64_t m);
 

@@ -18,6 +18,7 @@ enum : uint32_t {
   kDevTimeoutMma = 2,
   kDevTimeoutEpilogue = 3,
   kDevTimeoutTest = 4,
+  kDevTimeoutGridSync = 5,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -28,16 +29,6 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
-}
-
-// Programmatic dependent launch: a dependent grid may start while its
-// primary runs; griddep_wait() returns once the primary grid has completed
-// and its memory is visible.  A no-op when the launch had no such edge.
-__device__ __forceinline__ void griddep_wait() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-__device__ __forceinline__ void griddep_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ------------------------------------------------------------------ mbarrier
@@ -122,7 +113,55 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// ------------------------------------------------------------------ grid-wide arrival counters
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One thread per CTA: publish this CTA's prior global writes (generic and
+// async proxy), count it in *ctr and wait, bounded, until `expected` CTAs
+// have arrived.  On timeout records `code` and raises *abort_flag.
+__device__ __forceinline__ bool grid_arrive_wait(uint32_t* ctr, uint32_t expected,
+                                                 uint64_t timeout_ns,
+                                                 volatile uint32_t* abort_flag, uint32_t* status,
+                                                 uint32_t code) {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  __threadfence();
+  atomicAdd(ctr, 1u);
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_gpu(ctr) < expected) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      *abort_flag = 1u;
+      if (status) atomicCAS(status, 0u, code);
+      return false;
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
 // ------------------------------------------------------------------ TMA
+// Bring a tensor-map tile into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }

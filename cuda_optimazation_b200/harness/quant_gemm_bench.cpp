@@ -315,6 +315,7 @@ Row run_skinny(const Options& o) {
   CHECK_QG(qg_quantize_nvfp4(dw, QG_DTYPE_F32, n, k, QG_LAYOUT_MMA, wq, wsf, wts, qws, nullptr));
   const size_t wsb = qg_gemm_nvfp4_skinny_workspace_bytes(m, n, k);
   void* ws = dalloc(wsb);
+  CHECK_CUDA(cudaMemset(ws, 0, wsb));  // counters start at zero
   const int cdt = o.out_bf16 ? QG_DTYPE_BF16 : QG_DTYPE_F32;
   void* dc = dalloc(m * n * (o.out_bf16 ? 2 : 4));
   Row r;
@@ -326,13 +327,13 @@ Row run_skinny(const Options& o) {
                                   QG_LAYOUT_MMA, ws, wsb, nullptr, nullptr));
   }, o.iterations);
   r.gflops = 2.0 * m * n * k / (r.ms * 1e6);
-  // The quantised activations live in the workspace after the fp32 sums.
-  auto al = [](int64_t v) { return (v + 255) / 256 * 256; };
-  const uint8_t* base = static_cast<const uint8_t*>(ws);
-  const uint8_t* xq = base + al(m * n * 4);
-  const uint8_t* xsf = xq + al(m * k / 2);
-  const float* xts = reinterpret_cast<const float*>(xsf + al(qg_scale_bytes(m, k, 16)));
+  // The check quantises the activations with the standalone quantiser (the
+  // fused one is specified to match it bit for bit).
+  void *xq = dalloc(m * k / 2), *xsf = dalloc(qg_scale_bytes(m, k, 16));
+  float* xts = static_cast<float*>(dalloc(4));
+  CHECK_QG(qg_quantize_nvfp4(dx, QG_DTYPE_F32, m, k, QG_LAYOUT_MMA, xq, xsf, xts, qws, nullptr));
   auto A = fetch_nvfp4(xq, xsf, xts, m, k), W = fetch_nvfp4(wq, wsf, wts, n, k);
+  for (void* p : {xq, xsf, static_cast<void*>(xts)}) cudaFree(p);
   r.matched = check_rows(A, W, fetch_c(dc, m * n, o.out_bf16), m, n, o.out_bf16, &r.frob);
   for (void* p : {static_cast<void*>(dx), static_cast<void*>(dw), wq, wsf,
                   static_cast<void*>(wts), qws, ws, dc})

@@ -225,6 +225,13 @@ def block_scaled_gemm(a, b, out_dtype: torch.dtype = torch.bfloat16,
     return out
 
 
+def skinny_workspace(m: int, n: int, k: int, device) -> torch.Tensor:
+    """A zero-filled workspace for gemm_nvfp4_skinny (reusable across calls
+    on one stream: every completed call leaves its counters zero)."""
+    need = int(lib().qg_gemm_nvfp4_skinny_workspace_bytes(m, n, k))
+    return torch.zeros(need, dtype=torch.uint8, device=device)
+
+
 def gemm_nvfp4_skinny(x: torch.Tensor, w: "Nvfp4Result", out_dtype: torch.dtype = torch.bfloat16,
                       out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
                       status: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
@@ -239,7 +246,7 @@ def gemm_nvfp4_skinny(x: torch.Tensor, w: "Nvfp4Result", out_dtype: torch.dtype 
         out = torch.empty(m, n, dtype=out_dtype, device=x.device)
     need = int(lib().qg_gemm_nvfp4_skinny_workspace_bytes(m, n, k))
     if workspace is None or workspace.numel() < need:
-        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+        workspace = skinny_workspace(m, n, k, x.device)
     rc = lib().qg_gemm_nvfp4_skinny(x.data_ptr(), _dtype_code(x), m, w.quantized.data_ptr(),
                                     w.block_scales.data_ptr(), w.tensor_scale.data_ptr(),
                                     out.data_ptr(), _dtype_code(out), n, k, out.stride(0),

@@ -156,8 +156,13 @@ int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void
  * qg_quantize_nvfp4 would, then C[m, n] = (ts_x * w_ts) * x_q . w_q^T with the
  * pre-quantised weights w_q (n x k, MMA layout, scales in sf_layout).  The
  * weights are streamed once at HBM rate (stream-K over 128-row weight tiles
- * on every SM).  `workspace` (device, qg_gemm_nvfp4_skinny_workspace_bytes)
- * holds the fp32 partial sums and the quantised activations.  K % 32 == 0.
+ * on every SM), in ONE cooperative launch that also quantises x.
+ * `workspace` (device, qg_gemm_nvfp4_skinny_workspace_bytes) holds the
+ * partial tiles, the quantised activations and grid arrival counters: it
+ * must be zero-filled before its first use and is left ready for the next
+ * call (re-zero it after a call that returned a device timeout).  One
+ * workspace serves one stream at a time.  K % 32 == 0.  The result is
+ * deterministic (split tiles are summed in a fixed order).
  * No reference counterpart kernel: the reference harness runs square
  * problems only (GEMMquant_sm110/src/quant_gemm_bench.cu:3038-3079); this is
  * the decode configuration of its quant-GEMM path. */

@@ -65,3 +65,39 @@ def test_skinny_rejects_large_m(qlib):
                                 d.data_ptr(), 1, 256, 256, 256, 1, d.data_ptr(), 1 << 30, None,
                                 None)
     assert rc == qlib.ERR_SHAPE
+
+
+def test_skinny_fp32_activations(qlib, oracle):
+    """fp32 x (the other input dtype of the in-kernel quantiser)."""
+    m, n, k = 24, 640, 2048
+    xa = oracle.normal(m * k, 321).reshape(m, k)
+    xw = oracle.normal(n * k, 8, 0.0, 0.02).reshape(n, k)
+    W = qlib.make_nvfp4(torch.from_numpy(xw).cuda())
+    got = qlib.gemm_nvfp4_skinny(torch.from_numpy(xa).cuda(), W, torch.float32).cpu().numpy()
+    qa, sa, ta = oracle.nvfp4_mma(xa, 0)
+    qw, sw, tw = oracle.nvfp4_mma(xw, 0)
+    av, asf = oracle.nvfp4_decode(qa, sa, m, k)
+    wv, wsf = oracle.nvfp4_decode(qw, sw, n, k)
+    ref = oracle.gemm(av, wv, asf, wsf, m, n, k, 16) * np.float32(np.float32(ta) * np.float32(tw))
+    check_gemm(got, ref)
+
+
+def test_skinny_workspace_reuse_and_determinism(qlib, oracle):
+    """One workspace across calls with different activations: the grid and
+    tile counters reset themselves, and split tiles are summed in a fixed
+    order, so a repeated call is bit-identical."""
+    m, n, k = 16, 28672, 2048
+    xw = oracle.normal(n * k, 9, 0.0, 0.02).reshape(n, k)
+    W = qlib.make_nvfp4(torch.from_numpy(xw).cuda())
+    ws = qlib.skinny_workspace(m, n, k, "cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    xs = [activations(oracle, m, k, s).cuda() for s in (1, 2)]
+    outs = [qlib.gemm_nvfp4_skinny(xs[i % 2], W, torch.float32, workspace=ws, status=status)
+            for i in range(4)]
+    rc, code = qlib.read_status(status)
+    assert rc == qlib.OK, code
+    assert torch.equal(outs[0], outs[2]) and torch.equal(outs[1], outs[3])
+    assert not torch.equal(outs[0], outs[1])
+    # Counters are left zero (the trailing grid-arrival words included).
+    fresh = qlib.gemm_nvfp4_skinny(xs[0], W, torch.float32)
+    assert torch.equal(fresh, outs[0])
