@@ -8,9 +8,13 @@
 //
 // A cluster of two CTAs (one per SM) owns a 256 x 256 output tile.  Each CTA
 // loads its own 128 rows of A and its own 128-row half of B; the leader CTA
-// (rank 0) issues tcgen05.mma.cta_group::2 (M = 256, N = 256), which reads A
-// and B from both CTAs' shared memory and accumulates rows [0,128) in the
-// leader's TMEM and rows [128,256) in the peer's.
+// (rank 0) issues tcgen05.mma.cta_group::2, which reads A and B from both
+// CTAs' shared memory and accumulates rows [0,128) in the leader's TMEM and
+// rows [128,256) in the peer's.  For NVFP4 two leader threads (warps 1 and
+// 10) issue M = 256, N = 128 MMAs into the two halves of the accumulator:
+// measured, one issuing thread spends ~56 ns per MMA plus ~150 ns per stage
+// on waits and commits, more than the 4 x 69 ns the tensor pipe needs for a
+// stage at N = 256, and issues from two warps overlap.
 //
 // Scale factors reach TMEM through tcgen05.st from registers, not through
 // tcgen05.cp: copy instructions execute in the tensor pipe in order with the
@@ -20,11 +24,12 @@
 // memory and write the layout the MMA reads (row r at lane r%32 of every
 // quadrant, column r/32, byte = scale index) for their own quadrant.
 //
-// Roles (both CTAs, 10 warps):
+// Roles (both CTAs, 10 warps, 11 for NVFP4):
 //   warp 0      TMA producer.  A/B loads complete on the LEADER's full barrier
 //               (cta_group::2 form, armed by the leader with both CTAs'
 //               bytes); scale loads complete on this CTA's own sf_full barrier.
-//   warp 1      TMEM allocation for the pair; in the leader, the MMA issuer.
+//   warp 1      TMEM allocation for the pair; in the leader, MMA issuer 0.
+//   warp 10     (NVFP4) in the leader, MMA issuer 1.
 //   warps 2..5  epilogue: each CTA drains its own accumulator rows.
 //   warps 6..9  scale stagers.
 // No TMA load uses cluster multicast.  Every wait is bounded (qg_ptx.cuh).
@@ -61,7 +66,12 @@ struct PairCfg {
   static constexpr int kTmemCols = 512;
   static_assert(kTmemSfBase + kStages * kTmemSfStageCols <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
-  static constexpr int kThreads = 320;
+  // NVFP4: two MMA issuers in the leader, each owning one N = 128 half of
+  // the accumulator (a single issuing thread cannot keep the tensor pipe
+  // busy at 4 MMAs per stage).  MXFP8 keeps one issuer at N = 256.
+  static constexpr int kIssuers = kFp4 ? 2 : 1;
+  static constexpr int kIssueN = kBN / kIssuers;
+  static constexpr int kThreads = 320 + 32 * (kIssuers - 1);
 };
 
 __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
@@ -92,13 +102,30 @@ __device__ __forceinline__ void stage_scales(const uint8_t* ssfa, const uint8_t*
     a[4 * c + 1] = v.y;
     a[4 * c + 2] = v.z;
     a[4 * c + 3] = v.w;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint4 w = lds128(ssfb + (c * 2 + h) * 512 + lane * 16);
-      b[8 * c + 4 * h] = w.x;
-      b[8 * c + 4 * h + 1] = w.y;
-      b[8 * c + 4 * h + 2] = w.z;
-      b[8 * c + 4 * h + 3] = w.w;
+    const uint4 w0 = lds128(ssfb + (c * 2) * 512 + lane * 16);
+    const uint4 w1 = lds128(ssfb + (c * 2 + 1) * 512 + lane * 16);
+    if (Cfg::kIssuers == 2) {
+      // Issuer 0's MMA B rows are tile rows 0-63 | 128-191, issuer 1's
+      // 64-127 | 192-255 (each CTA contributes half of an MMA's N): column
+      // r/32 of a 128-row block holds rows 32*col.., so the halves take
+      // columns {0,1} and {2,3} of both blocks.
+      b[8 * c] = w0.x;
+      b[8 * c + 1] = w0.y;
+      b[8 * c + 2] = w1.x;
+      b[8 * c + 3] = w1.y;
+      b[8 * c + 4] = w0.z;
+      b[8 * c + 5] = w0.w;
+      b[8 * c + 6] = w1.z;
+      b[8 * c + 7] = w1.w;
+    } else {
+      b[8 * c] = w0.x;
+      b[8 * c + 1] = w0.y;
+      b[8 * c + 2] = w0.z;
+      b[8 * c + 3] = w0.w;
+      b[8 * c + 4] = w1.x;
+      b[8 * c + 5] = w1.y;
+      b[8 * c + 6] = w1.z;
+      b[8 * c + 7] = w1.w;
     }
   }
   tmem_st_32x32b<Cfg::kSfaCols>(t_quad + sfa_col, a);
@@ -106,7 +133,7 @@ __device__ __forceinline__ void stage_scales(const uint8_t* ssfa, const uint8_t*
 }
 
 template <bool kFp4, bool kOutBf16>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
     gemm_pair_kernel(const __grid_constant__ GemmParams p) {
   using Cfg = PairCfg<kFp4>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -119,8 +146,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
   uint64_t* empty_bar = bars + 3 * Cfg::kStages;    // each CTA
   uint64_t* acc_full = bars + 4 * Cfg::kStages;     // each CTA
   uint64_t* acc_empty = acc_full + 1;               // leader: 8 epilogue warps
-  uint64_t* drain_bar = acc_full + 2;               // leader
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 3);
+  uint64_t* drain_bar = acc_full + 2;               // leader: [kIssuers]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 4);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x / 32;
@@ -135,11 +162,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&sf_full[s], 1);
       mbar_init(&sf_ready[s], 8);
-      mbar_init(&empty_bar[s], 1);
+      mbar_init(&empty_bar[s], Cfg::kIssuers);
     }
-    mbar_init(acc_full, 1);
+    mbar_init(acc_full, Cfg::kIssuers);
     mbar_init(acc_empty, 8);
-    mbar_init(drain_bar, 1);
+    for (int i = 0; i < Cfg::kIssuers; ++i) mbar_init(&drain_bar[i], 1);
     *abort_flag = 0u;
     fence_barrier_init();
     tma_prefetch_desc(&p.tm_a);
@@ -167,13 +194,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       const uint64_t pol = l2_policy_evict_last();
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
+      // Counters stepped incrementally: no division on the per-stage path.
+      int stage = 0, kb = 0, tile = pair;
+      uint32_t phase = 0;
+      int mt = tile % p.num_m_tiles, nt = tile / p.num_m_tiles;
+      const bool skip_loads = (p.diag & 4u) != 0;
       for (int g = 0; g < total_kb; ++g) {
-        const int stage = g % Cfg::kStages;
-        const uint32_t phase = static_cast<uint32_t>((g / Cfg::kStages) & 1);
-        const int tile = pair + (g / nkb) * npairs;
-        const int kb = g % nkb;
-        const int mt = tile % p.num_m_tiles;
-        const int nt = tile / p.num_m_tiles;
+        if (g > 0) {
+          if (++stage == Cfg::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          if (++kb == nkb) {
+            kb = 0;
+            tile += npairs;
+            mt = tile % p.num_m_tiles;
+            nt = tile / p.num_m_tiles;
+          }
+        }
         if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.timeout_ns, abort_flag, p.status,
                                kDevTimeoutProducer)) {
           ok = false;
@@ -183,34 +221,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
         uint8_t* sb = sa + Cfg::kABytes;
         uint8_t* ssfa = sb + Cfg::kBBytes;
         uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
-        const bool cp_mode = (p.diag & 16u) != 0 || (p.diag & 64u) != 0;
-        if (p.diag & 4u) {
-          if (leader) mbar_arrive(&full_bar[stage]);
-          if (!cp_mode) mbar_arrive(&sf_full[stage]);
-          continue;
-        }
-        if (cp_mode) {
-          // Scales through tcgen05.cp issued by the MMA thread: all bytes on
-          // the leader's full barrier.
-          const uint32_t fl = mapa_shared(smem_u32(&full_bar[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * (Cfg::kAbTx + Cfg::kSfTx));
-          tma_load_3d_pair(ssfa, &p.tm_sfa, fl, 0, mt * 2 + static_cast<int>(rank),
-                           kb * Cfg::kSfChunks, pol);
-          tma_load_3d_pair(ssfb, &p.tm_sfb, fl, 0, nt * 2, kb * Cfg::kSfChunks, pol);
-          tma_load_2d_pair(sa, &p.tm_a, fl, kb * Cfg::kBKBytes,
-                           mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM, pol);
-          tma_load_2d_pair(sb, &p.tm_b, fl, kb * Cfg::kBKBytes,
-                           nt * Cfg::kBN + static_cast<int>(rank) * Cfg::kBNHalf, pol);
+        if (skip_loads) {
+          mbar_arrive(leader ? &full_bar[stage] : &sf_full[stage]);
           continue;
         }
         const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
-        if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::kAbTx);
-        mbar_arrive_expect_tx(&sf_full[stage], Cfg::kSfTx);
-        // Scales first: they are small, land early, and the stagers move them
-        // into TMEM while A and B are still arriving.
-        tma_load_3d(ssfa, &p.tm_sfa, &sf_full[stage], 0, mt * 2 + static_cast<int>(rank),
+        // The leader's scales complete on its full barrier with both CTAs'
+        // A/B bytes (its stagers then wait once per stage, and their arrival
+        // on sf_ready also tells the issuers that A/B have landed); the
+        // peer's scales complete on its own sf_full.  Scales go first: they
+        // are small and land early.
+        uint64_t* sf_bar = leader ? &full_bar[stage] : &sf_full[stage];
+        if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::kAbTx + Cfg::kSfTx);
+        else mbar_arrive_expect_tx(&sf_full[stage], Cfg::kSfTx);
+        tma_load_3d(ssfa, &p.tm_sfa, sf_bar, 0, mt * 2 + static_cast<int>(rank),
                     kb * Cfg::kSfChunks, pol);
-        tma_load_3d(ssfb, &p.tm_sfb, &sf_full[stage], 0, nt * 2, kb * Cfg::kSfChunks, pol);
+        tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol);
         tma_load_2d_pair(sa, &p.tm_a, full_leader, kb * Cfg::kBKBytes,
                          mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM, pol);
         tma_load_2d_pair(sb, &p.tm_b, full_leader, kb * Cfg::kBKBytes,
@@ -225,23 +251,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
         uint32_t dummy = 0;
         for (int s = 0; s < Cfg::kStages; ++s) {
           if (!(issued_mask & (1u << s))) continue;
-          mbar_wait_bounded(&sf_full[s], (issued_parity >> s) & 1u, p.timeout_ns, &dummy,
-                            nullptr, 0);
-          if (leader)
-            mbar_wait_bounded(&full_bar[s], (issued_parity >> s) & 1u, p.timeout_ns, &dummy,
-                              nullptr, 0);
+          mbar_wait_bounded(leader ? &full_bar[s] : &sf_full[s], (issued_parity >> s) & 1u,
+                            p.timeout_ns, &dummy, nullptr, 0);
         }
         if (!leader) spin_ns(200000);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 10) {
     // ---------------------------------------------------------------- MMA
-    if (leader && lane == 0) {
+    // Issuer h (warp 1: h = 0, warp 10: h = 1) accumulates output columns of
+    // its N half into TMEM columns [h * kIssueN, (h + 1) * kIssueN).  The
+    // issue loop is the pipeline's serial path (one thread per issuer):
+    // stage, phase, descriptors and scale columns are stepped by constants
+    // and the diagnostic switches are read once.
+    const int h = warp == 1 ? 0 : 1;
+    if (leader && lane == 0 && h < Cfg::kIssuers) {
       const uint32_t idesc_base =
-          kFp4 ? make_idesc_block_scaled(2 * Cfg::kBM, Cfg::kBN, 1u, 0u, 0u, 0u)
-               : make_idesc_block_scaled(2 * Cfg::kBM, Cfg::kBN, 0u, 1u, 0u, 0u);
+          kFp4 ? make_idesc_block_scaled(2 * Cfg::kBM, Cfg::kIssueN, 1u, 0u, 0u, 0u)
+               : make_idesc_block_scaled(2 * Cfg::kBM, Cfg::kIssueN, 0u, 1u, 0u, 0u);
+      const bool skip_mma = (p.diag & 2u) != 0;
+      // B rows [h * kIssueN / 2, +kIssueN / 2) of each CTA's 128-row half.
+      const uint64_t adesc0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
+      const uint64_t bdesc0 =
+          adesc0 + ((Cfg::kABytes + h * (Cfg::kIssueN / 2) * Cfg::kBKBytes) >> 4);
+      constexpr uint64_t kStageDesc = Cfg::kStageBytes >> 4;
+      const uint32_t sf0 = tmem_base + Cfg::kTmemSfBase;
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(h * Cfg::kIssueN);
       bool ok = true;
-      int g = 0;
+      int stage = 0;
+      uint32_t phase = 0;
+      uint64_t adesc = adesc0, bdesc = bdesc0;
+      uint32_t sfa_col = sf0;
       for (int it = 0; it < my_tiles && ok; ++it) {
         if (!mbar_wait_bounded(acc_empty, (it & 1) ^ 1u, p.timeout_ns, abort_flag, p.status,
                                kDevTimeoutMma)) {
@@ -249,91 +289,91 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        for (int kb = 0; kb < nkb; ++kb, ++g) {
-          const int stage = g % Cfg::kStages;
-          const uint32_t phase = static_cast<uint32_t>((g / Cfg::kStages) & 1);
-          const bool cp_mode = (p.diag & 16u) != 0;
-          if (!mbar_wait_bounded(&full_bar[stage], phase, p.timeout_ns, abort_flag, p.status,
-                                 kDevTimeoutMma) ||
-              (!cp_mode && !mbar_wait_bounded(&sf_ready[stage], phase, p.timeout_ns, abort_flag,
-                                              p.status, kDevTimeoutMma))) {
+        uint32_t acc = 0;
+        for (int kb = 0; kb < nkb; ++kb) {
+          // sf_ready covers the A/B bytes too: the leader's stagers arrive
+          // only after full_bar.
+          if (!mbar_wait_bounded(&sf_ready[stage], phase, p.timeout_ns, abort_flag, p.status,
+                                 kDevTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          uint8_t* sa = smem + stage * Cfg::kStageBytes;
-          uint8_t* sb = sa + Cfg::kABytes;
-          const uint32_t sfa_col = tmem_base + Cfg::kTmemSfBase + stage * Cfg::kTmemSfStageCols;
           const uint32_t sfb_col = sfa_col + Cfg::kSfaCols;
-          if (cp_mode && !(p.diag & 1u)) {
-            uint8_t* ssfa = sb + Cfg::kBBytes;
-            uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
-#pragma unroll
-            for (int c = 0; c < Cfg::kSfChunks; ++c) {
-              tmem_cp_pair_32x128b_warpx4(
-                  sfa_col + c * 4, make_smem_desc(smem_u32(ssfa + c * 512), 0, 128, kSwizzleNone));
-#pragma unroll
-              for (int h = 0; h < 2; ++h)
-                tmem_cp_pair_32x128b_warpx4(
-                    sfb_col + c * 8 + h * 4,
-                    make_smem_desc(smem_u32(ssfb + (c * 2 + h) * 512), 0, 128, kSwizzleNone));
-            }
-          }
-          const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, kSwizzle128B);
-          const uint64_t bdesc = make_smem_desc(smem_u32(sb), 16, 1024, kSwizzle128B);
-          if (!(p.diag & 2u)) {
+          if (!skip_mma) {
 #pragma unroll
             for (int j = 0; j < Cfg::kMmaPerStage; ++j) {
               const uint64_t koff = static_cast<uint64_t>(j * 2);  // +32 B of K
-              const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
               if (kFp4) {
-                mma_pair_mxf4nvf4(tmem_base, adesc + koff, bdesc + koff, idesc_base,
-                                  sfa_col + j * 4, sfb_col + j * 8, acc);
+                mma_pair_mxf4nvf4(d_tmem, adesc + koff, bdesc + koff, idesc_base,
+                                  sfa_col + j * 4, sfb_col + j * 8 + h * 4, acc);
               } else {
                 const uint32_t idesc = idesc_base | (static_cast<uint32_t>(j) << 29) |
                                        (static_cast<uint32_t>(j) << 4);
-                mma_pair_mxf8f6f4(tmem_base, adesc + koff, bdesc + koff, idesc, sfa_col,
+                mma_pair_mxf8f6f4(d_tmem, adesc + koff, bdesc + koff, idesc, sfa_col,
                                   sfb_col, acc);
               }
+              acc = 1;
             }
           }
           tc_commit_pair(&empty_bar[stage], 0x3);
+          if (++stage == Cfg::kStages) {
+            stage = 0;
+            phase ^= 1u;
+            adesc = adesc0;
+            bdesc = bdesc0;
+            sfa_col = sf0;
+          } else {
+            adesc += kStageDesc;
+            bdesc += kStageDesc;
+            sfa_col += Cfg::kTmemSfStageCols;
+          }
         }
         if (ok) tc_commit_pair(acc_full, 0x3);
       }
-      tc_commit_pair(drain_bar, 0x1);
+      tc_commit_pair(&drain_bar[h], 0x1);
       uint32_t dummy = 0;
-      mbar_wait_bounded(drain_bar, 0, p.timeout_ns, &dummy, nullptr, 0);
+      mbar_wait_bounded(&drain_bar[h], 0, p.timeout_ns, &dummy, nullptr, 0);
     }
   } else if (warp >= 6) {
     // ---------------------------------------------------------------- scale stagers
     const int quad = warp % 4;
-    const int stager_kb = (p.diag & 16u) ? 0 : total_kb;  // diag 64: stage, loads as cp mode
+    const int stager_kb = total_kb;
     const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    const bool no_wait = (p.diag & 32u) != 0, skip_st = (p.diag & 1u) != 0;
+    int stage = 0;
+    uint32_t phase = 0;
     for (int g = 0; g < stager_kb; ++g) {
-      const int stage = g % Cfg::kStages;
-      const uint32_t phase = static_cast<uint32_t>((g / Cfg::kStages) & 1);
-      // One lane polls the barrier; the warp follows it.
-      bool ok = true;
-      if (lane == 0 && !(p.diag & 32u))
-        ok = mbar_wait_bounded(&sf_full[stage], phase, p.timeout_ns, abort_flag, p.status,
-                               kDevTimeoutMma);
-      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-      if (!(p.diag & 32u)) mbar_try_wait(&sf_full[stage], phase);  // acquire for every lane
+      if (g > 0 && ++stage == Cfg::kStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+      // Every lane polls (and so acquires) the stage barrier itself: one
+      // wait per stage on the stager's serial path.  Leader: the full
+      // barrier (its scales and both CTAs' A/B); peer: its sf_full.
+      bool ok = no_wait || mbar_wait_bounded(leader ? &full_bar[stage] : &sf_full[stage], phase,
+                                             p.timeout_ns, abort_flag, p.status, kDevTimeoutMma);
+      if (!__all_sync(0xffffffffu, ok)) break;
       const uint8_t* ssfa = smem + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
       const uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
       const uint32_t sfa_col = Cfg::kTmemSfBase + stage * Cfg::kTmemSfStageCols;
-      if (!(p.diag & 1u)) {
+      if (!skip_st) {
         stage_scales<kFp4>(ssfa, ssfb, t_quad, sfa_col, sfa_col + Cfg::kSfaCols, lane);
         tmem_wait_st();
       }
       tc_fence_before();
       __syncwarp();
-      // A release-scoped arrive at cluster scope costs ~1 us here and serialises
-      // the stagers (measured: 2.2 vs 4.1 PF/s).  The relaxed arrive is
-      // enough: tcgen05.wait::st has already completed the TMEM writes and
-      // tcgen05.fence::before_thread_sync orders them before the arrive.
-      if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&sf_ready[stage]), 0));
+      if (leader) {
+        // The stage's A/B bytes are in (the full barrier was the wait), so
+        // sf_ready alone tells the MMA issuers the stage is complete.
+        if (lane == 0) mbar_arrive(&sf_ready[stage]);
+      } else if (lane == 0) {
+        // A release-scoped arrive at cluster scope costs ~1 us here and
+        // serialises the stagers (measured: 2.2 vs 4.1 PF/s).  The relaxed
+        // arrive is enough: tcgen05.wait::st has already completed the TMEM
+        // writes and tcgen05.fence::before_thread_sync orders them before it.
+        mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&sf_ready[stage]), 0));
+      }
     }
   } else {
     // ---------------------------------------------------------------- epilogue
@@ -343,6 +383,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     if (p.a_ts) alpha *= *p.a_ts;
     if (p.b_ts) alpha *= *p.b_ts;
     const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    // 64-column blocks: with two issuers TMEM block 1 holds output block 2
+    // and block 2 output block 1 (issuer h's MMA N rows are h*64.. of each
+    // CTA's half); the map is its own inverse.
+    auto tmem_block = [](int b) { return Cfg::kIssuers == 2 && (b == 1 || b == 2) ? 3 - b : b; };
     for (int it = 0; it < my_tiles; ++it) {
       const int tile = pair + it * npairs;
       const int mt = tile % p.num_m_tiles;
@@ -378,9 +422,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
           uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.c) +
                                                 row * p.ldc + n0);
 #pragma unroll
-          for (int v = 0; v < Cfg::kBN / 8; ++v)
-            dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2],
-                                packed[4 * v + 3]);
+          for (int v = 0; v < Cfg::kBN / 8; ++v) {
+            const int pv = 4 * (tmem_block(v / 8) * 8 + v % 8);
+            dst[v] = make_uint4(packed[pv], packed[pv + 1], packed[pv + 2], packed[pv + 3]);
+          }
         }
       } else {
         // fp32 output or a ragged tile: 32 columns at a time, accumulator
@@ -396,7 +441,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
           }
-          const int col0 = n0 + cc * 32;
+          const int col0 = n0 + tmem_block(cc / 2) * 64 + (cc % 2) * 32;
           if (row_ok && col0 < p.n) {
             const bool vec = p.vec_ok && col0 + 32 <= p.n;
             if (kOutBf16) {
