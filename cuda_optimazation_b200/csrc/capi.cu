@@ -166,6 +166,18 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
   p.num_n_tiles = static_cast<int>((n + tn - 1) / tn);
   p.num_k_blocks = static_cast<int>((row_bytes + gemm_stage_k_bytes() - 1) / gemm_stage_k_bytes());
   p.vec_ok = aligned16(c) && ((ldc * esize) % 16 == 0);
+  if (pair && esize == 2 && p.vec_ok) {
+    // C through TMA stores: 64-column x 32-row boxes (one epilogue warp's
+    // rows), 128-byte swizzle matching the staging layout in shared memory.
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldc * 2)};
+    const cuuint32_t box[2] = {64u, 32u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    p.tma_c = encode_fn()(&p.tm_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c, dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
   p.a_ts = fp4 ? a_ts : nullptr;
   p.b_ts = fp4 ? b_ts : nullptr;
   p.status = status;

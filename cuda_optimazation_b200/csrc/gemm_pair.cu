@@ -58,7 +58,10 @@ struct PairCfg {
   static constexpr int kAbTx = kABytes + kBBytes;
   static constexpr int kSfTx = kSfaBytes + kSfbBytes;
   static constexpr int kStageBytes = (kAbTx + kSfTx + 1023) / 1024 * 1024;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 512 + 1024;
+  // NVFP4 with bf16 C: per epilogue warp two 64-column x 32-row staging
+  // boxes (SWIZZLE_128B) for TMA stores of the output.
+  static constexpr int kEpiBytes = kFp4 ? 4 * 2 * 4096 : 0;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 512 + 1024;
   static constexpr int kSfaCols = kSfChunks * 4;
   static constexpr int kSfbCols = kSfChunks * 8;
   static constexpr int kTmemSfBase = kBN;
@@ -139,15 +142,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStageBytes);
+  uint8_t* epi_smem = smem + Cfg::kStages * Cfg::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + Cfg::kEpiBytes);
   uint64_t* full_bar = bars;                        // leader: A/B bytes of both CTAs
   uint64_t* sf_full = bars + Cfg::kStages;          // each CTA: its scale bytes
   uint64_t* sf_ready = bars + 2 * Cfg::kStages;     // leader: 8 stager warps
   uint64_t* empty_bar = bars + 3 * Cfg::kStages;    // each CTA
   uint64_t* acc_full = bars + 4 * Cfg::kStages;     // each CTA
-  uint64_t* acc_empty = acc_full + 1;               // leader: 8 epilogue warps
-  uint64_t* drain_bar = acc_full + 2;               // leader: [kIssuers]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 4);
+  uint64_t* acc_empty = acc_full + 1;               // leader: [kIssuers], 8 epilogue warps
+  uint64_t* drain_bar = acc_full + 3;               // leader: [kIssuers]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 5);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x / 32;
@@ -165,7 +169,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
       mbar_init(&empty_bar[s], Cfg::kIssuers);
     }
     mbar_init(acc_full, Cfg::kIssuers);
-    mbar_init(acc_empty, 8);
+    for (int i = 0; i < Cfg::kIssuers; ++i) mbar_init(&acc_empty[i], 8);
     for (int i = 0; i < Cfg::kIssuers; ++i) mbar_init(&drain_bar[i], 1);
     *abort_flag = 0u;
     fence_barrier_init();
@@ -283,7 +287,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
       uint64_t adesc = adesc0, bdesc = bdesc0;
       uint32_t sfa_col = sf0;
       for (int it = 0; it < my_tiles && ok; ++it) {
-        if (!mbar_wait_bounded(acc_empty, (it & 1) ^ 1u, p.timeout_ns, abort_flag, p.status,
+        if (!mbar_wait_bounded(&acc_empty[h], (it & 1) ^ 1u, p.timeout_ns, abort_flag, p.status,
                                kDevTimeoutMma)) {
           ok = false;
           break;
@@ -378,7 +382,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
   } else {
     // ---------------------------------------------------------------- epilogue
     const int quad = warp % 4;
-    const uint32_t acc_empty_leader = mapa_shared(smem_u32(acc_empty), 0);
+    // acc_empty[h] (leader) is released as soon as this warp has read issuer
+    // h's TMEM columns, so issuer 0 starts the next tile while the second
+    // half is still being read.  Relaxed remote arrive: tcgen05.wait::ld has
+    // completed the reads and fence::before_thread_sync orders them first.
+    const uint32_t acc_empty_leader0 = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    const uint32_t acc_empty_leader1 = mapa_shared(smem_u32(&acc_empty[Cfg::kIssuers - 1]), 0);
     float alpha = 1.0f;
     if (p.a_ts) alpha *= *p.a_ts;
     if (p.b_ts) alpha *= *p.b_ts;
@@ -393,31 +402,81 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
       const int nt = tile / p.num_m_tiles;
       bool ok = true;
       if (lane == 0)
-        ok = mbar_wait_bounded<false, 256>(acc_full, it & 1, p.timeout_ns, abort_flag, p.status,
-                               kDevTimeoutEpilogue);
+        ok = mbar_wait_bounded<false, 32>(acc_full, it & 1, p.timeout_ns, abort_flag, p.status,
+                                          kDevTimeoutEpilogue);
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
       mbar_try_wait(acc_full, it & 1);
       tc_fence_after();
       const int row = mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM + quad * 32 + lane;
       const bool row_ok = row < p.m && !(p.diag & 8u);
       const int n0 = nt * Cfg::kBN;
-      if (kOutBf16 && p.vec_ok && n0 + Cfg::kBN <= p.n) {
+      if (Cfg::kEpiBytes > 0 && kOutBf16 && p.tma_c) {
+        // TMEM -> registers -> bf16 in a swizzled shared-memory box -> TMA
+        // store (coalesced, asynchronous, clipped at the matrix edge).  One
+        // 64-column TMEM block per box; two boxes alternate.
+        const int row0 = mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM + quad * 32;
+        uint8_t* ebuf = epi_smem + quad * 8192;
+#pragma unroll
+        for (int q = 0; q < Cfg::kBN / 64; ++q) {
+          uint8_t* box = ebuf + (q & 1) * 4096;
+          if ((q & 1) == 0) {
+            if (lane == 0) tma_store_wait_read<0>();  // both boxes read by earlier stores
+            __syncwarp();
+          }
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(t_row + q * 64, r0);
+          tmem_ld_32x32b_x32(t_row + q * 64 + 32, r1);
+          tmem_wait_ld();
+          if ((Cfg::kIssuers == 2 && q == Cfg::kBN / 128 - 1) || q == Cfg::kBN / 64 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+              mbar_arrive_cluster_relaxed(q == Cfg::kBN / 64 - 1 ? acc_empty_leader1
+                                                                 : acc_empty_leader0);
+          }
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t* src = c < 4 ? r0 + c * 8 : r1 + (c - 4) * 8;
+            const uint4 v = make_uint4(
+                bf16x2_bits(__uint_as_float(src[0]) * alpha, __uint_as_float(src[1]) * alpha),
+                bf16x2_bits(__uint_as_float(src[2]) * alpha, __uint_as_float(src[3]) * alpha),
+                bf16x2_bits(__uint_as_float(src[4]) * alpha, __uint_as_float(src[5]) * alpha),
+                bf16x2_bits(__uint_as_float(src[6]) * alpha, __uint_as_float(src[7]) * alpha));
+            *reinterpret_cast<uint4*>(box + lane * 128 + ((c ^ (lane & 7)) * 16)) = v;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && !(p.diag & 8u)) {
+            tma_store_2d(&p.tm_c, box, n0 + tmem_block(q) * 64, row0);
+            tma_store_commit();
+          }
+        }
+      } else if (kOutBf16 && p.vec_ok && n0 + Cfg::kBN <= p.n) {
         // Full tile: the whole accumulator row goes to registers as bf16,
         // the accumulator is handed back, then 16-byte stores.
         uint32_t packed[Cfg::kBN / 2];
 #pragma unroll
-        for (int cc = 0; cc < Cfg::kBN / 16; ++cc) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(t_row + cc * 16, r);
+        for (int cc = 0; cc < Cfg::kBN / 32; ++cc) {
+          // Two 16-column loads in flight per wait.
+          uint32_t r0[16], r1[16];
+          tmem_ld_32x32b_x16(t_row + cc * 32, r0);
+          tmem_ld_32x32b_x16(t_row + cc * 32 + 16, r1);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            packed[cc * 8 + j] = bf16x2_bits(__uint_as_float(r[2 * j]) * alpha,
-                                             __uint_as_float(r[2 * j + 1]) * alpha);
+          for (int j = 0; j < 8; ++j) {
+            packed[cc * 16 + j] = bf16x2_bits(__uint_as_float(r0[2 * j]) * alpha,
+                                              __uint_as_float(r0[2 * j + 1]) * alpha);
+            packed[cc * 16 + 8 + j] = bf16x2_bits(__uint_as_float(r1[2 * j]) * alpha,
+                                                  __uint_as_float(r1[2 * j + 1]) * alpha);
+          }
+          if ((Cfg::kIssuers == 2 && cc == Cfg::kBN / 64 - 1) || cc == Cfg::kBN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+              mbar_arrive_cluster_relaxed(cc == Cfg::kBN / 32 - 1 ? acc_empty_leader1
+                                                                  : acc_empty_leader0);
+          }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
         if (row_ok) {
           uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.c) +
                                                 row * p.ldc + n0);
@@ -436,10 +495,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
           __syncwarp();
           tmem_ld_32x32b_x32(t_row + cc * 32, r);
           tmem_wait_ld();
-          if (cc == Cfg::kBN / 32 - 1) {
+          if ((Cfg::kIssuers == 2 && cc == Cfg::kBN / 64 - 1) || cc == Cfg::kBN / 32 - 1) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
+            if (lane == 0)
+              mbar_arrive_cluster_relaxed(cc == Cfg::kBN / 32 - 1 ? acc_empty_leader1
+                                                                  : acc_empty_leader0);
           }
           const int col0 = n0 + tmem_block(cc / 2) * 64 + (cc % 2) * 32;
           if (row_ok && col0 < p.n) {
@@ -486,6 +547,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
     }
   }
 
+  if (Cfg::kEpiBytes > 0 && warp >= 2 && warp <= 5 && (threadIdx.x % 32) == 0)
+    tma_store_wait_all<0>();  // output stores done before shared memory is released
   tc_fence_before();
   cluster_sync();  // the leader's MMAs into both TMEMs are drained
   if (warp == 1) {

@@ -12,6 +12,8 @@ struct GemmParams {
   CUtensorMap tm_b;    // uint8 [rows][K bytes], box 128 B x kBN, SWIZZLE_128B
   CUtensorMap tm_sfa;  // uint32 [scale_blocks][row_blocks][128], box (128, kBM/128, chunks)
   CUtensorMap tm_sfb;
+  CUtensorMap tm_c;    // bf16 C, box 64 x 32, SWIZZLE_128B (valid when tma_c)
+  int tma_c;           // pair kernel may store C through TMA
   void* c;
   int64_t ldc;  // elements
   int m, n, k;
