@@ -72,7 +72,10 @@ def profile_traffic(kernel_tag: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples while the GPU is loaded."""
+    """SM clock, power and clock-event (throttle) reasons sampled while the
+    timed region runs: NVML polled every 5 ms from a thread (nvidia-smi
+    needs ~1 s to start, longer than a short timed region); nvidia-smi -lms
+    when NVML cannot be loaded.  Reads only; changes no GPU setting."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -82,8 +85,28 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines: list[str] = []
+        self.nvml = None
+        self.handle = None
+        self.stop = threading.Event()
+        self.thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            try:
+                props = torch.cuda.get_device_properties(index)
+                bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+        except Exception:
+            self.nvml = None
 
     def __enter__(self):
+        if self.nvml is not None:
+            self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+            self.thread.start()
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -95,11 +118,34 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _poll_nvml(self):
+        nv, h = self.nvml, self.handle
+        bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+        try:
+            smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        except Exception:
+            smax = 0
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                flags = ["Active" if rs & b else "Not Active" for b in bits]
+                self.lines.append(", ".join([str(self.index), str(sm), str(smax), f"{pw:.1f}",
+                                             hex(rs)] + flags))
+            except Exception:
+                break
+            self.stop.wait(0.005)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.thread is not None and self.nvml is not None:
+            self.thread.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
