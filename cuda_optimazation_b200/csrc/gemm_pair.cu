@@ -10,7 +10,7 @@
 // loads its own 128 rows of A and its own 128-row half of B; the leader CTA
 // (rank 0) issues tcgen05.mma.cta_group::2, which reads A and B from both
 // CTAs' shared memory and accumulates rows [0,128) in the leader's TMEM and
-// rows [128,256) in the peer's.  For NVFP4 two leader threads (warps 1 and
+// rows [128,256) in the peer's.  Two leader threads (warps 1 and
 // 10) issue M = 256, N = 128 MMAs into the two halves of the accumulator:
 // measured, one issuing thread spends ~56 ns per MMA plus ~150 ns per stage
 // on waits and commits, more than the 4 x 69 ns the tensor pipe needs for a
@@ -24,12 +24,13 @@
 // memory and write the layout the MMA reads (row r at lane r%32 of every
 // quadrant, column r/32, byte = scale index) for their own quadrant.
 //
-// Roles (both CTAs, 10 warps, 11 for NVFP4):
+// Roles (both CTAs, 11 warps):
 //   warp 0      TMA producer.  A/B loads complete on the LEADER's full barrier
 //               (cta_group::2 form, armed by the leader with both CTAs'
-//               bytes); scale loads complete on this CTA's own sf_full barrier.
+//               bytes and its own scale bytes); the peer's scale loads
+//               complete on its own sf_full barrier.
 //   warp 1      TMEM allocation for the pair; in the leader, MMA issuer 0.
-//   warp 10     (NVFP4) in the leader, MMA issuer 1.
+//   warp 10     in the leader, MMA issuer 1.
 //   warps 2..5  epilogue: each CTA drains its own accumulator rows.
 //   warps 6..9  scale stagers.
 // No TMA load uses cluster multicast.  Every wait is bounded (qg_ptx.cuh).
@@ -48,7 +49,7 @@ struct PairCfg {
   static constexpr int kBN = 256;       // N of the pair tile
   static constexpr int kBNHalf = 128;   // rows of B each CTA loads
   static constexpr int kBKBytes = 128;  // K bytes per stage (one SWIZZLE_128B row)
-  static constexpr int kStages = kFp4 ? 5 : 6;
+  static constexpr int kStages = 5;
   static constexpr int kMmaPerStage = 4;
   static constexpr int kSfChunks = kFp4 ? 4 : 1;  // 512-B chunks along K per 128 rows
   static constexpr int kABytes = kBM * kBKBytes;
@@ -58,9 +59,9 @@ struct PairCfg {
   static constexpr int kAbTx = kABytes + kBBytes;
   static constexpr int kSfTx = kSfaBytes + kSfbBytes;
   static constexpr int kStageBytes = (kAbTx + kSfTx + 1023) / 1024 * 1024;
-  // NVFP4 with bf16 C: per epilogue warp two 64-column x 32-row staging
-  // boxes (SWIZZLE_128B) for TMA stores of the output.
-  static constexpr int kEpiBytes = kFp4 ? 4 * 2 * 4096 : 0;
+  // bf16 C: per epilogue warp two 64-column x 32-row staging boxes
+  // (SWIZZLE_128B) for TMA stores of the output.
+  static constexpr int kEpiBytes = 4 * 2 * 4096;
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 512 + 1024;
   static constexpr int kSfaCols = kSfChunks * 4;
   static constexpr int kSfbCols = kSfChunks * 8;
@@ -69,10 +70,10 @@ struct PairCfg {
   static constexpr int kTmemCols = 512;
   static_assert(kTmemSfBase + kStages * kTmemSfStageCols <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
-  // NVFP4: two MMA issuers in the leader, each owning one N = 128 half of
-  // the accumulator (a single issuing thread cannot keep the tensor pipe
-  // busy at 4 MMAs per stage).  MXFP8 keeps one issuer at N = 256.
-  static constexpr int kIssuers = kFp4 ? 2 : 1;
+  // Two MMA issuers in the leader, each owning one N = 128 half of the
+  // accumulator (a single issuing thread cannot keep the tensor pipe busy
+  // at 4 MMAs per stage).
+  static constexpr int kIssuers = 2;
   static constexpr int kIssueN = kBN / kIssuers;
   static constexpr int kThreads = 320 + 32 * (kIssuers - 1);
 };
@@ -315,7 +316,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
                 const uint32_t idesc = idesc_base | (static_cast<uint32_t>(j) << 29) |
                                        (static_cast<uint32_t>(j) << 4);
                 mma_pair_mxf8f6f4(d_tmem, adesc + koff, bdesc + koff, idesc, sfa_col,
-                                  sfb_col, acc);
+                                  sfb_col + h * 4, acc);
               }
               acc = 1;
             }
