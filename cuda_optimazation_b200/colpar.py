@@ -9,7 +9,11 @@ B200s.  The scheme:
 * A (quantised once) is broadcast from rank 0 with NCCL;
 * every rank runs its local GEMM with no communication;
 * optionally the bf16 output shards are all-gathered over NVLink and laid out
-  as the full M x N matrix.
+  as the full M x N matrix: either with NCCL after the GEMM
+  (``gather_columns``) or fused into the GEMM, whose epilogue stores every
+  output tile into every rank's full C over peer memory
+  (``GatherBuffers`` + ``colpar_gemm(..., fused=...)``), so the transfer
+  overlaps the math.
 
 Shards are multiples of ``align`` rows (256, the CTA-pair tile) so every rank
 runs full tiles; the last rank takes the remainder.  ``local_gemm`` is
@@ -82,3 +86,66 @@ def colpar_gemm(a, b_local, n_total: int, local_gemm: Optional[Callable] = None,
     if not gather or dist.get_world_size(group) == 1:
         return c_local
     return gather_columns(c_local, n_total, group=group)
+
+
+def shard_rows(op, lo: int, hi: int):
+    """Rows [lo, hi) of a quantised NVFP4 operand (values, scales, shared
+    tensor scale) as views.  Scales must use the K-major chunk layout
+    (LAYOUT_MMA_KMAJOR), where a run of whole 128-row blocks is contiguous;
+    lo and hi are multiples of 128."""
+    from .qgemm import LAYOUT_MMA_KMAJOR, Nvfp4Result
+    if op.layout != LAYOUT_MMA_KMAJOR:
+        raise ValueError("row shards need the K-major scale layout")
+    if lo % 128 or (hi % 128 and hi != op.rows):
+        raise ValueError("shard bounds must be 128-row aligned")
+    row_bytes = op.k // 2
+    chunk_row = ((op.k // 16 + 3) // 4) * 512  # bytes of one 128-row block's scales
+    q = op.quantized[lo * row_bytes: hi * row_bytes]
+    sf = op.block_scales[(lo // 128) * chunk_row: ((hi + 127) // 128) * chunk_row]
+    return Nvfp4Result(q, sf, op.tensor_scale, hi - lo, op.k, op.layout)
+
+
+class GatherBuffers:
+    """Per-rank full bf16 C [m, n_total] plus the peers' buffers mapped into
+    this process with CUDA IPC (handles exchanged over the process group).
+    ``ptrs`` lists every rank's buffer in rank order (this rank's own
+    included) for ``qgemm.gemm_nvfp4_gather``."""
+
+    def __init__(self, m: int, n_total: int, device, group=None):
+        from . import qgemm as q
+        self.q = q
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > q.MAX_RANKS:
+            raise ValueError("at most 8 ranks")
+        self.c = torch.empty(m, n_total, dtype=torch.bfloat16, device=device)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, q.ipc_export(self.c), group=group)
+        self.ptrs = []
+        self._mapped = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.ptrs.append(self.c.data_ptr())
+            else:
+                p = q.ipc_import(h)
+                self._mapped.append(p)
+                self.ptrs.append(p)
+        dist.barrier(group=group)
+
+    def close(self):
+        for p in self._mapped:
+            self.q.ipc_close(p)
+        self._mapped = []
+
+
+def colpar_gemm_fused(a, b_local, n_total: int, bufs: "GatherBuffers", group=None,
+                      status=None) -> torch.Tensor:
+    """Column-parallel GEMM with the all-gather fused into the epilogue:
+    this rank's columns go straight into every rank's ``bufs.c``.  Returns
+    this rank's full C once every rank's kernel has finished (device
+    synchronise + barrier)."""
+    lo, _ = shard_range(n_total, dist.get_world_size(group), dist.get_rank(group))
+    bufs.q.gemm_nvfp4_gather(a, b_local, bufs.ptrs, lo, n_total, status=status)
+    torch.cuda.synchronize()
+    dist.barrier(group=group)
+    return bufs.c

@@ -11,6 +11,7 @@
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 
 #include "../../include/qgemm.h"
@@ -88,6 +89,19 @@ bool make_scale_map(CUtensorMap* m, const void* base, int64_t mn, int64_t k, int
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// bf16 output [rows][cols] with row stride ldc elements, as 64-column x
+// 32-row TMA store boxes with the 128-byte swizzle of the staging buffer.
+bool make_output_map(CUtensorMap* map, void* base, int64_t rows, int64_t cols, int64_t ldc) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldc * 2)};
+  const cuuint32_t box[2] = {64u, 32u};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 uint64_t default_timeout_ns() {
   static uint64_t t = [] {
     const char* e = std::getenv("QG_WAIT_TIMEOUT_NS");
@@ -129,9 +143,20 @@ int gemm_variant(bool fp4, int64_t m) {
   return fp4 ? 0 : 2;
 }
 
+// `gather` (fused column-parallel output gather): this GPU computes the
+// columns [col0, col0 + n) of a C with row stride ldc and stores them into
+// every buffer of c_ranks (nranks of them, peer buffers IPC-mapped); only the
+// pair kernel with bf16 output does this.
+struct Gather {
+  void* const* c_ranks = nullptr;
+  int nranks = 0;
+  int64_t col0 = 0;
+};
+
 int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
                 const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
-                int64_t k, int64_t ldc, int sf_layout, uint32_t* status, cudaStream_t stream) {
+                int64_t k, int64_t ldc, int sf_layout, uint32_t* status, cudaStream_t stream,
+                const Gather& gather = Gather()) {
   if (!a_q || !a_sf || !b_q || !b_sf || !c) return QG_ERR_ARG;
   if (c_dtype != QG_DTYPE_F32 && c_dtype != QG_DTYPE_BF16) return QG_ERR_DTYPE;
   if (sf_layout != QG_LAYOUT_MMA && sf_layout != QG_LAYOUT_MMA_KMAJOR) return QG_ERR_LAYOUT;
@@ -144,7 +169,7 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
   if (int d = check_device()) return d;
   if (!encode_fn()) return QG_ERR_CUDA;
   const int sv = fp4 ? 16 : 32;
-  const int variant = gemm_variant(fp4, m);
+  const int variant = gather.nranks > 0 ? 1 : gemm_variant(fp4, m);
   const bool pair = variant == 1;
   // Tile of one scheduling unit (a CTA pair: 256 x 256; one CTA: 128 x 256)
   // and the rows each CTA's TMA boxes cover.
@@ -169,17 +194,17 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
   p.num_n_tiles = static_cast<int>((n + tn - 1) / tn);
   p.num_k_blocks = static_cast<int>((row_bytes + gemm_stage_k_bytes() - 1) / gemm_stage_k_bytes());
   p.vec_ok = aligned16(c) && ((ldc * esize) % 16 == 0);
-  if (pair && esize == 2 && p.vec_ok) {
-    // C through TMA stores: 64-column x 32-row boxes (one epilogue warp's
-    // rows), 128-byte swizzle matching the staging layout in shared memory.
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldc * 2)};
-    const cuuint32_t box[2] = {64u, 32u};
-    const cuuint32_t estr[2] = {1u, 1u};
-    p.tma_c = encode_fn()(&p.tm_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c, dims, strides, box,
-                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  if (gather.nranks > 0) {
+    if (esize != 2 || !p.vec_ok || (gather.col0 % 8) != 0) return QG_ERR_ALIGN;
+    for (int r = 0; r < gather.nranks; ++r) {
+      if (!gather.c_ranks[r] || !aligned16(gather.c_ranks[r])) return QG_ERR_ALIGN;
+      uint16_t* base = static_cast<uint16_t*>(gather.c_ranks[r]) + gather.col0;
+      if (!make_output_map(&p.tm_out[r], base, m, n, ldc)) return QG_ERR_CUDA;
+    }
+    p.n_out = gather.nranks;
+  } else if (pair && esize == 2 && p.vec_ok) {
+    if (!make_output_map(&p.tm_out[0], c, m, n, ldc)) return QG_ERR_CUDA;
+    p.n_out = 1;
   }
   p.a_ts = fp4 ? a_ts : nullptr;
   p.b_ts = fp4 ? b_ts : nullptr;
@@ -411,6 +436,81 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   if (grid > skinny_max_ctas()) grid = skinny_max_ctas();
   if (launch_gemm_skinny(p, static_cast<int>(grid), s) != cudaSuccess) return QG_ERR_CUDA;
   return QG_OK;
+}
+
+int qg_gemm_nvfp4_gather(const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
+                         const void* b_sf, const float* b_ts, void* const* c_ranks, int nranks,
+                         int64_t col0, int64_t m, int64_t n_local, int64_t k, int64_t ldc,
+                         int sf_layout, uint32_t* status, qg_stream_t stream) {
+  if (!c_ranks || nranks < 1 || nranks > QG_MAX_RANKS) return QG_ERR_ARG;
+  if (col0 < 0 || col0 + n_local > ldc) return QG_ERR_SHAPE;
+  Gather g;
+  g.c_ranks = c_ranks;
+  g.nranks = nranks;
+  g.col0 = col0;
+  return gemm_common(true, a_q, a_sf, a_ts, b_q, b_sf, b_ts, c_ranks[0], QG_DTYPE_BF16, m,
+                     n_local, k, ldc, sf_layout, status, reinterpret_cast<cudaStream_t>(stream), g);
+}
+
+// CUDA IPC of device buffers (the fused gather's peer outputs).  The handle
+// carries the cudaIpcMemHandle_t of the allocation that holds dptr and
+// dptr's offset in it, so buffers from a caching allocator work too.
+namespace {
+std::mutex g_ipc_mu;
+std::map<void*, void*> g_ipc_base;  // imported pointer -> mapped allocation base
+}  // namespace
+
+static_assert(sizeof(cudaIpcMemHandle_t) + sizeof(uint64_t) == QG_IPC_HANDLE_BYTES, "IPC handle");
+
+int qg_ipc_export(const void* dptr, void* handle_out) {
+  if (!dptr || !handle_out) return QG_ERR_ARG;
+  using RangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static RangeFn range = [] {
+    void* fp = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fp, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<RangeFn>(nullptr);
+    return reinterpret_cast<RangeFn>(fp);
+  }();
+  if (!range) return QG_ERR_CUDA;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dptr)) != CUDA_SUCCESS) return QG_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return QG_ERR_CUDA;
+  const uint64_t off = reinterpret_cast<uint64_t>(dptr) - static_cast<uint64_t>(base);
+  std::memcpy(handle_out, &h, sizeof(h));
+  std::memcpy(static_cast<uint8_t*>(handle_out) + sizeof(h), &off, sizeof(off));
+  return QG_OK;
+}
+
+int qg_ipc_import(const void* handle, void** dptr_out) {
+  if (!handle || !dptr_out) return QG_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  uint64_t off = 0;
+  std::memcpy(&h, handle, sizeof(h));
+  std::memcpy(&off, static_cast<const uint8_t*>(handle) + sizeof(h), sizeof(off));
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return QG_ERR_CUDA;
+  void* p = static_cast<uint8_t*>(base) + off;
+  std::lock_guard<std::mutex> lk(g_ipc_mu);
+  g_ipc_base[p] = base;
+  *dptr_out = p;
+  return QG_OK;
+}
+
+int qg_ipc_close(void* dptr) {
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_ipc_mu);
+    auto it = g_ipc_base.find(dptr);
+    if (it == g_ipc_base.end()) return QG_ERR_ARG;
+    base = it->second;
+    g_ipc_base.erase(it);
+  }
+  return cudaIpcCloseMemHandle(base) == cudaSuccess ? QG_OK : QG_ERR_CUDA;
 }
 
 int qg_read_status(uint32_t* status, uint32_t* device_code, qg_stream_t stream) {

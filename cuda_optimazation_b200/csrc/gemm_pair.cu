@@ -411,10 +411,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
       const int row = mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM + quad * 32 + lane;
       const bool row_ok = row < p.m && !(p.diag & 8u);
       const int n0 = nt * Cfg::kBN;
-      if (Cfg::kEpiBytes > 0 && kOutBf16 && p.tma_c) {
+      if (Cfg::kEpiBytes > 0 && kOutBf16 && p.n_out > 0) {
         // TMEM -> registers -> bf16 in a swizzled shared-memory box -> TMA
-        // store (coalesced, asynchronous, clipped at the matrix edge).  One
-        // 64-column TMEM block per box; two boxes alternate.
+        // store (coalesced, asynchronous, clipped at the matrix edge) to each
+        // destination; for the fused gather the peers' copies cross NVLink
+        // while the next tiles are computed.  One 64-column TMEM block per
+        // box; two boxes alternate.
         const int row0 = mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM + quad * 32;
         uint8_t* ebuf = epi_smem + quad * 8192;
 #pragma unroll
@@ -448,7 +450,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && !(p.diag & 8u)) {
-            tma_store_2d(&p.tm_c, box, n0 + tmem_block(q) * 64, row0);
+            for (int d = 0; d < p.n_out; ++d)
+              tma_store_2d(&p.tm_out[d], box, n0 + tmem_block(q) * 64, row0);
             tma_store_commit();
           }
         }

@@ -12,8 +12,13 @@ struct GemmParams {
   CUtensorMap tm_b;    // uint8 [rows][K bytes], box 128 B x kBN, SWIZZLE_128B
   CUtensorMap tm_sfa;  // uint32 [scale_blocks][row_blocks][128], box (128, kBM/128, chunks)
   CUtensorMap tm_sfb;
-  CUtensorMap tm_c;    // bf16 C, box 64 x 32, SWIZZLE_128B (valid when tma_c)
-  int tma_c;           // pair kernel may store C through TMA
+  // bf16 C through TMA stores (pair kernel): box 64 x 32, SWIZZLE_128B.
+  // n_out destinations receive the same tile: this GPU's C, or for the
+  // fused column-parallel gather every rank's C (peer buffers mapped with
+  // CUDA IPC).  n_out == 0: direct stores to c.
+  static constexpr int kMaxOut = 8;
+  CUtensorMap tm_out[kMaxOut];
+  int n_out;
   void* c;
   int64_t ldc;  // elements
   int m, n, k;

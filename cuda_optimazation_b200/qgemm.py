@@ -53,6 +53,11 @@ SIGNATURES = {
     "qg_gemm_nvfp4_skinny": (_I32, [_VP, _I32, _I64, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64,
                                     _I32, _VP, ctypes.c_size_t, _VP, _VP]),
     "qg_gemm_nvfp4_skinny_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64]),
+    "qg_gemm_nvfp4_gather": (_I32, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64,
+                                    _I64, _I64, _I32, _VP, _VP]),
+    "qg_ipc_export": (_I32, [_VP, _VP]),
+    "qg_ipc_import": (_I32, [_VP, _VP]),
+    "qg_ipc_close": (_I32, [_VP]),
     "qg_read_status": (_I32, [_VP, _VP, _VP]),
     "qg_selftest_wait_timeout": (_I32, [_U64, _VP, _VP]),
 }
@@ -254,6 +259,47 @@ def gemm_nvfp4_skinny(x: torch.Tensor, w: "Nvfp4Result", out_dtype: torch.dtype 
                                     _ptr(status), _stream(stream))
     _check(rc, "qg_gemm_nvfp4_skinny")
     return out
+
+
+IPC_HANDLE_BYTES = 72
+MAX_RANKS = 8
+
+
+def ipc_export(t: torch.Tensor) -> bytes:
+    """CUDA IPC handle (+ offset) of the device buffer behind `t`."""
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(lib().qg_ipc_export(t.data_ptr(), buf), "qg_ipc_export")
+    return buf.raw
+
+
+def ipc_import(handle: bytes) -> int:
+    """Map a peer's buffer (from ipc_export in another process); returns the
+    device pointer in this process."""
+    ptr = ctypes.c_void_p()
+    _check(lib().qg_ipc_import(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES),
+                               ctypes.byref(ptr)), "qg_ipc_import")
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check(lib().qg_ipc_close(ctypes.c_void_p(ptr)), "qg_ipc_close")
+
+
+def gemm_nvfp4_gather(a: "Nvfp4Result", b_local: "Nvfp4Result", c_ptrs: list[int], col0: int,
+                      ldc: int, status: Optional[torch.Tensor] = None, stream=None) -> None:
+    """Column-parallel GEMM with the all-gather fused in: computes
+    C[:, col0:col0+b_local.rows] = A . B_local^T (bf16) into every buffer of
+    c_ptrs (this rank's own full C and the peers' IPC-mapped ones)."""
+    if len(c_ptrs) < 1 or len(c_ptrs) > MAX_RANKS:
+        raise ValueError("1..8 output buffers")
+    arr = (ctypes.c_void_p * len(c_ptrs))(*c_ptrs)
+    rc = lib().qg_gemm_nvfp4_gather(a.quantized.data_ptr(), a.block_scales.data_ptr(),
+                                    a.tensor_scale.data_ptr(), b_local.quantized.data_ptr(),
+                                    b_local.block_scales.data_ptr(),
+                                    b_local.tensor_scale.data_ptr(), arr, len(c_ptrs), col0,
+                                    a.rows, b_local.rows, a.k, ldc, a.layout, _ptr(status),
+                                    _stream(stream))
+    _check(rc, "qg_gemm_nvfp4_gather")
 
 
 def read_status(status: torch.Tensor, stream=None) -> tuple[int, int]:

@@ -174,6 +174,38 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
 /* Workspace bytes qg_gemm_nvfp4_skinny needs. */
 size_t qg_gemm_nvfp4_skinny_workspace_bytes(int64_t m, int64_t n, int64_t k);
 
+/* ---- Column-parallel GEMM with the output all-gather fused in ----------
+ * BASELINE config 5 shards B along N over the GPUs of one box
+ * (GEMMquant_sm110 itself is single-GPU; the north star asks for the N-sharded
+ * split with an optional output all-gather).  Instead of a GEMM followed by
+ * a collective, the CTA-pair GEMM's epilogue TMA-stores every output box
+ * into the C buffer of EVERY rank, so the NVLink transfer overlaps the math
+ * tile by tile.
+ *
+ * c_ranks[r] (r < nranks <= QG_MAX_RANKS) is rank r's full bf16 C (m rows,
+ * row stride ldc elements), this process's own buffer included; peers'
+ * buffers are mapped with qg_ipc_import.  This call computes
+ * C[:, col0 : col0 + n_local] = (a_ts*b_ts) * A . B_local^T (B_local: the
+ * n_local rows of B this rank owns, NVFP4, MMA layout) and writes those
+ * columns into every c_ranks[r].  col0 % 8 == 0, ldc % 8 == 0, buffers
+ * 16-byte aligned.  Stream-ordered on this GPU only: the caller orders the
+ * ranks (e.g. synchronise + a host barrier) before reading the gathered C. */
+#define QG_MAX_RANKS 8
+int qg_gemm_nvfp4_gather(const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
+                         const void* b_sf, const float* b_ts, void* const* c_ranks, int nranks,
+                         int64_t col0, int64_t m, int64_t n_local, int64_t k, int64_t ldc,
+                         int sf_layout, uint32_t* status, qg_stream_t stream);
+
+/* CUDA IPC for the gather's peer buffers.  A handle is QG_IPC_HANDLE_BYTES:
+ * the cudaIpcMemHandle_t of the allocation holding dptr plus dptr's offset
+ * in it (so pointers inside a caching allocator's block work).  Import maps
+ * a peer's buffer into this process (peer access enabled lazily); close
+ * unmaps it.  No reference counterpart. */
+#define QG_IPC_HANDLE_BYTES 72
+int qg_ipc_export(const void* dptr, void* handle_out);
+int qg_ipc_import(const void* handle, void** dptr_out);
+int qg_ipc_close(void* dptr);
+
 /* Read and clear a device status word (synchronises `stream`).  Returns
  * QG_OK, QG_ERR_TIMEOUT or QG_ERR_CUDA; *device_code (may be NULL) gets the
  * raw device code. */
