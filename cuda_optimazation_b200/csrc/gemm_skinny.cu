@@ -115,14 +115,14 @@ struct SegCursor {
   }
 };
 
-// Diagnostic stamp (QG_DIAG_FLAGS bit 6): CTA 0 writes %globaltimer into
+// Diagnostic stamp (QG_DIAG_FLAGS bit 6): CTA (diag >> 16) writes %globaltimer into
 // slot `i` of the last (never used by a launched CTA) partial slice pair.
 __device__ __forceinline__ void trace_cta(const SkinnyParams& p, int i) {
   if (p.diag & 64u)
     reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * 2 * p.m * 128)[i] = globaltimer_ns();
 }
 __device__ __forceinline__ void trace(const SkinnyParams& p, int i) {
-  if ((p.diag & 64u) && blockIdx.x == 0 && i < 512)
+  if ((p.diag & 64u) && blockIdx.x == (p.diag >> 16) && i < 512)
     reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * 2 * p.m * 128)[i] = globaltimer_ns();
 }
 
@@ -567,6 +567,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
       mbar_try_wait(&acc_full[buf], (seg >> 1) & 1);
       tc_fence_after();
+      if (quad == 0 && lane == 0) trace(p, 120 + seg);
       const int col = quad * 32 + lane;
       const int n = t * Cfg::kBM + col;
       const bool n_ok = n < p.n;
@@ -574,19 +575,27 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       const int cl = contributor(static_cast<int64_t>(t + 1) * ur.nkb - 1);
       float* mine = p.part + static_cast<int64_t>(blockIdx.x * 2 + (t == my_first ? 0 : 1)) *
                                  p.m * Cfg::kBM;
+      // TMEM reads queue behind the MMAs already issued for the next
+      // segment, so each wait can cost the queued MMA time: read up to 64
+      // columns per wait (one wait for kN <= 64, two for kN = 128).
+      constexpr int kGroup = kN < 64 ? kN : 64;
 #pragma unroll
-      for (int cc = 0; cc < kN / 16; ++cc) {
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(t_quad + static_cast<uint32_t>(buf * kN + cc * 16), r);
+      for (int gc = 0; gc < kN / kGroup; ++gc) {
+        uint32_t r[kGroup];
+#pragma unroll
+        for (int cc = 0; cc < kGroup / 16; ++cc)
+          tmem_ld_32x32b_x16(t_quad + static_cast<uint32_t>(buf * kN + gc * kGroup + cc * 16),
+                             *reinterpret_cast<uint32_t(*)[16]>(r + cc * 16));
         tmem_wait_ld();
-        if (cc == kN / 16 - 1) {
+        if (gc == kN / kGroup - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
+        if (gc == 0 && quad == 0 && lane == 0) trace(p, 110 + seg);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = cc * 16 + j;
+        for (int j = 0; j < kGroup; ++j) {
+          const int m = gc * kGroup + j;
           if (m < p.m) {
             const float v = __uint_as_float(r[j]);
             if (cf == cl) {

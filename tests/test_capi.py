@@ -44,3 +44,23 @@ def test_argument_validation_without_gpu(qlib):
                            None, None) == qlib.ERR_ARG
     assert L.qg_quantize_nvfp4(None, 0, 1, 16, 1, None, None, None, None, None) == qlib.ERR_ARG
     assert L.qg_read_status(None, None, None) == qlib.ERR_ARG
+
+
+def test_gather_and_ipc_argument_validation_without_gpu(qlib):
+    import ctypes
+    L = qlib.lib()
+    one = (ctypes.c_void_p * 1)(ctypes.c_void_p(16))
+    nine = (ctypes.c_void_p * 9)(*([ctypes.c_void_p(16)] * 9))
+    # Rank count outside 1..8 and a shard that runs past ldc are rejected first.
+    assert L.qg_gemm_nvfp4_gather(None, None, None, None, None, None, one, 0, 0, 256, 256, 256,
+                                  256, 1, None, None) == qlib.ERR_ARG
+    assert L.qg_gemm_nvfp4_gather(None, None, None, None, None, None, nine, 9, 0, 256, 256, 256,
+                                  256, 1, None, None) == qlib.ERR_ARG
+    assert L.qg_gemm_nvfp4_gather(None, None, None, None, None, None, one, 1, 128, 256, 256, 256,
+                                  256, 1, None, None) == qlib.ERR_SHAPE
+    assert L.qg_gemm_nvfp4_gather(None, None, None, None, None, None, None, 1, 0, 256, 256, 256,
+                                  256, 1, None, None) == qlib.ERR_ARG
+    assert L.qg_ipc_export(None, None) == qlib.ERR_ARG
+    assert L.qg_ipc_import(None, None) == qlib.ERR_ARG
+    assert L.qg_ipc_close(ctypes.c_void_p(4096)) == qlib.ERR_ARG  # never imported
+    assert qlib.IPC_HANDLE_BYTES == 72 and qlib.MAX_RANKS == 8

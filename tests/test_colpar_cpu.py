@@ -83,3 +83,23 @@ def test_colpar_two_gloo_ranks_match_oracle(tmp_path, oracle):
     assert got.shape == (m, n)
     # The shards run the same O2 per output element: bit equality.
     assert np.array_equal(got, ref)
+
+
+def test_shard_rows_kmajor_views():
+    """Row shards of a K-major NVFP4 operand are contiguous views of the
+    values and of whole 128-row scale blocks (checked on CPU tensors)."""
+    from cuda_optimazation_b200 import colpar
+    from cuda_optimazation_b200.qgemm import LAYOUT_MMA, LAYOUT_MMA_KMAJOR, Nvfp4Result
+    rows, k = 768, 512
+    sf_blocks = (k // 16 + 3) // 4
+    q = torch.arange(rows * k // 2, dtype=torch.int64).to(torch.uint8)
+    sf = torch.arange((rows // 128) * sf_blocks * 512, dtype=torch.int64).to(torch.uint8)
+    op = Nvfp4Result(q, sf, torch.ones(1), rows, k, LAYOUT_MMA_KMAJOR)
+    sh = colpar.shard_rows(op, 256, 512)
+    assert sh.rows == 256 and sh.k == k
+    assert torch.equal(sh.quantized, q[256 * k // 2: 512 * k // 2])
+    assert torch.equal(sh.block_scales, sf[2 * sf_blocks * 512: 4 * sf_blocks * 512])
+    with pytest.raises(ValueError):
+        colpar.shard_rows(op, 100, 512)
+    with pytest.raises(ValueError):
+        colpar.shard_rows(Nvfp4Result(q, sf, torch.ones(1), rows, k, LAYOUT_MMA), 0, 256)
