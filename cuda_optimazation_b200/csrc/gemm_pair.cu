@@ -419,53 +419,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
         // box; two boxes alternate.
         const int row0 = mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM + quad * 32;
         uint8_t* ebuf = epi_smem + quad * 8192;
-#ifdef QG_PAIR_EPI_LOADALL
-        // Whole accumulator row to registers as bf16 first (TMEM reads issued
-        // after the next tile's MMAs would queue behind them), then both
-        // halves handed back, then the boxes.
-        uint32_t packed[Cfg::kBN / 2];
-#pragma unroll
-        for (int q = 0; q < Cfg::kBN / 64; ++q) {
-          uint32_t r0[32], r1[32];
-          tmem_ld_32x32b_x32(t_row + q * 64, r0);
-          tmem_ld_32x32b_x32(t_row + q * 64 + 32, r1);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            packed[q * 32 + j] = bf16x2_bits(__uint_as_float(r0[2 * j]) * alpha,
-                                             __uint_as_float(r0[2 * j + 1]) * alpha);
-            packed[q * 32 + 16 + j] = bf16x2_bits(__uint_as_float(r1[2 * j]) * alpha,
-                                                  __uint_as_float(r1[2 * j + 1]) * alpha);
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_cluster_relaxed(acc_empty_leader0);
-          if (Cfg::kIssuers == 2) mbar_arrive_cluster_relaxed(acc_empty_leader1);
-        }
-#pragma unroll
-        for (int q = 0; q < Cfg::kBN / 64; ++q) {
-          uint8_t* box = ebuf + (q & 1) * 4096;
-          if ((q & 1) == 0) {
-            if (lane == 0) tma_store_wait_read<0>();  // both boxes read by earlier stores
-            __syncwarp();
-          }
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const uint32_t* src = packed + q * 32 + c * 4;
-            *reinterpret_cast<uint4*>(box + lane * 128 + ((c ^ (lane & 7)) * 16)) =
-                make_uint4(src[0], src[1], src[2], src[3]);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && !(p.diag & 8u)) {
-            for (int d = 0; d < p.n_out; ++d)
-              tma_store_2d(&p.tm_out[d], box, n0 + tmem_block(q) * 64, row0);
-            tma_store_commit();
-          }
-        }
-#else
 #pragma unroll
         for (int q = 0; q < Cfg::kBN / 64; ++q) {
           uint8_t* box = ebuf + (q & 1) * 4096;
@@ -502,7 +455,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
             tma_store_commit();
           }
         }
-#endif
       } else if (kOutBf16 && p.vec_ok && n0 + Cfg::kBN <= p.n) {
         // Full tile: the whole accumulator row goes to registers as bf16,
         // the accumulator is handed back, then 16-byte stores.

@@ -579,6 +579,19 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       // segment, so each wait can cost the queued MMA time: read up to 64
       // columns per wait (one wait for kN <= 64, two for kN = 128).
       constexpr int kGroup = kN < 64 ? kN : 64;
+      // One destination per segment: C (scaled, row stride ldc) for a whole
+      // tile, else this CTA's fp32 partial slice (row stride 128).  The
+      // per-element code is kept to a multiply, an address step and a store:
+      // the unrolled epilogue competes for instruction cache with four other
+      // roles, and a fetch miss under the weight stream costs microseconds.
+      const bool whole = cf == cl;
+      const bool st_ok = !(p.diag & 8u) && (!whole || n_ok);
+      const float scale = whole ? alpha : 1.0f;
+      const bool bf16_dst = whole && p.out_bf16;
+      const int64_t stride = whole ? p.ldc : Cfg::kBM;
+      float* dstf = whole ? reinterpret_cast<float*>(p.c) + n : mine + col;
+      __nv_bfloat16* dstb = reinterpret_cast<__nv_bfloat16*>(p.c) + n;
+      const int mrows = p.m;
 #pragma unroll
       for (int gc = 0; gc < kN / kGroup; ++gc) {
         uint32_t r[kGroup];
@@ -593,17 +606,20 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
           if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
         if (gc == 0 && quad == 0 && lane == 0) trace(p, 110 + seg);
+        if (!st_ok) continue;
+        if (bf16_dst) {
 #pragma unroll
-        for (int j = 0; j < kGroup; ++j) {
-          const int m = gc * kGroup + j;
-          if (m < p.m) {
-            const float v = __uint_as_float(r[j]);
-            if (cf == cl) {
-              if (n_ok) store_c(m, n, v * alpha);
-            } else {
-              __stcg(mine + m * Cfg::kBM + col, v);
-            }
-          }
+          for (int j = 0; j < kGroup; ++j)
+            if (gc * kGroup + j < mrows)
+              dstb[(gc * kGroup + j) * stride] = __float2bfloat16_rn(__uint_as_float(r[j]) * scale);
+        } else if (whole) {
+#pragma unroll
+          for (int j = 0; j < kGroup; ++j)
+            if (gc * kGroup + j < mrows) dstf[(gc * kGroup + j) * stride] = __uint_as_float(r[j]) * scale;
+        } else {
+#pragma unroll
+          for (int j = 0; j < kGroup; ++j)
+            if (gc * kGroup + j < mrows) __stcg(dstf + (gc * kGroup + j) * stride, __uint_as_float(r[j]));
         }
       }
       if (quad == 0 && lane == 0) trace(p, 100 + seg);
@@ -627,12 +643,14 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
         const int64_t slice = static_cast<int64_t>(p.m) * Cfg::kBM;
         const int nb = t * Cfg::kBM + quad * 32 + c8;
         const bool vec = p.vec_ok && nb + 8 <= p.n;
+#pragma unroll 1
         for (int m0 = 0; m0 < p.m; m0 += 32) {
           float acc[4][8];
 #pragma unroll
           for (int i = 0; i < 4; ++i)
 #pragma unroll
             for (int e = 0; e < 8; ++e) acc[i][e] = 0.0f;
+#pragma unroll 1
           for (int c = cf; c <= cl; c += 2) {
             const bool two = c + 1 <= cl;
             const float* s0 = p.part + (c * 2 + (t == first_tile(c) ? 0 : 1)) * slice + quad * 32 + c8;
