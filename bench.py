@@ -36,6 +36,9 @@ ROOT = Path(__file__).resolve().parent
 
 WORKLOADS = {
     "nvfp4_8192": dict(fmt="nvfp4", m=8192, n=8192, k=8192, out="bf16", cfg=1),
+    # the same GEMM with the output requantised to NVFP4 in the epilogue
+    # (the reference's tc6 fused epilogue; SURVEY next-step f1)
+    "nvfp4_8192_requant": dict(fmt="nvfp4", m=8192, n=8192, k=8192, out="nvfp4", cfg=1),
     "nvfp4_256": dict(fmt="nvfp4", m=256, n=256, k=256, out="fp32", cfg=0),
     "mxfp8_ffn": dict(fmt="mxfp8", m=4096, n=14336, k=4096, out="bf16", cfg=2),
     "colpar": dict(fmt="nvfp4", m=16384, n=53248, k=8192, out="bf16", cfg=4),
@@ -207,11 +210,12 @@ def run_ours(args, w, rank, world, dist, torch):
     else:
         n = n_total
     out_dtype = torch.bfloat16 if w["out"] == "bf16" else torch.float32
+    requant = w["out"] == "nvfp4"
     gen = torch.Generator(device=dev)
     b_std = 0.02 if w["fmt"] == "mxfp8" else 1.0
     # Operand sets rotate between steps so no step finds its inputs in L2.
     set_bytes = (m + n) * k * (0.5 if w["fmt"] == "nvfp4" else 1.0)
-    out_bytes = m * n * (2 if w["out"] == "bf16" else 4)
+    out_bytes = m * n * {"bf16": 2, "fp32": 4, "nvfp4": 0.5625}[w["out"]]
     nsets = 1 if set_bytes + out_bytes > 3 * 126e6 else 3
     sets = []
     for s in range(nsets):
@@ -229,13 +233,34 @@ def run_ours(args, w, rank, world, dist, torch):
         # A is broadcast once from rank 0 (untimed).
         for A, _ in sets:
             cp.broadcast_operand([A.quantized, A.block_scales, A.tensor_scale], src=0)
-    C = torch.empty(m, n, dtype=out_dtype, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
+    if requant:
+        # NVFP4 output (values then REF_LINEAR scales in one buffer) under a
+        # fixed output tensor scale, as tc6 takes it.
+        qbytes = m * n // 2
+        C = torch.empty(qbytes + m * n // 16, dtype=torch.uint8, device=dev)
+        out_ts = torch.full((1,), 4.0, dtype=torch.float32, device=dev)
+    else:
+        C = torch.empty(m, n, dtype=out_dtype, device=dev)
     torch.cuda.synchronize()
+
+    def gemm_into(aq, asf, ats, bq, bsf, bts, dst, layout):
+        if requant:
+            q.gemm_nvfp4_requant_raw(aq, asf, ats, bq, bsf, bts, out_ts, dst[:qbytes],
+                                     dst[qbytes:], m, n, k, q.LAYOUT_REF_LINEAR, layout,
+                                     status=status)
+        elif w["fmt"] == "nvfp4":
+            q.gemm_nvfp4_raw(aq, asf, ats, bq, bsf, bts, dst, m, n, k, layout, status)
+        else:
+            q.gemm_mxfp8_raw(aq, asf, bq, bsf, dst, m, n, k, layout, status)
 
     def step(i):
         A, B = sets[i % nsets]
-        q.block_scaled_gemm(A, B, out=C, status=status)
+        if requant:
+            gemm_into(A.quantized, A.block_scales, A.tensor_scale, B.quantized, B.block_scales,
+                      B.tensor_scale, C, A.layout)
+        else:
+            q.block_scaled_gemm(A, B, out=C, status=status)
 
     flops_rank = 2.0 * m * n * k
     for i in range(args.warmup):
@@ -332,14 +357,14 @@ def run_ours(args, w, rank, world, dist, torch):
              ("bsf", B0.block_scales))}
     hts = [A0.tensor_scale.cpu().pin_memory() if hasattr(A0, "tensor_scale") else None,
            B0.tensor_scale.cpu().pin_memory() if hasattr(B0, "tensor_scale") else None]
-    hout = [torch.empty(m, n, dtype=out_dtype).pin_memory() for _ in range(2)]
+    hout = [torch.empty_like(C, device="cpu").pin_memory() for _ in range(2)]
     # Two device buffer sets so step i's host->device copies (copy-in
     # stream) and step i-1's device->host read of the result (copy-out
     # stream) overlap step i's GEMM, as a serving loop would run them; every
     # step still moves its full inputs in and its full result out.
     dA = [{name: torch.empty_like(h, device=dev) for name, h in host.items()} for _ in range(2)]
     dts = [[None if h is None else torch.empty_like(h, device=dev) for h in hts] for _ in range(2)]
-    dC = [torch.empty(m, n, dtype=out_dtype, device=dev) for _ in range(2)]
+    dC = [torch.empty_like(C) for _ in range(2)]
     h2d = sum(h.numel() * h.element_size() for h in host.values()) + \
         sum(h.numel() * 4 for h in hts if h is not None)
     d2h = hout[0].numel() * hout[0].element_size()
@@ -362,12 +387,8 @@ def run_ours(args, w, rank, world, dist, torch):
             ev_in[b_].record(s_in)
         stream.wait_event(ev_in[b_])
         stream.wait_event(ev_out[b_])               # C[b_] read back (step i-2)
-        if w["fmt"] == "nvfp4":
-            q.gemm_nvfp4_raw(dA[b_]["aq"], dA[b_]["asf"], dts[b_][0], dA[b_]["bq"],
-                             dA[b_]["bsf"], dts[b_][1], dC[b_], m, n, k, A0.layout, status)
-        else:
-            q.gemm_mxfp8_raw(dA[b_]["aq"], dA[b_]["asf"], dA[b_]["bq"], dA[b_]["bsf"], dC[b_],
-                             m, n, k, A0.layout, status)
+        gemm_into(dA[b_]["aq"], dA[b_]["asf"], dts[b_][0], dA[b_]["bq"], dA[b_]["bsf"],
+                  dts[b_][1], dC[b_], A0.layout)
         ev_gemm[b_].record(stream)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_gemm[b_])

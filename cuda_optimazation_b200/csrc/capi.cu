@@ -153,12 +153,23 @@ struct Gather {
   int64_t col0 = 0;
 };
 
+// `requant` (q != null): NVFP4 output written by the pair kernel's
+// requantising epilogue instead of C (c / c_dtype / ldc unused).
+struct Requant {
+  uint8_t* q = nullptr;
+  uint8_t* sf = nullptr;
+  const float* ts = nullptr;
+  uint32_t* amax = nullptr;
+  int layout = 0;
+};
+
 int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
                 const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
                 int64_t k, int64_t ldc, int sf_layout, uint32_t* status, cudaStream_t stream,
-                const Gather& gather = Gather()) {
-  if (!a_q || !a_sf || !b_q || !b_sf || !c) return QG_ERR_ARG;
-  if (c_dtype != QG_DTYPE_F32 && c_dtype != QG_DTYPE_BF16) return QG_ERR_DTYPE;
+                const Gather& gather = Gather(), const Requant& requant = Requant()) {
+  const bool rq = requant.q != nullptr;
+  if (!a_q || !a_sf || !b_q || !b_sf || (!c && !rq)) return QG_ERR_ARG;
+  if (!rq && c_dtype != QG_DTYPE_F32 && c_dtype != QG_DTYPE_BF16) return QG_ERR_DTYPE;
   if (sf_layout != QG_LAYOUT_MMA && sf_layout != QG_LAYOUT_MMA_KMAJOR) return QG_ERR_LAYOUT;
   if (m < 1 || n < 1 || k < 32 || (k % 32) != 0 || ldc < n) return QG_ERR_SHAPE;
   if (m > (1ll << 31) - 1 || n > (1ll << 31) - 1 || k > (1ll << 31) - 1) return QG_ERR_SHAPE;
@@ -169,7 +180,7 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
   if (int d = check_device()) return d;
   if (!encode_fn()) return QG_ERR_CUDA;
   const int sv = fp4 ? 16 : 32;
-  const int variant = gather.nranks > 0 ? 1 : gemm_variant(fp4, m);
+  const int variant = (gather.nranks > 0 || rq) ? 1 : gemm_variant(fp4, m);
   const bool pair = variant == 1;
   // Tile of one scheduling unit (a CTA pair: 256 x 256; one CTA: 128 x 256)
   // and the rows each CTA's TMA boxes cover.
@@ -206,6 +217,17 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
     if (!make_output_map(&p.tm_out[0], c, m, n, ldc)) return QG_ERR_CUDA;
     p.n_out = 1;
   }
+  if (rq) {
+    p.vec_ok = 0;
+    p.n_out = 0;
+    p.rq_q = requant.q;
+    p.rq_sf = requant.sf;
+    p.rq_ts = requant.ts;
+    p.rq_amax = requant.amax;
+    p.rq_layout = requant.layout;
+    p.rq_row_blocks = static_cast<int>((m + 127) / 128);
+    p.rq_sf_blocks = static_cast<int>((n / 16 + 3) / 4);
+  }
   p.a_ts = fp4 ? a_ts : nullptr;
   p.b_ts = fp4 ? b_ts : nullptr;
   p.status = status;
@@ -216,7 +238,7 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
   if (pair) {
     const int64_t pairs = num_sms() / 2;
     const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
-    e = launch_gemm_pair(p, fp4, c_dtype == QG_DTYPE_BF16, grid, stream);
+    e = launch_gemm_pair(p, fp4, rq ? 2 : (c_dtype == QG_DTYPE_BF16 ? 1 : 0), grid, stream);
   } else {
     const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
     e = variant == 2 ? launch_gemm_blockscaled(p, fp4, c_dtype == QG_DTYPE_BF16, grid, stream)
@@ -342,6 +364,34 @@ int qg_gemm_nvfp4(const void* a_q, const void* a_sf, const float* a_ts, const vo
                   int64_t k, int64_t ldc, int sf_layout, uint32_t* status, qg_stream_t stream) {
   return gemm_common(true, a_q, a_sf, a_ts, b_q, b_sf, b_ts, c, c_dtype, m, n, k, ldc, sf_layout,
                      status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int qg_gemm_nvfp4_requant(const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
+                          const void* b_sf, const float* b_ts, const float* out_ts, void* out_q,
+                          void* out_sf, int out_layout, uint32_t* out_amax, int64_t m, int64_t n,
+                          int64_t k, int sf_layout, uint32_t* status, qg_stream_t stream) {
+  if (!out_q || !out_sf) return QG_ERR_ARG;
+  if (out_layout < QG_LAYOUT_REF_LINEAR || out_layout > QG_LAYOUT_MMA_KMAJOR) return QG_ERR_LAYOUT;
+  if (n < 16 || (n % 16) != 0) return QG_ERR_SHAPE;
+  if (!aligned16(out_q) || (reinterpret_cast<uintptr_t>(out_sf) & 3u) ||
+      (out_amax && (reinterpret_cast<uintptr_t>(out_amax) & 3u)))
+    return QG_ERR_ALIGN;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (out_layout != QG_LAYOUT_REF_LINEAR && m > 0 && ((m % 128) != 0 || ((n / 16) % 4) != 0) &&
+      k >= 32 && (k % 32) == 0 && a_q && a_sf && b_q && b_sf) {
+    // Padded scale slots of the MMA layouts must read as zero scales.
+    if (cudaMemsetAsync(out_sf, 0, static_cast<size_t>(qg_scale_bytes(m, n, 16)), s) !=
+        cudaSuccess)
+      return QG_ERR_CUDA;
+  }
+  Requant r;
+  r.q = static_cast<uint8_t*>(out_q);
+  r.sf = static_cast<uint8_t*>(out_sf);
+  r.ts = out_ts;
+  r.amax = out_amax;
+  r.layout = out_layout;
+  return gemm_common(true, a_q, a_sf, a_ts, b_q, b_sf, b_ts, nullptr, QG_DTYPE_F32, m, n, k, n,
+                     sf_layout, status, s, Gather(), r);
 }
 
 int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, void* c,
@@ -523,6 +573,15 @@ int qg_read_status(uint32_t* status, uint32_t* device_code, qg_stream_t stream) 
   if (cudaMemsetAsync(status, 0, sizeof(uint32_t), s) != cudaSuccess) return QG_ERR_CUDA;
   if (device_code) *device_code = v;
   return v == 0 ? QG_OK : QG_ERR_TIMEOUT;
+}
+
+int qg_selftest_e2m1_cvt(unsigned long long* out, qg_stream_t stream) {
+  if (!out) return QG_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return QG_ERR_ALIGN;
+  if (int d = check_device()) return d;
+  return launch_e2m1_cvt_selftest(out, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? QG_OK
+             : QG_ERR_CUDA;
 }
 
 int qg_selftest_wait_timeout(uint64_t timeout_ns, uint32_t* status, qg_stream_t stream) {

@@ -33,11 +33,13 @@
 //   warp 10     in the leader, MMA issuer 1.
 //   warps 2..5  epilogue: each CTA drains its own accumulator rows.
 //   warps 6..9  scale stagers.
+//   warps 11..14 (NVFP4-output kernel only) more epilogue warps.
 // No TMA load uses cluster multicast.  Every wait is bounded (qg_ptx.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include "qg_codec.cuh"
 #include "qg_gemm.h"
 #include "qg_ptx.cuh"
 
@@ -136,10 +138,21 @@ __device__ __forceinline__ void stage_scales(const uint8_t* ssfa, const uint8_t*
   tmem_st_32x32b<Cfg::kSfbCols>(t_quad + sfb_col, b);
 }
 
-template <bool kFp4, bool kOutBf16>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
+// kOut: 0 fp32 C, 1 bf16 C, 2 NVFP4 output (values + e4m3 block scales,
+// requantised in the epilogue as the reference's tc6 store_tile does,
+// GEMMsm110/include/backends/tc6_nvfp4.cuh:460-503).
+// Threads per CTA: 11 warps; the NVFP4-output epilogue adds four more
+// epilogue warps (11..14, one per TMEM lane quadrant).
+template <int kOut>
+constexpr int pair_threads() {
+  return kOut == 2 ? 480 : 352;
+}
+
+template <bool kFp4, int kOut>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>(), 1)
     gemm_pair_kernel(const __grid_constant__ GemmParams p) {
   using Cfg = PairCfg<kFp4>;
+  constexpr bool kOutBf16 = kOut == 1;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -170,7 +183,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
       mbar_init(&empty_bar[s], Cfg::kIssuers);
     }
     mbar_init(acc_full, Cfg::kIssuers);
-    for (int i = 0; i < Cfg::kIssuers; ++i) mbar_init(&acc_empty[i], 8);
+    for (int i = 0; i < Cfg::kIssuers; ++i) mbar_init(&acc_empty[i], kOut == 2 ? 16 : 8);
     for (int i = 0; i < Cfg::kIssuers; ++i) mbar_init(&drain_bar[i], 1);
     *abort_flag = 0u;
     fence_barrier_init();
@@ -340,7 +353,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
       uint32_t dummy = 0;
       mbar_wait_bounded(&drain_bar[h], 0, p.timeout_ns, &dummy, nullptr, 0);
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 6 && warp <= 9) {
     // ---------------------------------------------------------------- scale stagers
     const int quad = warp % 4;
     const int stager_kb = total_kb;
@@ -397,6 +410,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
     // and block 2 output block 1 (issuer h's MMA N rows are h*64.. of each
     // CTA's half); the map is its own inverse.
     auto tmem_block = [](int b) { return Cfg::kIssuers == 2 && (b == 1 || b == 2) ? 3 - b : b; };
+    // NVFP4 output: 1 / tensor scale (IEEE division, as the reference's host
+    // quantizer forms it) and the running amax of this lane's outputs.
+    float rq_inv_ts = 1.0f, rq_max = 0.0f;
+    if constexpr (kOut == 2) rq_inv_ts = __fdiv_rn(1.0f, p.rq_ts ? *p.rq_ts : 1.0f);
     for (int it = 0; it < my_tiles; ++it) {
       const int tile = pair + it * npairs;
       const int mt = tile % p.num_m_tiles;
@@ -411,7 +428,82 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
       const int row = mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM + quad * 32 + lane;
       const bool row_ok = row < p.m && !(p.diag & 8u);
       const int n0 = nt * Cfg::kBN;
-      if (Cfg::kEpiBytes > 0 && kOutBf16 && p.n_out > 0) {
+      if constexpr (kOut == 2) {
+        // NVFP4 output.  Each lane owns one output row, so a 16-column block
+        // (one e4m3 scale) lies in one thread's registers: the block amax
+        // needs no shuffles.  The element values are alpha * acc, the same
+        // fp32 numbers the fp32-output GEMM stores, quantised with the
+        // make_nvfp4_reference steps
+        // (GEMMsm110/include/requant/nvfp4_reference.cuh:76-112) under the
+        // caller's tensor scale.  Two warps per TMEM lane quadrant (warps 2-5
+        // and 11-14) split the columns: for each issuer's 128-column half a
+        // warp loads its 64 columns, hands the half back at once (the next
+        // tile's MMAs start while this tile is requantised), then encodes.
+        const int sub = warp >= 11 ? 1 : 0;
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          const int tb = 2 * h + sub;
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(t_row + tb * 64, r0);
+          tmem_ld_32x32b_x32(t_row + tb * 64 + 32, r1);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster_relaxed(h ? acc_empty_leader1 : acc_empty_leader0);
+          const int col0 = n0 + tmem_block(tb) * 64;
+          if (!row_ok || col0 >= p.n) continue;
+          uint32_t w[8];
+          uint32_t sbits[4];
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const uint32_t* src = g < 2 ? r0 + g * 16 : r1 + (g - 2) * 16;
+            float v[16];
+            float bmax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              v[i] = __fmul_rn(__uint_as_float(src[i]), alpha);
+              bmax = fmaxf(bmax, fabsf(v[i]));
+            }
+            if (col0 + 16 * g < p.n) rq_max = fmaxf(rq_max, bmax);
+            sbits[g] = nvfp4_encode_block_cvt(v, bmax, rq_inv_ts, w[2 * g], w[2 * g + 1]);
+            if (p.rq_layout == 0) {
+              // REF_LINEAR: element 2i in the high nibble (pack_fp4.cuh:11-15).
+              w[2 * g] = ((w[2 * g] & 0x0f0f0f0fu) << 4) | ((w[2 * g] >> 4) & 0x0f0f0f0fu);
+              w[2 * g + 1] =
+                  ((w[2 * g + 1] & 0x0f0f0f0fu) << 4) | ((w[2 * g + 1] >> 4) & 0x0f0f0f0fu);
+            }
+          }
+          const int64_t e0 = static_cast<int64_t>(row) * p.n + col0;
+          const bool full = col0 + 64 <= p.n;
+          if (full && (p.n % 32) == 0) {
+            uint4* dst = reinterpret_cast<uint4*>(p.rq_q + e0 / 2);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          } else {
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              if (col0 + 16 * g < p.n)
+                reinterpret_cast<uint2*>(p.rq_q + e0 / 2)[g] = make_uint2(w[2 * g], w[2 * g + 1]);
+          }
+          int64_t so;
+          bool word;
+          if (p.rq_layout == 0) {
+            so = e0 / 16;
+            word = full && (p.n % 64) == 0;
+          } else {
+            so = mma_scale_offset(row, col0 / 16, p.rq_row_blocks, p.rq_sf_blocks, p.rq_layout);
+            word = full;
+          }
+          if (word) {
+            *reinterpret_cast<uint32_t*>(p.rq_sf + so) =
+                sbits[0] | (sbits[1] << 8) | (sbits[2] << 16) | (sbits[3] << 24);
+          } else {
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              if (col0 + 16 * g < p.n) p.rq_sf[so + g] = static_cast<uint8_t>(sbits[g]);
+          }
+        }
+      } else if (Cfg::kEpiBytes > 0 && kOutBf16 && p.n_out > 0) {
         // TMEM -> registers -> bf16 in a swizzled shared-memory box -> TMA
         // store (coalesced, asynchronous, clipped at the matrix edge) to each
         // destination; for the fused gather the peers' copies cross NVLink
@@ -549,6 +641,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
         }
       }
     }
+    if constexpr (kOut == 2) {
+      if (p.rq_amax) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) rq_max = fmaxf(rq_max, __shfl_xor_sync(0xffffffffu, rq_max, o));
+        // Non-negative floats order like their bit patterns.
+        if (lane == 0 && rq_max > 0.0f) atomicMax(p.rq_amax, __float_as_uint(rq_max));
+      }
+    }
   }
 
   if (Cfg::kEpiBytes > 0 && warp >= 2 && warp <= 5 && (threadIdx.x % 32) == 0)
@@ -561,10 +661,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(352, 1)
   }
 }
 
-template <bool kFp4, bool kOutBf16>
+template <bool kFp4, int kOut>
 static cudaError_t launch_pair_one(const GemmParams& p, int grid, cudaStream_t stream) {
   using Cfg = PairCfg<kFp4>;
-  auto kern = gemm_pair_kernel<kFp4, kOutBf16>;
+  auto kern = gemm_pair_kernel<kFp4, kOut>;
   static bool attr_done = false;
   if (!attr_done) {
     cudaError_t e =
@@ -572,18 +672,20 @@ static cudaError_t launch_pair_one(const GemmParams& p, int grid, cudaStream_t s
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  kern<<<grid, kOut == 2 ? pair_threads<kOut>() : Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm_pair(const GemmParams& p, bool fp4, bool out_bf16, int grid,
+cudaError_t launch_gemm_pair(const GemmParams& p, bool fp4, int out_kind, int grid,
                              cudaStream_t stream) {
   if (fp4) {
-    return out_bf16 ? launch_pair_one<true, true>(p, grid, stream)
-                    : launch_pair_one<true, false>(p, grid, stream);
+    if (out_kind == 2) return launch_pair_one<true, 2>(p, grid, stream);
+    return out_kind == 1 ? launch_pair_one<true, 1>(p, grid, stream)
+                         : launch_pair_one<true, 0>(p, grid, stream);
   }
-  return out_bf16 ? launch_pair_one<false, true>(p, grid, stream)
-                  : launch_pair_one<false, false>(p, grid, stream);
+  if (out_kind == 2) return cudaErrorInvalidValue;
+  return out_kind == 1 ? launch_pair_one<false, 1>(p, grid, stream)
+                       : launch_pair_one<false, 0>(p, grid, stream);
 }
 
 int pair_tile_m() { return 2 * PairCfg<true>::kBM; }

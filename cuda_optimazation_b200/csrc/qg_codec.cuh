@@ -136,4 +136,42 @@ __device__ __forceinline__ uint32_t nvfp4_encode_block(const float (&v)[16], flo
   return sbits;
 }
 
+// Two fp32 values -> one byte of e2m1 codes with the hardware conversion
+// (round to nearest even, saturating at +-6): `hi` lands in bits 7..4, `lo` in
+// bits 3..0.  For every non-NaN fp32 input the code equals e2m1_encode's
+// (checked over all 2^32 bit patterns on the GPU by
+// qg_selftest_e2m1_cvt); NaN inputs are mapped to +0 by the caller, as
+// e2m1_encode does.
+__device__ __forceinline__ uint32_t e2m1x2_cvt(float hi, float lo) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}"
+      : "=r"(out)
+      : "f"(hi), "f"(lo));
+  return out;
+}
+
+// nvfp4_encode_block with the hardware e2m1 conversion (the requantising GEMM
+// epilogue's form): same scale and same codes, low nibble first; `bmax` is
+// the block's max |v| (NaN-free, as fmaxf drops NaN operands).
+__device__ __forceinline__ uint32_t nvfp4_encode_block_cvt(const float (&v)[16], float bmax,
+                                                           float inv_ts, uint32_t& lo,
+                                                           uint32_t& hi) {
+  const float namax = __fmul_rn(bmax, inv_ts);
+  const uint32_t sbits = e4m3_round_up(__fdiv_rn(namax, 6.0f));
+  const float bs = e4m3_decode_positive(sbits);
+  const float mult = bs > 0.0f ? __fdiv_rn(inv_ts, bs) : 0.0f;
+  lo = 0;
+  hi = 0;
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    float x0 = __fmul_rn(v[i], mult), x1 = __fmul_rn(v[i + 1], mult);
+    x0 = x0 == x0 ? x0 : 0.0f;  // NaN -> +0
+    x1 = x1 == x1 ? x1 : 0.0f;
+    const uint32_t byte = e2m1x2_cvt(x1, x0);
+    if (i < 8) lo |= byte << (4 * i);
+    else hi |= byte << (4 * (i - 8));
+  }
+  return sbits;
+}
+
 }  // namespace qg

@@ -26,6 +26,16 @@ struct GemmParams {
   int vec_ok;  // 16-byte vector stores are legal for every full 32-column run
   const float* a_ts;
   const float* b_ts;
+  // NVFP4 output (requantising epilogue, pair kernel): values [m][n/2] and
+  // one e4m3 scale per 16 columns in layout rq_layout (REF_LINEAR or an MMA
+  // order with rq_row_blocks x rq_sf_blocks chunks), decoded with the tensor
+  // scale *rq_ts; the output's amax is max-reduced into *rq_amax (optional).
+  uint8_t* rq_q;
+  uint8_t* rq_sf;
+  const float* rq_ts;
+  uint32_t* rq_amax;
+  int rq_layout;
+  int rq_row_blocks, rq_sf_blocks;
   uint32_t* status;
   uint64_t timeout_ns;
   // Diagnostics only (QG_DIAG_FLAGS; results are wrong when set): bit 0
@@ -74,7 +84,8 @@ int skinny_mma_n(int64_t m);
 
 cudaError_t launch_gemm_blockscaled(const GemmParams& p, bool fp4, bool out_bf16, int grid,
                                     cudaStream_t stream);
-cudaError_t launch_gemm_pair(const GemmParams& p, bool fp4, bool out_bf16, int grid,
+// out_kind: 0 fp32 C, 1 bf16 C, 2 NVFP4 output (rq_* fields; fp4 only).
+cudaError_t launch_gemm_pair(const GemmParams& p, bool fp4, int out_kind, int grid,
                              cudaStream_t stream);
 cudaError_t launch_gemm_solo(const GemmParams& p, bool fp4, bool out_bf16, int grid,
                              cudaStream_t stream);
@@ -96,6 +107,7 @@ cudaError_t launch_quantize_mxfp8(const void* x, bool bf16, int64_t rows, int64_
 cudaError_t launch_repack_nvfp4(const uint8_t* sq, const uint8_t* ssf, int src_layout,
                                 uint8_t* dq, uint8_t* dsf, int dst_layout, int64_t rows,
                                 int64_t k, cudaStream_t stream);
+cudaError_t launch_e2m1_cvt_selftest(unsigned long long* out, cudaStream_t stream);
 cudaError_t launch_wait_timeout_selftest(uint64_t timeout_ns, uint32_t* status,
                                          cudaStream_t stream);
 

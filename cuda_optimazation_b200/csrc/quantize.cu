@@ -254,6 +254,50 @@ cudaError_t launch_repack_nvfp4(const uint8_t* sq, const uint8_t* ssf, int src_l
   return cudaGetLastError();
 }
 
+// Exhaustive check of the hardware e2m1 conversion against e2m1_encode (the
+// bit-exact restatement of encode_e2m1_rn, e2m1_encode.cuh:18-44) over all
+// 2^32 fp32 bit patterns, each converted in both nibble positions.  out[0]:
+// mismatches on non-NaN inputs, out[1]: on NaN inputs, out[2]: the largest
+// mismatching non-NaN bit pattern + 1 (0 if none).
+__global__ void __launch_bounds__(256) e2m1_cvt_selftest_kernel(unsigned long long* out) {
+  unsigned long long bad = 0, bad_nan = 0, last = 0;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  for (uint64_t u = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+       u < (1ull << 32); u += stride) {
+    const float f = __uint_as_float(static_cast<uint32_t>(u));
+    const uint32_t want = e2m1_encode(f);
+    const uint32_t a = e2m1x2_cvt(f, 0.0f) >> 4;
+    const uint32_t b = e2m1x2_cvt(0.0f, f) & 0xfu;
+    if (a != want || b != want) {
+      if (f != f) {
+        ++bad_nan;
+      } else {
+        ++bad;
+        last = u + 1;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    bad += __shfl_xor_sync(0xffffffffu, bad, o);
+    bad_nan += __shfl_xor_sync(0xffffffffu, bad_nan, o);
+    const unsigned long long l = __shfl_xor_sync(0xffffffffu, last, o);
+    last = l > last ? l : last;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    if (bad) atomicAdd(&out[0], bad);
+    if (bad_nan) atomicAdd(&out[1], bad_nan);
+    if (last) atomicMax(&out[2], last);
+  }
+}
+
+cudaError_t launch_e2m1_cvt_selftest(unsigned long long* out, cudaStream_t stream) {
+  if (cudaMemsetAsync(out, 0, 3 * sizeof(unsigned long long), stream) != cudaSuccess)
+    return cudaGetLastError();
+  e2m1_cvt_selftest_kernel<<<num_sms() * 8, 256, 0, stream>>>(out);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_wait_timeout_selftest(uint64_t timeout_ns, uint32_t* status,
                                          cudaStream_t stream) {
   wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(timeout_ns, status);

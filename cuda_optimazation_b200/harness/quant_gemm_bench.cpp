@@ -19,7 +19,9 @@
 //     (GEMMquant_sm110/scripts/run_quant_gemm_1024.py:404-410).
 // Backends: nvfp4_q1_native_fp4_mainloop (the reference's planned slot,
 // run_quant_gemm_1024.py:37-43), mxfp8_q0_tcgen05_block_scaled,
-// nvfp4_skinny_q0 (decode GEMM, fused activation quantisation), all.
+// nvfp4_skinny_q0 (decode GEMM, fused activation quantisation),
+// nvfp4_q0_tc6_fused_epilogue (NVFP4 output requantised in the epilogue,
+// the reference's tc6 row), all.
 //
 // Inputs are seeded N(0,1) (std::mt19937_64, A: seed, B: seed ^ 0xbb67ae85),
 // quantised on the device by the library.  The check recomputes sampled
@@ -341,6 +343,136 @@ Row run_skinny(const Options& o) {
   return r;
 }
 
+// Host form of the NVFP4 block rule the requantising epilogue follows
+// (make_nvfp4_reference, GEMMsm110/include/requant/nvfp4_reference.cuh:76-112):
+// s = smallest e4m3 code >= max|x / ts| / 6, q = e2m1 round-to-nearest-even
+// of x * ((1/ts) / s), saturating at 6, NaN -> +0, sign kept.
+uint8_t host_e2m1(float x) {
+  if (std::isnan(x)) return 0;
+  const float a = std::fabs(x);
+  const uint8_t c = (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) +
+                    (a >= 3.5f) + (a > 5.0f);
+  return static_cast<uint8_t>((std::signbit(x) ? 8 : 0) | c);
+}
+uint8_t host_e4m3_up(float v) {
+  if (!(v > 0.0f)) return 0;
+  for (int c = 1; c < 0x7e; ++c)
+    if (e4m3(static_cast<uint8_t>(c)) >= v) return static_cast<uint8_t>(c);
+  return 0x7e;
+}
+// One row of n values -> n/2 bytes (first value in the high nibble) and n/16
+// scale bytes, under inverse tensor scale inv_ts.
+void host_requant_row(const float* x, int64_t n, float inv_ts, uint8_t* q, uint8_t* sf) {
+  for (int64_t b = 0; b < n / 16; ++b) {
+    float namax = 0.0f;
+    for (int i = 0; i < 16; ++i) namax = std::max(namax, std::fabs(x[b * 16 + i] * inv_ts));
+    const uint8_t s = host_e4m3_up(namax / 6.0f);
+    sf[b] = s;
+    const float bs = e4m3(s);
+    const float mult = bs > 0.0f ? inv_ts / bs : 0.0f;
+    for (int i = 0; i < 16; i += 2)
+      q[(b * 16 + i) / 2] = static_cast<uint8_t>((host_e2m1(x[b * 16 + i] * mult) << 4) |
+                                                 host_e2m1(x[b * 16 + i + 1] * mult));
+  }
+}
+
+// NVFP4 GEMM with the NVFP4 requantisation fused into the epilogue
+// (nvfp4_q0_tc6_fused_epilogue, the reference's tc6 row,
+// run_quant_gemm_1024.py:28-35).  The output tensor scale comes from the fp32
+// output (amax / 2688), handed to the kernel as tc6 is handed its inverse
+// (GEMMsm110/src/main.cu:2379-2390).  Pass rule as the reference's
+// benchmark_tc6_kernel (main.cu:150-223): over the sampled rows, the
+// reconstruction rmse <= 1.1 x that of the host quantisation of the exact
+// rows + 1e-6 and max |err| <= 1.25 x + 1e-5; bit_exact (bytes equal to the
+// host rule applied to the device's fp32 output rows) is required as well.
+Row run_requant(const Options& o) {
+  const int64_t m = o.m, n = o.n, k = o.k;
+  auto ha = normal(m * k, o.seed), hb = normal(n * k, o.seed ^ 0xbb67ae85ull);
+  float *da = static_cast<float*>(dalloc(m * k * 4)), *db = static_cast<float*>(dalloc(n * k * 4));
+  CHECK_CUDA(cudaMemcpy(da, ha.data(), m * k * 4, cudaMemcpyHostToDevice));
+  CHECK_CUDA(cudaMemcpy(db, hb.data(), n * k * 4, cudaMemcpyHostToDevice));
+  void *aq = dalloc(m * k / 2), *asf = dalloc(qg_scale_bytes(m, k, 16));
+  void *bq = dalloc(n * k / 2), *bsf = dalloc(qg_scale_bytes(n, k, 16));
+  float *ats = static_cast<float*>(dalloc(4)), *bts = static_cast<float*>(dalloc(4));
+  void* ws = dalloc(qg_quantize_workspace_bytes());
+  CHECK_QG(qg_quantize_nvfp4(da, QG_DTYPE_F32, m, k, QG_LAYOUT_MMA, aq, asf, ats, ws, nullptr));
+  CHECK_QG(qg_quantize_nvfp4(db, QG_DTYPE_F32, n, k, QG_LAYOUT_MMA, bq, bsf, bts, ws, nullptr));
+  uint32_t* status = static_cast<uint32_t*>(dalloc(4));
+  CHECK_CUDA(cudaMemset(status, 0, 4));
+  // The fp32 output once (untimed): tensor scale and the bit-exact check.
+  void* dc = dalloc(m * n * 4);
+  CHECK_QG(qg_gemm_nvfp4(aq, asf, ats, bq, bsf, bts, dc, QG_DTYPE_F32, m, n, k, n, QG_LAYOUT_MMA,
+                         status, nullptr));
+  const std::vector<float> c = fetch_c(dc, m * n, false);
+  float amax = 0.0f;
+  for (float v : c) amax = std::max(amax, std::fabs(v));
+  const float ts = amax > 0.0f ? amax / 2688.0f : 1.0f;
+  float* dts = static_cast<float*>(dalloc(4));
+  CHECK_CUDA(cudaMemcpy(dts, &ts, 4, cudaMemcpyHostToDevice));
+  void *oq = dalloc(m * n / 2), *osf = dalloc(m * n / 16);
+  Row r;
+  r.backend = "nvfp4_q0_tc6_fused_epilogue";
+  r.version = "tcgen05 mxf4nvf4 GEMM + NVFP4 requant epilogue (B200)";
+  r.precision = "nvfp4->nvfp4";
+  r.ms = time_launches([&] {
+    CHECK_QG(qg_gemm_nvfp4_requant(aq, asf, ats, bq, bsf, bts, dts, oq, osf, QG_LAYOUT_REF_LINEAR,
+                                   nullptr, m, n, k, QG_LAYOUT_MMA, status, nullptr));
+  }, o.iterations);
+  CHECK_QG(qg_read_status(status, nullptr, nullptr));
+  r.gflops = 2.0 * m * n * k / (r.ms * 1e6);
+  std::vector<uint8_t> gq(m * n / 2), gsf(m * n / 16);
+  CHECK_CUDA(cudaMemcpy(gq.data(), oq, gq.size(), cudaMemcpyDeviceToHost));
+  CHECK_CUDA(cudaMemcpy(gsf.data(), osf, gsf.size(), cudaMemcpyDeviceToHost));
+  auto A = fetch_nvfp4(aq, asf, ats, m, k), B = fetch_nvfp4(bq, bsf, bts, n, k);
+  const float inv_ts = 1.0f / ts;
+  const int samples = static_cast<int>(std::min<int64_t>(m, 16));
+  size_t mismatches = 0;
+  double se_got = 0, se_ref = 0, se_exact = 0, max_got = 0, max_ref = 0;
+  std::vector<float> exact(n);
+  std::vector<uint8_t> hq(n / 2), hsf(n / 16), eq(n / 2), esf(n / 16);
+  const int64_t sfk = k / 16;
+  for (int s = 0; s < samples; ++s) {
+    const int64_t row = (static_cast<int64_t>(s) * 131) % m;
+    host_requant_row(&c[row * n], n, inv_ts, hq.data(), hsf.data());
+    for (int64_t i = 0; i < n / 2; ++i) mismatches += hq[i] != gq[row * n / 2 + i];
+    for (int64_t i = 0; i < n / 16; ++i) mismatches += hsf[i] != gsf[row * n / 16 + i];
+    for (int64_t col = 0; col < n; ++col) {
+      double sum = 0.0;
+      for (int64_t kk = 0; kk < k; ++kk)
+        sum += (static_cast<double>(A.v[row * k + kk]) * A.s[row * sfk + kk / 16]) *
+               (static_cast<double>(B.v[col * k + kk]) * B.s[col * sfk + kk / 16]);
+      exact[col] = static_cast<float>(sum) * (A.ts * B.ts);
+    }
+    host_requant_row(exact.data(), n, inv_ts, eq.data(), esf.data());
+    for (int64_t col = 0; col < n; ++col) {
+      const uint8_t gb = gq[row * n / 2 + col / 2], eb = eq[col / 2];
+      const int sh = (col & 1) ? 0 : 4;
+      const double got = e2m1((gb >> sh) & 15) * e4m3(gsf[row * n / 16 + col / 16]) * ts;
+      const double ref = e2m1((eb >> sh) & 15) * e4m3(esf[col / 16]) * ts;
+      const double eg = got - exact[col], er = ref - exact[col];
+      se_got += eg * eg;
+      se_ref += er * er;
+      se_exact += static_cast<double>(exact[col]) * exact[col];
+      max_got = std::max(max_got, std::fabs(eg));
+      max_ref = std::max(max_ref, std::fabs(er));
+    }
+  }
+  const double cnt = static_cast<double>(samples) * n;
+  const double rmse_got = std::sqrt(se_got / cnt), rmse_ref = std::sqrt(se_ref / cnt);
+  r.matched = rmse_got <= rmse_ref * 1.10 + 1e-6 && max_got <= max_ref * 1.25 + 1e-5 &&
+              mismatches == 0;
+  r.frob = std::sqrt(se_got / std::max(se_exact, 1e-300));  // relative error of the NVFP4 output
+  std::cout << "nvfp4_q0_tc6_fused_epilogue: tensor_scale=" << ts
+            << ", bit_exact=" << (mismatches == 0) << ", mismatches=" << mismatches
+            << ", rmse=" << rmse_got << " (ref=" << rmse_ref << "), max_abs_error=" << max_got
+            << " (ref=" << max_ref << ")\n";
+  for (void* p : {static_cast<void*>(da), static_cast<void*>(db), aq, asf, bq, bsf,
+                  static_cast<void*>(ats), static_cast<void*>(bts), ws, dc,
+                  static_cast<void*>(status), static_cast<void*>(dts), oq, osf})
+    cudaFree(p);
+  return r;
+}
+
 void write_row(std::ofstream& csv, const Row& r, const Options& o) {
   const double peak_tflops = r.precision.rfind("mxfp8", 0) == 0 ? 4500.0 : 9000.0;
   std::cout << r.backend << ": " << r.ms << " ms, " << r.gflops << " GFLOP/s, matched="
@@ -359,7 +491,7 @@ void usage(const char* p) {
             << "       " << p << " M N K backend [--seed S] [--out-dtype bf16|fp32]\n"
             << "       " << p << " --m=M --n=N --k=K [--iterations=I] [--swizzle=S]\n"
             << "backends: all|nvfp4_q1_native_fp4_mainloop|mxfp8_q0_tcgen05_block_scaled|"
-               "nvfp4_skinny_q0\n";
+               "nvfp4_skinny_q0|nvfp4_q0_tc6_fused_epilogue\n";
 }
 
 bool parse(int argc, char** argv, Options* o) {
@@ -398,7 +530,8 @@ bool parse(int argc, char** argv, Options* o) {
   const std::string& b = o->backend;
   return o->m > 0 && o->n > 0 && o->k > 0 &&
          (b == "all" || b == "nvfp4_q1_native_fp4_mainloop" ||
-          b == "mxfp8_q0_tcgen05_block_scaled" || b == "nvfp4_skinny_q0");
+          b == "mxfp8_q0_tcgen05_block_scaled" || b == "nvfp4_skinny_q0" ||
+          b == "nvfp4_q0_tc6_fused_epilogue");
 }
 
 }  // namespace
@@ -438,6 +571,16 @@ int main(int argc, char** argv) {
     Row r = run_mxfp8(o);
     write_row(csv, r, o);
     all_ok &= r.matched;
+  }
+  if (want("nvfp4_q0_tc6_fused_epilogue")) {
+    if (o.n % 16 != 0) {
+      std::cerr << "nvfp4_q0_tc6_fused_epilogue needs N % 16 == 0\n";
+      all_ok = false;
+    } else {
+      Row r = run_requant(o);
+      write_row(csv, r, o);
+      all_ok &= r.matched;
+    }
   }
   if (want("nvfp4_skinny_q0")) {
     Row r = run_skinny(o);

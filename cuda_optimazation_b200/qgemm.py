@@ -48,6 +48,8 @@ SIGNATURES = {
     "qg_repack_nvfp4": (_I32, [_VP, _VP, _I32, _VP, _VP, _I32, _I64, _I64, _VP]),
     "qg_gemm_nvfp4": (_I32, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64, _I64,
                              _I32, _VP, _VP]),
+    "qg_gemm_nvfp4_requant": (_I32, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I32, _VP,
+                                     _I64, _I64, _I64, _I32, _VP, _VP]),
     "qg_gemm_mxfp8": (_I32, [_VP, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64, _I64, _I32, _VP,
                              _VP]),
     "qg_gemm_nvfp4_skinny": (_I32, [_VP, _I32, _I64, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64,
@@ -59,6 +61,7 @@ SIGNATURES = {
     "qg_ipc_import": (_I32, [_VP, _VP]),
     "qg_ipc_close": (_I32, [_VP]),
     "qg_read_status": (_I32, [_VP, _VP, _VP]),
+    "qg_selftest_e2m1_cvt": (_I32, [_VP, _VP]),
     "qg_selftest_wait_timeout": (_I32, [_U64, _VP, _VP]),
 }
 
@@ -228,6 +231,45 @@ def block_scaled_gemm(a, b, out_dtype: torch.dtype = torch.bfloat16,
         gemm_mxfp8_raw(a.quantized, a.block_scales, b.quantized, b.block_scales, out, m, n, k,
                        a.layout, status, stream)
     return out
+
+
+def gemm_nvfp4_requant_raw(a_q, a_sf, a_ts, b_q, b_sf, b_ts, out_ts, out_q, out_sf, m, n, k,
+                           out_layout=LAYOUT_REF_LINEAR, sf_layout=LAYOUT_MMA,
+                           out_amax: Optional[torch.Tensor] = None,
+                           status: Optional[torch.Tensor] = None, stream=None) -> None:
+    """NVFP4 output of A . B^T into preallocated uint8 tensors out_q (m*n/2
+    bytes) and out_sf (m*n/16 bytes, or the MMA layout's size)."""
+    rc = lib().qg_gemm_nvfp4_requant(a_q.data_ptr(), a_sf.data_ptr(), _ptr(a_ts), b_q.data_ptr(),
+                                     b_sf.data_ptr(), _ptr(b_ts), _ptr(out_ts), out_q.data_ptr(),
+                                     out_sf.data_ptr(), out_layout, _ptr(out_amax), m, n, k,
+                                     sf_layout, _ptr(status), _stream(stream))
+    _check(rc, "qg_gemm_nvfp4_requant")
+
+
+def gemm_nvfp4_requant(a: Nvfp4Result, b: Nvfp4Result, out_ts: torch.Tensor,
+                       out_layout: int = LAYOUT_REF_LINEAR,
+                       out_amax: Optional[torch.Tensor] = None,
+                       status: Optional[torch.Tensor] = None, stream=None) -> Nvfp4Result:
+    """NVFP4 GEMM whose output is requantised to NVFP4 in the epilogue (the
+    tc6 fused epilogue, GEMMsm110/include/backends/tc6_nvfp4.cuh:460-503).
+    ``out_ts`` is the output's tensor scale (float32[1] on the device), given
+    by the caller as tc6 takes its inverse; the result is an ``Nvfp4Result``
+    of m rows and n columns in ``out_layout``.  ``out_amax`` (int32[1] on the
+    device, zeroed by the caller) receives the float bit pattern of the
+    output's amax."""
+    if a.k != b.k or a.layout != b.layout:
+        raise ValueError("operands must share K and layout")
+    m, n, k = a.rows, b.rows, a.k
+    dev = a.quantized.device
+    q = torch.empty(m * n // 2, dtype=torch.uint8, device=dev)
+    if out_layout == LAYOUT_REF_LINEAR:
+        sf = torch.empty(m * n // 16, dtype=torch.uint8, device=dev)
+    else:
+        sf = torch.empty(sm1xx_scale_storage_size(m, n, 16), dtype=torch.uint8, device=dev)
+    gemm_nvfp4_requant_raw(a.quantized, a.block_scales, a.tensor_scale, b.quantized,
+                           b.block_scales, b.tensor_scale, out_ts, q, sf, m, n, k, out_layout,
+                           a.layout, out_amax, status, stream)
+    return Nvfp4Result(q, sf, out_ts, m, n, out_layout)
 
 
 def skinny_workspace(m: int, n: int, k: int, device) -> torch.Tensor:

@@ -142,6 +142,31 @@ int qg_gemm_nvfp4(const void* a_q, const void* a_sf, const float* a_ts, const vo
                   const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
                   int64_t k, int64_t ldc, int sf_layout, uint32_t* status, qg_stream_t stream);
 
+/* NVFP4 GEMM whose output is NVFP4: the epilogue requantises each
+ * 16-column block of every output row to e2m1 values plus one e4m3 scale,
+ * instead of storing bf16 / fp32.  The element values are the fp32 numbers
+ * qg_gemm_nvfp4 would store (alpha = a_ts * b_ts applied), quantised with
+ * the steps of make_nvfp4_reference (nvfp4_reference.cuh:76-112) under the
+ * caller's tensor scale *out_ts (device float; NULL = 1.0): for every block,
+ * s = e4m3_round_up(max|v / ts| / 6), q = e2m1(v * ((1/ts) / s)).  The
+ * result is therefore bit-identical to qg_quantize_nvfp4's block step
+ * applied to qg_gemm_nvfp4's fp32 output with the same tensor scale.
+ * out_q receives m*n/2 bytes, out_sf the scales in out_layout
+ * (QG_LAYOUT_REF_LINEAR: m*n/16 bytes in flat order, high nibble first, the
+ * reference's layout; an MMA layout: qg_scale_bytes(m, n, 16) bytes, low
+ * nibble first, so the output feeds the next GEMM as its A operand with
+ * K = n).  out_amax (device uint32, may be NULL) is max-reduced with the
+ * bit pattern of max|v| over the outputs (a float; the caller zeroes it), so
+ * the next call's tensor scale can be amax / 2688.  n % 16 == 0, out_q 16-B
+ * and out_sf 4-B aligned; other rules as qg_gemm_nvfp4.
+ * Replaces the tc6 fused NVFP4 epilogue (Tc6Runner and store_tile,
+ * GEMMsm110/include/backends/tc6_nvfp4.cuh:460-503, :561-619), which takes
+ * the inverse tensor scale as an argument in the same way. */
+int qg_gemm_nvfp4_requant(const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
+                          const void* b_sf, const float* b_ts, const float* out_ts, void* out_q,
+                          void* out_sf, int out_layout, uint32_t* out_amax, int64_t m, int64_t n,
+                          int64_t k, int sf_layout, uint32_t* status, qg_stream_t stream);
+
 /* MXFP8 x MXFP8 block-scaled GEMM on tcgen05 (kind::mxf8f6f4, ue8m0 per 32
  * K): C = sum_k a*sfa*b*sfb.  a_q / b_q are e4m3 bytes (M*K, N*K), K % 32
  * == 0.  Replaces the unscaled FP8 stages fp8_q0..q8
@@ -210,6 +235,15 @@ int qg_ipc_close(void* dptr);
  * QG_OK, QG_ERR_TIMEOUT or QG_ERR_CUDA; *device_code (may be NULL) gets the
  * raw device code. */
 int qg_read_status(uint32_t* status, uint32_t* device_code, qg_stream_t stream);
+
+/* Exhaustive self test of the hardware e2m1 conversion that the
+ * requantising GEMM epilogue uses (cvt.rn.satfinite.e2m1x2.f32) against the
+ * library's restatement of the reference encoder encode_e2m1_rn
+ * (GEMMsm110/include/requant/e2m1_encode.cuh:18-44), over all 2^32 fp32 bit
+ * patterns.  out (device, 3 x uint64, written on `stream`): [0] mismatches on
+ * non-NaN inputs (must be 0), [1] mismatches on NaN inputs (the epilogue maps
+ * NaN to +0 itself), [2] largest mismatching non-NaN pattern + 1. */
+int qg_selftest_e2m1_cvt(unsigned long long* out, qg_stream_t stream);
 
 /* Failure-path self test: launches one CTA that waits on an mbarrier no one
  * arrives on, bounded by `timeout_ns`, and records the timeout in *status.

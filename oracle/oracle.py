@@ -52,6 +52,7 @@ class Oracle:
             "qgo_scale_offset": (_I64, [_I64, _I64, _I64, _I64, _I32, _I32]),
             "qgo_scale_storage_size": (_I64, [_I64, _I64, _I32]),
             "qgo_nvfp4_reference": (None, [_f32p, _I64, _u8p, _u8p, _fp]),
+            "qgo_nvfp4_blocks_with_ts": (None, [_f32p, _I64, _F32, _u8p, _u8p]),
             "qgo_nvfp4_quantize_mma": (None, [_f32p, _I64, _I64, _I32, _u8p, _u8p, _fp]),
             "qgo_mxfp8_quantize": (None, [_f32p, _I64, _I64, _I32, _u8p, _u8p]),
             "qgo_block_scaled_gemm": (None, [_f32p, _f32p, _f32p, _f32p, _I64, _I64, _I64, _I32,
@@ -86,6 +87,32 @@ class Oracle:
         ts = ctypes.c_float(0)
         self.L.qgo_nvfp4_reference(x, x.size, q, sf, ctypes.byref(ts))
         return q, sf, ts.value
+
+    def nvfp4_with_ts(self, x: np.ndarray, ts: float):
+        """O1's block step under a given tensor scale (REF_LINEAR bytes)."""
+        x = np.ascontiguousarray(x, np.float32).ravel()
+        nb = (x.size + 15) // 16
+        q = np.zeros(nb * 8, np.uint8)
+        sf = np.zeros(nb, np.uint8)
+        self.L.qgo_nvfp4_blocks_with_ts(x, x.size, float(ts), q, sf)
+        return q, sf
+
+    @staticmethod
+    def linear_to_mma(q: np.ndarray, sf: np.ndarray, rows: int, k: int, order: int = 0):
+        """REF_LINEAR NVFP4 bytes of a rows x k matrix -> MMA layout (low
+        nibble first, scales at the L1 offsets of `order`; padded slots 0)."""
+        q = np.ascontiguousarray(q, np.uint8)
+        qm = ((q >> 4) | (q << 4)).astype(np.uint8)
+        sfk = k // 16
+        row_blocks, sf_blocks = (rows + 127) // 128, (sfk + 3) // 4
+        r = np.repeat(np.arange(rows, dtype=np.int64), sfk)
+        c = np.tile(np.arange(sfk, dtype=np.int64), rows)
+        chunk = (c // 4) * row_blocks + r // 128 if order == 0 else (r // 128) * sf_blocks + c // 4
+        w = r % 128
+        off = chunk * 512 + (w % 32) * 16 + (w // 32) * 4 + c % 4
+        out = np.zeros(row_blocks * sf_blocks * 512, np.uint8)
+        out[off] = np.asarray(sf, np.uint8)[: rows * sfk]
+        return qm, out
 
     def nvfp4_mma(self, x: np.ndarray, order: int = 0):
         rows, k = x.shape

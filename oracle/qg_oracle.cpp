@@ -160,11 +160,20 @@ int64_t qgo_scale_storage_size(int64_t mn_extent, int64_t k_extent, int sv) {
 // make_nvfp4_reference over a flat tensor of n elements: nvfp4_reference.cuh:76-112.
 // q gets ceil(n_pad/2) bytes (high nibble first), sf gets n_pad/16 bytes
 // (linear order), *ts the tensor scale.
+void qgo_nvfp4_blocks_with_ts(const float* x, int64_t n, float tscale, uint8_t* q, uint8_t* sf);
+
 void qgo_nvfp4_reference(const float* x, int64_t n, uint8_t* q, uint8_t* sf, float* ts) {
   float amax = 0.0f;
   for (int64_t i = 0; i < n; ++i) amax = std::max(amax, std::fabs(x[i]));
   const float tscale = amax > 0.0f ? amax / (kE4M3Max * kE2M1Max) : 1.0f;
   *ts = tscale;
+  qgo_nvfp4_blocks_with_ts(x, n, tscale, q, sf);
+}
+
+// The block loop of O1 (nvfp4_reference.cuh:84-111) under a given tensor
+// scale: what the tc6 epilogue computes from the inverse tensor scale it is
+// handed (tc6_nvfp4.cuh:460-503, Tc6Runner argument at main.cu:2388-2390).
+void qgo_nvfp4_blocks_with_ts(const float* x, int64_t n, float tscale, uint8_t* q, uint8_t* sf) {
   const float inv_ts = 1.0f / tscale;
   const int64_t blocks = (n + kNvfp4Block - 1) / kNvfp4Block;
   for (int64_t b = 0; b < blocks; ++b) {

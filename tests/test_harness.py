@@ -27,7 +27,8 @@ def test_bad_arguments_exit_nonzero(binary):
 @pytest.mark.parametrize("args", [["256", "all"], ["1024", "all"],
                                   ["512", "1024", "768", "nvfp4_q1_native_fp4_mainloop",
                                    "--out-dtype", "bf16"],
-                                  ["64", "4096", "2048", "nvfp4_skinny_q0"]])
+                                  ["64", "4096", "2048", "nvfp4_skinny_q0"],
+                                  ["512", "768", "1024", "nvfp4_q0_tc6_fused_epilogue"]])
 def test_csv_rows_matched(binary, tmp_path, args):
     r = subprocess.run([str(binary), *args], capture_output=True, text=True, cwd=tmp_path,
                        timeout=600)

@@ -180,3 +180,18 @@ def test_mxfp8_oracle_properties(oracle):
     amax = np.abs(x.reshape(64, 8, 32)).max(axis=2)
     e = np.floor(np.log2(amax)) - 8
     assert np.array_equal(sf.reshape(64, 8).astype(np.int64), (e + 127).astype(np.int64))
+
+
+def test_blocks_with_ts_and_linear_to_mma(oracle):
+    """O1's block step under a given tensor scale (the tc6 requant rule)
+    equals O1 when handed O1's own tensor scale, and the REF_LINEAR -> MMA
+    conversion used by the requant parity tests equals the oracle's direct
+    MMA quantizer."""
+    x = oracle.normal(130 * 64, 5).reshape(130, 64)
+    q, sf, ts = oracle.nvfp4_reference(x)
+    q2, sf2 = oracle.nvfp4_with_ts(x, ts)
+    assert np.array_equal(q, q2) and np.array_equal(sf, sf2)
+    for order in (0, 1):
+        qm, sm, _ = oracle.nvfp4_mma(x, order)
+        a, b = oracle.linear_to_mma(q, sf, 130, 64, order)
+        assert np.array_equal(a, qm) and np.array_equal(b, sm)
