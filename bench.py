@@ -39,6 +39,8 @@ WORKLOADS = {
     # the same GEMM with the output requantised to NVFP4 in the epilogue
     # (the reference's tc6 fused epilogue; SURVEY next-step f1)
     "nvfp4_8192_requant": dict(fmt="nvfp4", m=8192, n=8192, k=8192, out="nvfp4", cfg=1),
+    # MXFP4 (e2m1, ue8m0 per 32 K; the reference's CUTLASS 72a rows) at 8192^3
+    "mxfp4_8192": dict(fmt="mxfp4", m=8192, n=8192, k=8192, out="bf16", cfg=1),
     "nvfp4_256": dict(fmt="nvfp4", m=256, n=256, k=256, out="fp32", cfg=0),
     "mxfp8_ffn": dict(fmt="mxfp8", m=4096, n=14336, k=4096, out="bf16", cfg=2),
     "colpar": dict(fmt="nvfp4", m=16384, n=53248, k=8192, out="bf16", cfg=4),
@@ -189,6 +191,8 @@ def make_operands(q, torch, w, m_rows, n_rows, dev, gen, b_std=1.0):
     b = torch.randn(n_rows, k, generator=gen, device=dev, dtype=torch.float32) * b_std
     if w["fmt"] == "nvfp4":
         A, B = q.make_nvfp4(a), q.make_nvfp4(b)
+    elif w["fmt"] == "mxfp4":
+        A, B = q.make_mxfp4(a), q.make_mxfp4(b)
     else:
         A, B = q.make_mxfp8(a), q.make_mxfp8(b)
     del a, b
@@ -214,7 +218,7 @@ def run_ours(args, w, rank, world, dist, torch):
     gen = torch.Generator(device=dev)
     b_std = 0.02 if w["fmt"] == "mxfp8" else 1.0
     # Operand sets rotate between steps so no step finds its inputs in L2.
-    set_bytes = (m + n) * k * (0.5 if w["fmt"] == "nvfp4" else 1.0)
+    set_bytes = (m + n) * k * (1.0 if w["fmt"] == "mxfp8" else 0.5)
     out_bytes = m * n * {"bf16": 2, "fp32": 4, "nvfp4": 0.5625}[w["out"]]
     nsets = 1 if set_bytes + out_bytes > 3 * 126e6 else 3
     sets = []
@@ -251,6 +255,8 @@ def run_ours(args, w, rank, world, dist, torch):
                                      status=status)
         elif w["fmt"] == "nvfp4":
             q.gemm_nvfp4_raw(aq, asf, ats, bq, bsf, bts, dst, m, n, k, layout, status)
+        elif w["fmt"] == "mxfp4":
+            q.gemm_mxfp4_raw(aq, asf, bq, bsf, dst, m, n, k, layout, status)
         else:
             q.gemm_mxfp8_raw(aq, asf, bq, bsf, dst, m, n, k, layout, status)
 
@@ -420,7 +426,7 @@ def run_ours(args, w, rank, world, dist, torch):
     if rank != 0:
         return None
     pk = peaks()
-    ratio = 4.0 if w["fmt"] == "nvfp4" else 2.0
+    ratio = 2.0 if w["fmt"] == "mxfp8" else 4.0
     peak_tflops = pk["bf16_tflops"] * ratio
     avg_launch_ms = statistics.mean(launch_ms)
     achieved = flops_rank / (avg_launch_ms * 1e-3) / 1e12

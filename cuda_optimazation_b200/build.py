@@ -83,6 +83,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
 
 HARNESS_SRC = PKG / "harness" / "quant_gemm_bench.cpp"
 HARNESS_BIN = PKG / "bin" / "quant_gemm_sm110_bench"
+HARNESS_MXFP4_BIN = PKG / "bin" / "cutlass_72a_mxfp4_bf16_b200"
 
 
 def build_harness() -> Path:
@@ -96,6 +97,10 @@ def build_harness() -> Path:
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)
         raise RuntimeError("harness build failed")
+    # The same binary under the MXFP4 runner's name: its --m/--n/--k form
+    # then runs MXFP4 (what run_quant_gemm_1024.py's --cutlass-mxfp4-bin
+    # points at).
+    shutil.copy2(HARNESS_BIN, HARNESS_MXFP4_BIN)
     return HARNESS_BIN
 
 

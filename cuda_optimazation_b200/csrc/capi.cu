@@ -163,11 +163,13 @@ struct Requant {
   int layout = 0;
 };
 
-int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
+// fmt: 0 MXFP8, 1 NVFP4, 2 MXFP4 (pair kernel only).
+int gemm_common(int fmt, const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
                 const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
                 int64_t k, int64_t ldc, int sf_layout, uint32_t* status, cudaStream_t stream,
                 const Gather& gather = Gather(), const Requant& requant = Requant()) {
   const bool rq = requant.q != nullptr;
+  const bool fp4 = fmt != 0;
   if (!a_q || !a_sf || !b_q || !b_sf || (!c && !rq)) return QG_ERR_ARG;
   if (!rq && c_dtype != QG_DTYPE_F32 && c_dtype != QG_DTYPE_BF16) return QG_ERR_DTYPE;
   if (sf_layout != QG_LAYOUT_MMA && sf_layout != QG_LAYOUT_MMA_KMAJOR) return QG_ERR_LAYOUT;
@@ -179,8 +181,8 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
   if (row_bytes % 16 != 0) return QG_ERR_ALIGN;
   if (int d = check_device()) return d;
   if (!encode_fn()) return QG_ERR_CUDA;
-  const int sv = fp4 ? 16 : 32;
-  const int variant = (gather.nranks > 0 || rq) ? 1 : gemm_variant(fp4, m);
+  const int sv = fmt == 1 ? 16 : 32;
+  const int variant = (gather.nranks > 0 || rq || fmt == 2) ? 1 : gemm_variant(fp4, m);
   const bool pair = variant == 1;
   // Tile of one scheduling unit (a CTA pair: 256 x 256; one CTA: 128 x 256)
   // and the rows each CTA's TMA boxes cover.
@@ -188,7 +190,7 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
   const int tn = pair ? pair_tile_n() : gemm_tile_n();
   const int box_a = pair ? tm / 2 : tm;
   const int box_b = pair ? tn / 2 : tn;
-  const int chunks = gemm_sf_chunks_per_stage(fp4);
+  const int chunks = pair ? pair_sf_chunks_per_stage(fmt) : gemm_sf_chunks_per_stage(fp4);
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
   if (!make_operand_map(&p.tm_a, a_q, m, row_bytes, box_a)) return QG_ERR_CUDA;
@@ -228,8 +230,8 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
     p.rq_row_blocks = static_cast<int>((m + 127) / 128);
     p.rq_sf_blocks = static_cast<int>((n / 16 + 3) / 4);
   }
-  p.a_ts = fp4 ? a_ts : nullptr;
-  p.b_ts = fp4 ? b_ts : nullptr;
+  p.a_ts = fmt == 1 ? a_ts : nullptr;
+  p.b_ts = fmt == 1 ? b_ts : nullptr;
   p.status = status;
   p.timeout_ns = default_timeout_ns();
   p.diag = diag_flags();
@@ -238,7 +240,7 @@ int gemm_common(bool fp4, const void* a_q, const void* a_sf, const float* a_ts, 
   if (pair) {
     const int64_t pairs = num_sms() / 2;
     const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
-    e = launch_gemm_pair(p, fp4, rq ? 2 : (c_dtype == QG_DTYPE_BF16 ? 1 : 0), grid, stream);
+    e = launch_gemm_pair(p, fmt, rq ? 2 : (c_dtype == QG_DTYPE_BF16 ? 1 : 0), grid, stream);
   } else {
     const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
     e = variant == 2 ? launch_gemm_blockscaled(p, fp4, c_dtype == QG_DTYPE_BF16, grid, stream)
@@ -362,7 +364,7 @@ int qg_repack_nvfp4(const void* src_q, const void* src_sf, int src_layout, void*
 int qg_gemm_nvfp4(const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
                   const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
                   int64_t k, int64_t ldc, int sf_layout, uint32_t* status, qg_stream_t stream) {
-  return gemm_common(true, a_q, a_sf, a_ts, b_q, b_sf, b_ts, c, c_dtype, m, n, k, ldc, sf_layout,
+  return gemm_common(1, a_q, a_sf, a_ts, b_q, b_sf, b_ts, c, c_dtype, m, n, k, ldc, sf_layout,
                      status, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -390,14 +392,41 @@ int qg_gemm_nvfp4_requant(const void* a_q, const void* a_sf, const float* a_ts, 
   r.ts = out_ts;
   r.amax = out_amax;
   r.layout = out_layout;
-  return gemm_common(true, a_q, a_sf, a_ts, b_q, b_sf, b_ts, nullptr, QG_DTYPE_F32, m, n, k, n,
+  return gemm_common(1, a_q, a_sf, a_ts, b_q, b_sf, b_ts, nullptr, QG_DTYPE_F32, m, n, k, n,
                      sf_layout, status, s, Gather(), r);
+}
+
+int qg_gemm_mxfp4(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, void* c,
+                  int c_dtype, int64_t m, int64_t n, int64_t k, int64_t ldc, int sf_layout,
+                  uint32_t* status, qg_stream_t stream) {
+  return gemm_common(2, a_q, a_sf, nullptr, b_q, b_sf, nullptr, c, c_dtype, m, n, k, ldc,
+                     sf_layout, status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int qg_quantize_mxfp4(const void* x, int x_dtype, int64_t rows, int64_t k, int layout, void* q,
+                      void* sf, qg_stream_t stream) {
+  if (!x || !q || !sf) return QG_ERR_ARG;
+  if (x_dtype != QG_DTYPE_F32 && x_dtype != QG_DTYPE_BF16) return QG_ERR_DTYPE;
+  if (layout < QG_LAYOUT_REF_LINEAR || layout > QG_LAYOUT_MMA_KMAJOR) return QG_ERR_LAYOUT;
+  if (rows < 1 || k < 32 || (k % 32) != 0) return QG_ERR_SHAPE;
+  if (!aligned16(x) || !aligned16(q)) return QG_ERR_ALIGN;
+  if (int d = check_device()) return d;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (layout != QG_LAYOUT_REF_LINEAR && ((rows % 128) != 0 || ((k / 32) % 4) != 0)) {
+    if (cudaMemsetAsync(sf, 0, static_cast<size_t>(qg_scale_bytes(rows, k, 32)), s) != cudaSuccess)
+      return QG_ERR_CUDA;
+  }
+  return launch_quantize_mxfp4(x, x_dtype == QG_DTYPE_BF16, rows, k, layout,
+                               static_cast<uint8_t*>(q), static_cast<uint8_t*>(sf),
+                               s) == cudaSuccess
+             ? QG_OK
+             : QG_ERR_CUDA;
 }
 
 int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, void* c,
                   int c_dtype, int64_t m, int64_t n, int64_t k, int64_t ldc, int sf_layout,
                   uint32_t* status, qg_stream_t stream) {
-  return gemm_common(false, a_q, a_sf, nullptr, b_q, b_sf, nullptr, c, c_dtype, m, n, k, ldc,
+  return gemm_common(0, a_q, a_sf, nullptr, b_q, b_sf, nullptr, c, c_dtype, m, n, k, ldc,
                      sf_layout, status, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -498,7 +527,7 @@ int qg_gemm_nvfp4_gather(const void* a_q, const void* a_sf, const float* a_ts, c
   g.c_ranks = c_ranks;
   g.nranks = nranks;
   g.col0 = col0;
-  return gemm_common(true, a_q, a_sf, a_ts, b_q, b_sf, b_ts, c_ranks[0], QG_DTYPE_BF16, m,
+  return gemm_common(1, a_q, a_sf, a_ts, b_q, b_sf, b_ts, c_ranks[0], QG_DTYPE_BF16, m,
                      n_local, k, ldc, sf_layout, status, reinterpret_cast<cudaStream_t>(stream), g);
 }
 

@@ -45,7 +45,12 @@
 
 namespace qg {
 
-template <bool kFp4>
+// Operand formats of the pair kernel.
+constexpr int kFmtMxfp8 = 0;  // e4m3, ue8m0 per 32 K
+constexpr int kFmtNvfp4 = 1;  // e2m1, ue4m3 per 16 K (+ fp32 tensor scales)
+constexpr int kFmtMxfp4 = 2;  // e2m1, ue8m0 per 32 K
+
+template <int kFmt>
 struct PairCfg {
   static constexpr int kBM = 128;       // rows of A per CTA (256 per pair)
   static constexpr int kBN = 256;       // N of the pair tile
@@ -53,7 +58,9 @@ struct PairCfg {
   static constexpr int kBKBytes = 128;  // K bytes per stage (one SWIZZLE_128B row)
   static constexpr int kStages = 5;
   static constexpr int kMmaPerStage = 4;
-  static constexpr int kSfChunks = kFp4 ? 4 : 1;  // 512-B chunks along K per 128 rows
+  // 512-B scale chunks (4 scales per row) along K per 128 rows per stage:
+  // 256 K elements (fp4) or 128 (fp8) at 16 or 32 elements per scale.
+  static constexpr int kSfChunks = kFmt == kFmtNvfp4 ? 4 : (kFmt == kFmtMxfp4 ? 2 : 1);
   static constexpr int kABytes = kBM * kBKBytes;
   static constexpr int kBBytes = kBNHalf * kBKBytes;
   static constexpr int kSfaBytes = kSfChunks * 512;
@@ -94,11 +101,11 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
 // One stage's scales of this warp's TMEM quadrant: SFA chunks (4 columns
 // each, the 16-byte row r of a chunk holds rows r, r+32, r+64, r+96) and the
 // two 128-row SFB blocks per chunk (8 columns per chunk).
-template <bool kFp4>
+template <int kFmt>
 __device__ __forceinline__ void stage_scales(const uint8_t* ssfa, const uint8_t* ssfb,
                                              uint32_t t_quad, uint32_t sfa_col, uint32_t sfb_col,
                                              int lane) {
-  using Cfg = PairCfg<kFp4>;
+  using Cfg = PairCfg<kFmt>;
   uint32_t a[Cfg::kSfaCols];
   uint32_t b[Cfg::kSfbCols];
 #pragma unroll
@@ -148,10 +155,11 @@ constexpr int pair_threads() {
   return kOut == 2 ? 480 : 352;
 }
 
-template <bool kFp4, int kOut>
+template <int kFmt, int kOut>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>(), 1)
     gemm_pair_kernel(const __grid_constant__ GemmParams p) {
-  using Cfg = PairCfg<kFp4>;
+  using Cfg = PairCfg<kFmt>;
+  constexpr bool kFp4 = kFmt != kFmtMxfp8;
   constexpr bool kOutBf16 = kOut == 1;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -285,7 +293,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
     const int h = warp == 1 ? 0 : 1;
     if (leader && lane == 0 && h < Cfg::kIssuers) {
       const uint32_t idesc_base =
-          kFp4 ? make_idesc_block_scaled(2 * Cfg::kBM, Cfg::kIssueN, 1u, 0u, 0u, 0u)
+          kFp4 ? make_idesc_block_scaled(2 * Cfg::kBM, Cfg::kIssueN, 1u,
+                                         kFmt == kFmtMxfp4 ? 1u : 0u, 0u, 0u)
                : make_idesc_block_scaled(2 * Cfg::kBM, Cfg::kIssueN, 0u, 1u, 0u, 0u);
       const bool skip_mma = (p.diag & 2u) != 0;
       // B rows [h * kIssueN / 2, +kIssueN / 2) of each CTA's 128-row half.
@@ -322,7 +331,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
 #pragma unroll
             for (int j = 0; j < Cfg::kMmaPerStage; ++j) {
               const uint64_t koff = static_cast<uint64_t>(j * 2);  // +32 B of K
-              if (kFp4) {
+              if (kFmt == kFmtMxfp4) {
+                // Chunk j/2 holds this MMA's scales; ids 0 / 2 pick the pair.
+                const uint32_t sid = static_cast<uint32_t>((j & 1) * 2);
+                mma_pair_mxf4(d_tmem, adesc + koff, bdesc + koff,
+                              idesc_base | (sid << 29) | (sid << 4), sfa_col + (j / 2) * 4,
+                              sfb_col + (j / 2) * 8 + h * 4, acc);
+              } else if (kFp4) {
                 mma_pair_mxf4nvf4(d_tmem, adesc + koff, bdesc + koff, idesc_base,
                                   sfa_col + j * 4, sfb_col + j * 8 + h * 4, acc);
               } else {
@@ -376,7 +391,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
       const uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
       const uint32_t sfa_col = Cfg::kTmemSfBase + stage * Cfg::kTmemSfStageCols;
       if (!skip_st) {
-        stage_scales<kFp4>(ssfa, ssfb, t_quad, sfa_col, sfa_col + Cfg::kSfaCols, lane);
+        stage_scales<kFmt>(ssfa, ssfb, t_quad, sfa_col, sfa_col + Cfg::kSfaCols, lane);
         tmem_wait_st();
       }
       tc_fence_before();
@@ -661,10 +676,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
   }
 }
 
-template <bool kFp4, int kOut>
+template <int kFmt, int kOut>
 static cudaError_t launch_pair_one(const GemmParams& p, int grid, cudaStream_t stream) {
-  using Cfg = PairCfg<kFp4>;
-  auto kern = gemm_pair_kernel<kFp4, kOut>;
+  using Cfg = PairCfg<kFmt>;
+  auto kern = gemm_pair_kernel<kFmt, kOut>;
   static bool attr_done = false;
   if (!attr_done) {
     cudaError_t e =
@@ -676,19 +691,27 @@ static cudaError_t launch_pair_one(const GemmParams& p, int grid, cudaStream_t s
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm_pair(const GemmParams& p, bool fp4, int out_kind, int grid,
+cudaError_t launch_gemm_pair(const GemmParams& p, int fmt, int out_kind, int grid,
                              cudaStream_t stream) {
-  if (fp4) {
-    if (out_kind == 2) return launch_pair_one<true, 2>(p, grid, stream);
-    return out_kind == 1 ? launch_pair_one<true, 1>(p, grid, stream)
-                         : launch_pair_one<true, 0>(p, grid, stream);
+  if (fmt == kFmtNvfp4) {
+    if (out_kind == 2) return launch_pair_one<kFmtNvfp4, 2>(p, grid, stream);
+    return out_kind == 1 ? launch_pair_one<kFmtNvfp4, 1>(p, grid, stream)
+                         : launch_pair_one<kFmtNvfp4, 0>(p, grid, stream);
   }
   if (out_kind == 2) return cudaErrorInvalidValue;
-  return out_kind == 1 ? launch_pair_one<false, 1>(p, grid, stream)
-                       : launch_pair_one<false, 0>(p, grid, stream);
+  if (fmt == kFmtMxfp4)
+    return out_kind == 1 ? launch_pair_one<kFmtMxfp4, 1>(p, grid, stream)
+                         : launch_pair_one<kFmtMxfp4, 0>(p, grid, stream);
+  return out_kind == 1 ? launch_pair_one<kFmtMxfp8, 1>(p, grid, stream)
+                       : launch_pair_one<kFmtMxfp8, 0>(p, grid, stream);
 }
 
-int pair_tile_m() { return 2 * PairCfg<true>::kBM; }
-int pair_tile_n() { return PairCfg<true>::kBN; }
+int pair_tile_m() { return 2 * PairCfg<kFmtNvfp4>::kBM; }
+int pair_tile_n() { return PairCfg<kFmtNvfp4>::kBN; }
+int pair_sf_chunks_per_stage(int fmt) {
+  return fmt == kFmtNvfp4 ? PairCfg<kFmtNvfp4>::kSfChunks
+                          : (fmt == kFmtMxfp4 ? PairCfg<kFmtMxfp4>::kSfChunks
+                                              : PairCfg<kFmtMxfp8>::kSfChunks);
+}
 
 }  // namespace qg

@@ -84,9 +84,11 @@ int skinny_mma_n(int64_t m);
 
 cudaError_t launch_gemm_blockscaled(const GemmParams& p, bool fp4, bool out_bf16, int grid,
                                     cudaStream_t stream);
-// out_kind: 0 fp32 C, 1 bf16 C, 2 NVFP4 output (rq_* fields; fp4 only).
-cudaError_t launch_gemm_pair(const GemmParams& p, bool fp4, int out_kind, int grid,
+// fmt: 0 MXFP8, 1 NVFP4, 2 MXFP4.  out_kind: 0 fp32 C, 1 bf16 C, 2 NVFP4
+// output (rq_* fields; NVFP4 only).
+cudaError_t launch_gemm_pair(const GemmParams& p, int fmt, int out_kind, int grid,
                              cudaStream_t stream);
+int pair_sf_chunks_per_stage(int fmt);
 cudaError_t launch_gemm_solo(const GemmParams& p, bool fp4, bool out_bf16, int grid,
                              cudaStream_t stream);
 int pair_tile_m();
@@ -103,6 +105,8 @@ cudaError_t launch_quantize_nvfp4(const void* x, bool bf16, int64_t rows, int64_
                                   uint8_t* q, uint8_t* sf, float* ts, const uint32_t* amax_bits,
                                   cudaStream_t stream);
 cudaError_t launch_quantize_mxfp8(const void* x, bool bf16, int64_t rows, int64_t k, int layout,
+                                  uint8_t* q, uint8_t* sf, cudaStream_t stream);
+cudaError_t launch_quantize_mxfp4(const void* x, bool bf16, int64_t rows, int64_t k, int layout,
                                   uint8_t* q, uint8_t* sf, cudaStream_t stream);
 cudaError_t launch_repack_nvfp4(const uint8_t* sq, const uint8_t* ssf, int src_layout,
                                 uint8_t* dq, uint8_t* dsf, int dst_layout, int64_t rows,

@@ -415,6 +415,18 @@ __device__ __forceinline__ void mma_pair_mxf4nvf4(uint32_t d_tmem, uint64_t a_de
       "p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem));
 }
+// MXFP4: e2m1 operands with one ue8m0 scale per 32 K elements (two scales
+// per K = 64 MMA, picked by the scale ids 0 / 2 in the instruction descriptor).
+__device__ __forceinline__ void mma_pair_mxf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], "
+      "p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem));
+}
 __device__ __forceinline__ void mma_pair_mxf8f6f4(uint32_t d_tmem, uint64_t a_desc,
                                                   uint64_t b_desc, uint32_t idesc,
                                                   uint32_t sfa_tmem, uint32_t sfb_tmem,

@@ -167,6 +167,58 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ------------------------------------------------------------------ MXFP4
+// OCP MX v1.0 with E2M1 elements: one thread per 32-element block, ue8m0
+// exponent e = floor(log2(amax)) - 2 (emax of E2M1) clamped to [-127, 127]
+// (all-zero block: code 0), elements e2m1 RNE, saturating, of x * 2^-e
+// (NaN -> +0).  layout 0 packs the first element of a pair in the high
+// nibble, the MMA layouts in the low nibble.
+template <bool kBf16>
+__global__ void __launch_bounds__(256)
+    mxfp4_quantize_kernel(const void* x, int64_t rows, int64_t k, int layout, uint8_t* q,
+                          uint8_t* sf) {
+  const int64_t sfk = k / 32;
+  const int64_t nblocks = rows * sfk;
+  const int64_t row_blocks = (rows + 127) / 128;
+  const int64_t sf_blocks = (sfk + 3) / 4;
+  const bool high_first = layout == 0;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < nblocks;
+       b += stride) {
+    float v[32];
+    load16<kBf16>(x, b * 32, *reinterpret_cast<float(*)[16]>(&v[0]));
+    load16<kBf16>(x, b * 32 + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    int e = -127;
+    if (amax > 0.0f) e = max(-127, min(127, floor_log2_positive(amax) - 2));
+    // 2^-e: e <= 125 here, so the exponent field 127 - e is in [2, 254].
+    const float mul = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float x0 = __fmul_rn(v[8 * i + 2 * j], mul), x1 = __fmul_rn(v[8 * i + 2 * j + 1], mul);
+        x0 = x0 == x0 ? x0 : 0.0f;  // NaN -> +0
+        x1 = x1 == x1 ? x1 : 0.0f;
+        word |= (high_first ? e2m1x2_cvt(x0, x1) : e2m1x2_cvt(x1, x0)) << (8 * j);
+      }
+      w[i] = word;
+    }
+    reinterpret_cast<uint4*>(q)[b] = make_uint4(w[0], w[1], w[2], w[3]);
+    const uint8_t code = static_cast<uint8_t>(e + 127);
+    if (layout == 0) {
+      sf[b] = code;
+    } else {
+      const int64_t row = b / sfk, sc = b - row * sfk;
+      sf[mma_scale_offset(row, sc, row_blocks, sf_blocks, layout)] = code;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ repack
 __global__ void __launch_bounds__(256)
     nvfp4_repack_kernel(const uint8_t* sq, const uint8_t* ssf, int src_layout, uint8_t* dq,
@@ -242,6 +294,14 @@ cudaError_t launch_quantize_mxfp8(const void* x, bool bf16, int64_t rows, int64_
   const int grid = grid_for(rows * (k / 32), 256);
   if (bf16) mxfp8_quantize_kernel<true><<<grid, 256, 0, stream>>>(x, rows, k, layout, q, sf);
   else mxfp8_quantize_kernel<false><<<grid, 256, 0, stream>>>(x, rows, k, layout, q, sf);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_mxfp4(const void* x, bool bf16, int64_t rows, int64_t k, int layout,
+                                  uint8_t* q, uint8_t* sf, cudaStream_t stream) {
+  const int grid = grid_for(rows * (k / 32), 256);
+  if (bf16) mxfp4_quantize_kernel<true><<<grid, 256, 0, stream>>>(x, rows, k, layout, q, sf);
+  else mxfp4_quantize_kernel<false><<<grid, 256, 0, stream>>>(x, rows, k, layout, q, sf);
   return cudaGetLastError();
 }
 

@@ -21,7 +21,8 @@
 // run_quant_gemm_1024.py:37-43), mxfp8_q0_tcgen05_block_scaled,
 // nvfp4_skinny_q0 (decode GEMM, fused activation quantisation),
 // nvfp4_q0_tc6_fused_epilogue (NVFP4 output requantised in the epilogue,
-// the reference's tc6 row), all.
+// the reference's tc6 row), mxfp4_q0_tcgen05_block_scaled (the CUTLASS 72a
+// MXFP4 rows), all.
 //
 // Inputs are seeded N(0,1) (std::mt19937_64, A: seed, B: seed ^ 0xbb67ae85),
 // quantised on the device by the library.  The check recomputes sampled
@@ -144,6 +145,23 @@ HostOperand fetch_mxfp8(const void* dq, const void* dsf, int64_t rows, int64_t k
   o.v.resize(rows * k);
   o.s.resize(rows * (k / 32));
   for (int64_t i = 0; i < rows * k; ++i) o.v[i] = e4m3(q[i]);
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t c = 0; c < k / 32; ++c) o.s[r * (k / 32) + c] = ue8m0(sf[scale_offset(r, c, rows, k / 32)]);
+  return o;
+}
+
+HostOperand fetch_mxfp4(const void* dq, const void* dsf, int64_t rows, int64_t k) {
+  std::vector<uint8_t> q(rows * k / 2), sf(qg_scale_bytes(rows, k, 32));
+  CHECK_CUDA(cudaMemcpy(q.data(), dq, q.size(), cudaMemcpyDeviceToHost));
+  CHECK_CUDA(cudaMemcpy(sf.data(), dsf, sf.size(), cudaMemcpyDeviceToHost));
+  HostOperand o;
+  o.rows = rows, o.k = k, o.sv = 32;
+  o.v.resize(rows * k);
+  o.s.resize(rows * (k / 32));
+  for (int64_t i = 0; i < rows * k; ++i) {
+    const uint8_t b = q[i / 2];
+    o.v[i] = e2m1((i & 1) ? (b >> 4) : (b & 15));  // low nibble first
+  }
   for (int64_t r = 0; r < rows; ++r)
     for (int64_t c = 0; c < k / 32; ++c) o.s[r * (k / 32) + c] = ue8m0(sf[scale_offset(r, c, rows, k / 32)]);
   return o;
@@ -295,6 +313,39 @@ Row run_mxfp8(const Options& o) {
   CHECK_QG(qg_read_status(status, nullptr, nullptr));
   r.gflops = 2.0 * m * n * k / (r.ms * 1e6);
   auto A = fetch_mxfp8(aq, asf, m, k), B = fetch_mxfp8(bq, bsf, n, k);
+  r.matched = check_rows(A, B, fetch_c(dc, m * n, o.out_bf16), m, n, o.out_bf16, &r.frob);
+  for (void* p : {static_cast<void*>(da), static_cast<void*>(db), aq, asf, bq, bsf, dc,
+                  static_cast<void*>(status)})
+    cudaFree(p);
+  return r;
+}
+
+// MXFP4 x MXFP4 GEMM (mxfp4_q0_tcgen05_block_scaled, the reference's CUTLASS
+// 72a MXFP4 rows, run_quant_gemm_1024.py:54-73); A, B ~ N(0, 1).
+Row run_mxfp4(const Options& o) {
+  const int64_t m = o.m, n = o.n, k = o.k;
+  auto ha = normal(m * k, o.seed), hb = normal(n * k, o.seed ^ 0xbb67ae85ull);
+  float *da = static_cast<float*>(dalloc(m * k * 4)), *db = static_cast<float*>(dalloc(n * k * 4));
+  CHECK_CUDA(cudaMemcpy(da, ha.data(), m * k * 4, cudaMemcpyHostToDevice));
+  CHECK_CUDA(cudaMemcpy(db, hb.data(), n * k * 4, cudaMemcpyHostToDevice));
+  void *aq = dalloc(m * k / 2), *asf = dalloc(qg_scale_bytes(m, k, 32));
+  void *bq = dalloc(n * k / 2), *bsf = dalloc(qg_scale_bytes(n, k, 32));
+  CHECK_QG(qg_quantize_mxfp4(da, QG_DTYPE_F32, m, k, QG_LAYOUT_MMA, aq, asf, nullptr));
+  CHECK_QG(qg_quantize_mxfp4(db, QG_DTYPE_F32, n, k, QG_LAYOUT_MMA, bq, bsf, nullptr));
+  const int cdt = o.out_bf16 ? QG_DTYPE_BF16 : QG_DTYPE_F32;
+  void* dc = dalloc(m * n * (o.out_bf16 ? 2 : 4));
+  uint32_t* status = static_cast<uint32_t*>(dalloc(4));
+  CHECK_CUDA(cudaMemset(status, 0, 4));
+  Row r;
+  r.backend = "mxfp4_q0_tcgen05_block_scaled";
+  r.version = "tcgen05 mxf4nvf4 block32 ue8m0 (B200)";
+  r.precision = o.out_bf16 ? "mxfp4->bf16" : "mxfp4->fp32";
+  r.ms = time_launches([&] {
+    CHECK_QG(qg_gemm_mxfp4(aq, asf, bq, bsf, dc, cdt, m, n, k, n, QG_LAYOUT_MMA, status, nullptr));
+  }, o.iterations);
+  CHECK_QG(qg_read_status(status, nullptr, nullptr));
+  r.gflops = 2.0 * m * n * k / (r.ms * 1e6);
+  auto A = fetch_mxfp4(aq, asf, m, k), B = fetch_mxfp4(bq, bsf, n, k);
   r.matched = check_rows(A, B, fetch_c(dc, m * n, o.out_bf16), m, n, o.out_bf16, &r.frob);
   for (void* p : {static_cast<void*>(da), static_cast<void*>(db), aq, asf, bq, bsf, dc,
                   static_cast<void*>(status)})
@@ -491,7 +542,9 @@ void usage(const char* p) {
             << "       " << p << " M N K backend [--seed S] [--out-dtype bf16|fp32]\n"
             << "       " << p << " --m=M --n=N --k=K [--iterations=I] [--swizzle=S]\n"
             << "backends: all|nvfp4_q1_native_fp4_mainloop|mxfp8_q0_tcgen05_block_scaled|"
-               "nvfp4_skinny_q0|nvfp4_q0_tc6_fused_epilogue\n";
+               "nvfp4_skinny_q0|nvfp4_q0_tc6_fused_epilogue|mxfp4_q0_tcgen05_block_scaled\n"
+            << "Invoked under a name containing \"mxfp4\" (e.g. cutlass_72a_mxfp4_bf16_b200),\n"
+            << "the --m/--n/--k form runs MXFP4 (the CUTLASS 72a MXFP4 runner's binary).\n";
 }
 
 bool parse(int argc, char** argv, Options* o) {
@@ -510,7 +563,11 @@ bool parse(int argc, char** argv, Options* o) {
     else pos.push_back(a);
   }
   if (o->cutlass_cli) {
-    o->backend = "nvfp4_q1_native_fp4_mainloop";
+    // Under the MXFP4 runner's binary name (--cutlass-mxfp4-bin,
+    // run_quant_gemm_1024.py:615-624) the same CLI runs MXFP4.
+    const std::string self = argv[0];
+    const bool mx4 = self.substr(self.find_last_of('/') + 1).find("mxfp4") != std::string::npos;
+    o->backend = mx4 ? "mxfp4_q0_tcgen05_block_scaled" : "nvfp4_q1_native_fp4_mainloop";
     o->out_bf16 = true;
     o->square = false;
     return o->m > 0 && o->n > 0 && o->k > 0;
@@ -531,7 +588,7 @@ bool parse(int argc, char** argv, Options* o) {
   return o->m > 0 && o->n > 0 && o->k > 0 &&
          (b == "all" || b == "nvfp4_q1_native_fp4_mainloop" ||
           b == "mxfp8_q0_tcgen05_block_scaled" || b == "nvfp4_skinny_q0" ||
-          b == "nvfp4_q0_tc6_fused_epilogue");
+          b == "nvfp4_q0_tc6_fused_epilogue" || b == "mxfp4_q0_tcgen05_block_scaled");
 }
 
 }  // namespace
@@ -547,8 +604,9 @@ int main(int argc, char** argv) {
   cudaDeviceProp prop{};
   CHECK_CUDA(cudaGetDeviceProperties(&prop, dev));
   if (o.cutlass_cli) {
-    Row r = run_nvfp4(o);
-    std::cout << "  Problem Size: " << o.m << 'x' << o.n << 'x' << o.k << "\n"
+    Row r = o.backend == "mxfp4_q0_tcgen05_block_scaled" ? run_mxfp4(o) : run_nvfp4(o);
+    std::cout << "  Backend: " << r.backend << "\n"
+              << "  Problem Size: " << o.m << 'x' << o.n << 'x' << o.k << "\n"
               << "  Disposition: " << (r.matched ? "Passed" : "Failed") << "\n"
               << "  Avg runtime: " << r.ms << " ms\n"
               << "  GFLOPS: " << r.gflops << "\n";
@@ -569,6 +627,11 @@ int main(int argc, char** argv) {
   }
   if (want("mxfp8_q0_tcgen05_block_scaled")) {
     Row r = run_mxfp8(o);
+    write_row(csv, r, o);
+    all_ok &= r.matched;
+  }
+  if (want("mxfp4_q0_tcgen05_block_scaled")) {
+    Row r = run_mxfp4(o);
     write_row(csv, r, o);
     all_ok &= r.matched;
   }

@@ -45,6 +45,9 @@ SIGNATURES = {
     "qg_quantize_nvfp4_noalloc": (_I32, [_VP, _I32, _I64, _I64, _I32, _VP, _VP, _VP, _VP]),
     "qg_quantize_nvfp4_noalloc_max_elements": (_I64, []),
     "qg_quantize_mxfp8": (_I32, [_VP, _I32, _I64, _I64, _I32, _VP, _VP, _VP]),
+    "qg_quantize_mxfp4": (_I32, [_VP, _I32, _I64, _I64, _I32, _VP, _VP, _VP]),
+    "qg_gemm_mxfp4": (_I32, [_VP, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64, _I64, _I32, _VP,
+                             _VP]),
     "qg_repack_nvfp4": (_I32, [_VP, _VP, _I32, _VP, _VP, _I32, _I64, _I64, _VP]),
     "qg_gemm_nvfp4": (_I32, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64, _I64,
                              _I32, _VP, _VP]),
@@ -180,6 +183,30 @@ def make_mxfp8(x: torch.Tensor, layout: int = LAYOUT_MMA,
     return Mxfp8Result(q, sf, rows, k, layout)
 
 
+@dataclass
+class Mxfp4Result:
+    quantized: torch.Tensor     # uint8, e2m1 pairs
+    block_scales: torch.Tensor  # uint8, ue8m0 per 32 K elements
+    rows: int
+    k: int
+    layout: int
+
+
+def make_mxfp4(x: torch.Tensor, layout: int = LAYOUT_MMA,
+               stream: Optional[torch.cuda.Stream] = None) -> Mxfp4Result:
+    """Quantise a 2-D fp32/bf16 CUDA tensor to MXFP4 (e2m1 + ue8m0 per 32)."""
+    if x.dim() != 2 or not x.is_cuda or not x.is_contiguous():
+        raise ValueError("x must be a contiguous 2-D CUDA tensor")
+    rows, k = x.shape
+    q = torch.empty(rows * k // 2, dtype=torch.uint8, device=x.device)
+    nsf = rows * (k // 32) if layout == LAYOUT_REF_LINEAR else sm1xx_scale_storage_size(rows, k, 32)
+    sf = torch.empty(max(nsf, 1), dtype=torch.uint8, device=x.device)
+    rc = lib().qg_quantize_mxfp4(x.data_ptr(), _dtype_code(x), rows, k, layout, q.data_ptr(),
+                                 sf.data_ptr(), _stream(stream))
+    _check(rc, "qg_quantize_mxfp4")
+    return Mxfp4Result(q, sf, rows, k, layout)
+
+
 def repack_nvfp4(src: Nvfp4Result, dst_layout: int,
                  stream: Optional[torch.cuda.Stream] = None) -> Nvfp4Result:
     """Re-lay NVFP4 values and scales (REF_LINEAR <-> MMA <-> MMA_KMAJOR)."""
@@ -213,12 +240,22 @@ def gemm_mxfp8_raw(a_q, a_sf, b_q, b_sf, c, m, n, k, sf_layout=LAYOUT_MMA,
     _check(rc, "qg_gemm_mxfp8")
 
 
+def gemm_mxfp4_raw(a_q, a_sf, b_q, b_sf, c, m, n, k, sf_layout=LAYOUT_MMA,
+                   status: Optional[torch.Tensor] = None, stream=None) -> None:
+    rc = lib().qg_gemm_mxfp4(a_q.data_ptr(), a_sf.data_ptr(), b_q.data_ptr(), b_sf.data_ptr(),
+                             c.data_ptr(), _dtype_code(c), m, n, k, c.stride(0), sf_layout,
+                             _ptr(status), _stream(stream))
+    _check(rc, "qg_gemm_mxfp4")
+
+
 def block_scaled_gemm(a, b, out_dtype: torch.dtype = torch.bfloat16,
                       out: Optional[torch.Tensor] = None,
                       status: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
     """Tensor-core GEMM C = A . B^T over two quantised operands of the same
-    format (``Nvfp4Result`` pair or ``Mxfp8Result`` pair, both in one MMA
-    layout)."""
+    format (``Nvfp4Result``, ``Mxfp8Result`` or ``Mxfp4Result`` pair, both in
+    one MMA layout)."""
+    if type(a) is not type(b):
+        raise ValueError("operands must share the format")
     if a.k != b.k or a.layout != b.layout:
         raise ValueError("operands must share K and layout")
     m, n, k = a.rows, b.rows, a.k
@@ -227,6 +264,9 @@ def block_scaled_gemm(a, b, out_dtype: torch.dtype = torch.bfloat16,
     if isinstance(a, Nvfp4Result):
         gemm_nvfp4_raw(a.quantized, a.block_scales, a.tensor_scale, b.quantized, b.block_scales,
                        b.tensor_scale, out, m, n, k, a.layout, status, stream)
+    elif isinstance(a, Mxfp4Result):
+        gemm_mxfp4_raw(a.quantized, a.block_scales, b.quantized, b.block_scales, out, m, n, k,
+                       a.layout, status, stream)
     else:
         gemm_mxfp8_raw(a.quantized, a.block_scales, b.quantized, b.block_scales, out, m, n, k,
                        a.layout, status, stream)

@@ -123,6 +123,19 @@ int64_t qg_quantize_nvfp4_noalloc_max_elements(void);
 int qg_quantize_mxfp8(const void* x, int x_dtype, int64_t rows, int64_t k, int layout, void* q,
                       void* sf, qg_stream_t stream);
 
+/* MXFP4 quantizer (OCP MX v1.0 with E2M1 elements; the reference has no
+ * MXFP4 quantizer, its MXFP4 rows run CUTLASS example 72a with
+ * mx_float4_t, GEMMquant_sm110/build_and_run.sh:77-115): x (rows x k) ->
+ * e2m1 values `q` (rows*k/2 bytes) and ue8m0 scales per 32 K elements,
+ * scale exponent floor(log2(block amax)) - 2 clamped to [-127, 127]
+ * (all-zero blocks get code 0), elements e2m1 round-to-nearest-even of
+ * x * 2^-e, saturating at 6, NaN -> +0.  k % 32 == 0.  Layout REF_LINEAR
+ * packs the first element of each pair in the HIGH nibble and writes the
+ * scales as [rows][k/32]; the MMA layouts pack low nibble first with
+ * qg_scale_bytes(rows, k, 32) scale bytes. */
+int qg_quantize_mxfp4(const void* x, int x_dtype, int64_t rows, int64_t k, int layout, void* q,
+                      void* sf, qg_stream_t stream);
+
 /* Re-lay an NVFP4 operand between layouts (rows x k, k % 16 == 0).  Source
  * and destination must not alias. */
 int qg_repack_nvfp4(const void* src_q, const void* src_sf, int src_layout, void* dst_q,
@@ -173,6 +186,17 @@ int qg_gemm_nvfp4_requant(const void* a_q, const void* a_sf, const float* a_ts, 
  * (GEMMquant_sm110/src/quant_gemm_bench.cu:285-662, :1314-1373) with the
  * scaled format of cutlass-gemm-cpp-guide/cases/bs_mxfp8_1sm_p128. */
 int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, void* c,
+                  int c_dtype, int64_t m, int64_t n, int64_t k, int64_t ldc, int sf_layout,
+                  uint32_t* status, qg_stream_t stream);
+
+/* MXFP4 x MXFP4 block-scaled GEMM on tcgen05 (kind::mxf4nvf4.block32,
+ * ue8m0 scale per 32 K): C = sum_k a*sfa*b*sfb.  a_q / b_q are e2m1 codes
+ * in the MMA nibble order (M*K/2, N*K/2 bytes), scales in sf_layout (an MMA
+ * layout, qg_scale_bytes(rows, K, 32) bytes).  K % 32 == 0; rules otherwise
+ * as qg_gemm_nvfp4.  Replaces the CUTLASS 72a MXFP4 backend rows
+ * mxfp4_q0_cutlass_72a_mxfp4_bf16 / mxfp4_q1_cutlass_72a_swizzle1
+ * (GEMMquant_sm110/scripts/run_quant_gemm_1024.py:54-73). */
+int qg_gemm_mxfp4(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, void* c,
                   int c_dtype, int64_t m, int64_t n, int64_t k, int64_t ldc, int sf_layout,
                   uint32_t* status, qg_stream_t stream);
 

@@ -58,6 +58,8 @@ class Oracle:
             "qgo_block_scaled_gemm": (None, [_f32p, _f32p, _f32p, _f32p, _I64, _I64, _I64, _I32,
                                              _I64, _I64, _I32, _f32p]),
             "qgo_nvfp4_decode_mma": (None, [_u8p, _u8p, _I64, _I64, _I32, _f32p, _f32p]),
+            "qgo_mxfp4_quantize": (None, [_f32p, _I64, _I64, _I32, _u8p, _u8p]),
+            "qgo_mxfp4_decode": (None, [_u8p, _u8p, _I64, _I64, _I32, _f32p, _f32p]),
             "qgo_mxfp8_decode": (None, [_u8p, _u8p, _I64, _I64, _I32, _f32p, _f32p]),
             "qgo_fill_normal": (None, [_f32p, _I64, _U64, _F32, _F32]),
             "qgo_fill_requant_dist": (None, [_f32p, _I64, _U32, _I32]),
@@ -139,6 +141,22 @@ class Oracle:
         sf = np.zeros(nsf, np.uint8)
         self.L.qgo_mxfp8_quantize(x, rows, k, order, q, sf)
         return q, sf
+
+    def mxfp4(self, x: np.ndarray, order: int = 0):
+        rows, k = x.shape
+        x = np.ascontiguousarray(x, np.float32)
+        q = np.zeros(rows * k // 2, np.uint8)
+        nsf = rows * (k // 32) if order < 0 else self.L.qgo_scale_storage_size(rows, k, 32)
+        sf = np.zeros(nsf, np.uint8)
+        self.L.qgo_mxfp4_quantize(x, rows, k, order, q, sf)
+        return q, sf
+
+    def mxfp4_decode(self, q, sf, rows, k, order=0):
+        vals = np.zeros(rows * k, np.float32)
+        scales = np.zeros(rows * (k // 32), np.float32)
+        self.L.qgo_mxfp4_decode(np.ascontiguousarray(q), np.ascontiguousarray(sf), rows, k, order,
+                                vals, scales)
+        return vals, scales
 
     def mxfp8_decode(self, q, sf, rows, k, order=0):
         v = np.empty(rows * k, np.float32)

@@ -23,6 +23,8 @@
 // floor(log2(amax)) - emax_elem, emax_elem = 8 for E4M3, stored as E8M0 with
 // bias 127, elements RN-satfinite E4M3 of x / 2^e).  Parity for that
 // quantizer is therefore unpinned; the MXFP8 GEMM is pinned through O2.
+// qgo_mxfp4_quantize restates the same rule for E2M1 elements (emax_elem = 2),
+// also unpinned; the MXFP4 GEMM is pinned through O2 with SV = 32.
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -287,6 +289,55 @@ void qgo_nvfp4_decode_mma(const uint8_t* q, const uint8_t* sf, int64_t rows, int
 }
 
 // Decode MXFP8 operands (e4m3 bytes, L1 scales with SV 32).
+// MXFP4 (OCP MX v1.0 with E2M1 elements; no reference quantizer, parity
+// unpinned) for rows x k (k % 32 == 0): shared exponent floor(log2(amax)) - 2
+// (emax of E2M1), clamped to [-127, 127], all-zero block -> code 0; elements
+// encode_e2m1 (RNE, saturating, NaN -> 0) of x * 2^-e.  order < 0: the
+// first element of a pair in the high nibble (pack_fp4.cuh:11-15), scales
+// [rows][k/32]; order >= 0: low nibble first, scales at the L1 offsets.
+void qgo_mxfp4_quantize(const float* x, int64_t rows, int64_t k, int order, uint8_t* q,
+                        uint8_t* sf) {
+  const int sv = 32;
+  const int64_t sfk = k / sv;
+  if (order >= 0) std::memset(sf, 0, static_cast<size_t>(qgo_scale_storage_size(rows, k, sv)));
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t s = 0; s < sfk; ++s) {
+      const float* blk = x + r * k + s * sv;
+      float amax = 0.0f;
+      for (int i = 0; i < sv; ++i) amax = std::max(amax, std::fabs(blk[i]));
+      int e = -127;
+      if (amax > 0.0f) {
+        int ex;
+        std::frexp(amax, &ex);  // amax = f * 2^ex, f in [0.5, 1)
+        e = std::max(-127, std::min(127, (ex - 1) - 2));
+      }
+      const uint8_t code = static_cast<uint8_t>(e + 127);
+      if (order >= 0) sf[qgo_scale_offset(r, s * sv, rows, k, sv, order)] = code;
+      else sf[r * sfk + s] = code;
+      for (int i = 0; i < sv; i += 2) {
+        const uint8_t c0 = encode_e2m1(std::ldexp(blk[i], -e));
+        const uint8_t c1 = encode_e2m1(std::ldexp(blk[i + 1], -e));
+        q[(r * k + s * sv + i) / 2] =
+            order < 0 ? qgo_pack_e2m1x2(c0, c1) : static_cast<uint8_t>(c0 | (c1 << 4));
+      }
+    }
+  }
+}
+
+void qgo_mxfp4_decode(const uint8_t* q, const uint8_t* sf, int64_t rows, int64_t k, int order,
+                      float* vals, float* scales) {
+  for (int64_t r = 0; r < rows; ++r) {
+    for (int64_t c = 0; c < k; ++c) {
+      const uint8_t b = q[(r * k + c) / 2];
+      const bool high = (order < 0) == ((c & 1) == 0);
+      vals[r * k + c] = decode_e2m1(high ? (b >> 4) : (b & 15));
+    }
+    for (int64_t s = 0; s < k / 32; ++s)
+      scales[r * (k / 32) + s] = decode_ue8m0(
+          order >= 0 ? sf[qgo_scale_offset(r, s * 32, rows, k, 32, order)] : sf[r * (k / 32) + s]);
+  }
+}
+
 void qgo_mxfp8_decode(const uint8_t* q, const uint8_t* sf, int64_t rows, int64_t k, int order,
                       float* vals, float* scales) {
   for (int64_t r = 0; r < rows; ++r) {

@@ -28,7 +28,9 @@ def test_bad_arguments_exit_nonzero(binary):
                                   ["512", "1024", "768", "nvfp4_q1_native_fp4_mainloop",
                                    "--out-dtype", "bf16"],
                                   ["64", "4096", "2048", "nvfp4_skinny_q0"],
-                                  ["512", "768", "1024", "nvfp4_q0_tc6_fused_epilogue"]])
+                                  ["512", "768", "1024", "nvfp4_q0_tc6_fused_epilogue"],
+                                  ["384", "640", "1024", "mxfp4_q0_tcgen05_block_scaled",
+                                   "--out-dtype", "bf16"]])
 def test_csv_rows_matched(binary, tmp_path, args):
     r = subprocess.run([str(binary), *args], capture_output=True, text=True, cwd=tmp_path,
                        timeout=600)
@@ -52,3 +54,15 @@ def test_cutlass_cli_form(binary, tmp_path):
     t = re.search(r"Avg runtime:\s*([0-9.eE+-]+)\s*ms", r.stdout)
     g = re.search(r"GFLOPS:\s*([0-9.eE+-]+)", r.stdout)
     assert t and g and float(t.group(1)) > 0 and float(g.group(1)) > 0
+
+
+@pytest.mark.gpu
+def test_cutlass_cli_form_mxfp4_name(binary, tmp_path):
+    """Under the MXFP4 runner's binary name the CUTLASS CLI runs MXFP4
+    (run_quant_gemm_1024.py --cutlass-mxfp4-bin, :615-624)."""
+    mx = binary.parent / "cutlass_72a_mxfp4_bf16_b200"
+    r = subprocess.run([str(mx), "--m=512", "--n=512", "--k=1024", "--iterations=10",
+                        "--swizzle=1"], capture_output=True, text=True, cwd=tmp_path, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "Backend: mxfp4_q0_tcgen05_block_scaled" in r.stdout
+    assert "Disposition: Passed" in r.stdout

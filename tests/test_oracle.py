@@ -195,3 +195,23 @@ def test_blocks_with_ts_and_linear_to_mma(oracle):
         qm, sm, _ = oracle.nvfp4_mma(x, order)
         a, b = oracle.linear_to_mma(q, sf, 130, 64, order)
         assert np.array_equal(a, qm) and np.array_equal(b, sm)
+
+
+def test_mxfp4_oracle_known_answers(oracle):
+    """OCP MX v1.0 E2M1 rule worked by hand: block amax 1 -> shared exponent
+    floor(log2 1) - 2 = -2 (ue8m0 125), elements x * 4 rounded to the e2m1
+    grid (ties to even), saturating at 6; an all-zero block gets code 0."""
+    x = np.zeros((1, 64), np.float32)
+    x[0, :8] = [1.0, 0.5, 0.25, 0.3, -0.0625, 0.8125, -1.0, 0.375]
+    q, sf = oracle.mxfp4(x, -1)
+    assert sf.tolist() == [125, 0]
+    # x*4 = 4, 2, 1, 1.2, -0.25, 3.25, -4, 1.5 -> codes 6, 4, 2, 2, 8 (-0), 5, 14, 3
+    codes = [6, 4, 2, 2, 8, 5, 14, 3]
+    assert q[:4].tolist() == [(codes[i] << 4) | codes[i + 1] for i in range(0, 8, 2)]
+    assert not q[4:].any()
+    v, s = oracle.mxfp4_decode(q, sf, 1, 64, -1)
+    assert np.allclose(v[:8] * s[0], [1.0, 0.5, 0.25, 0.25, -0.0, 0.75, -1.0, 0.375])
+    # MMA order: low nibble first, scales at the L1 offsets
+    qm, sm = oracle.mxfp4(x, 0)
+    assert qm[0] == (codes[1] << 4) | codes[0]
+    assert sm[0] == 125
