@@ -361,6 +361,29 @@ int qg_repack_nvfp4(const void* src_q, const void* src_sf, int src_layout, void*
              : QG_ERR_CUDA;
 }
 
+int qg_repack_mx(int elem_bits, const void* src_q, const void* src_sf, int src_layout,
+                 void* dst_q, void* dst_sf, int dst_layout, int64_t rows, int64_t k,
+                 qg_stream_t stream) {
+  if (!src_q || !src_sf || !dst_q || !dst_sf) return QG_ERR_ARG;
+  if (elem_bits != 4 && elem_bits != 8) return QG_ERR_DTYPE;
+  if (src_layout < 0 || src_layout > 2 || dst_layout < 0 || dst_layout > 2) return QG_ERR_LAYOUT;
+  if (rows < 1 || k < 32 || (k % 32) != 0) return QG_ERR_SHAPE;
+  if (!aligned16(src_q) || !aligned16(dst_q)) return QG_ERR_ALIGN;
+  if (int d = check_device()) return d;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dst_layout != QG_LAYOUT_REF_LINEAR && ((rows % 128) != 0 || ((k / 32) % 4) != 0)) {
+    if (cudaMemsetAsync(dst_sf, 0, static_cast<size_t>(qg_scale_bytes(rows, k, 32)), s) !=
+        cudaSuccess)
+      return QG_ERR_CUDA;
+  }
+  return launch_repack_mx(elem_bits == 4, static_cast<const uint8_t*>(src_q),
+                          static_cast<const uint8_t*>(src_sf), src_layout,
+                          static_cast<uint8_t*>(dst_q), static_cast<uint8_t*>(dst_sf), dst_layout,
+                          rows, k, s) == cudaSuccess
+             ? QG_OK
+             : QG_ERR_CUDA;
+}
+
 int qg_gemm_nvfp4(const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
                   const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
                   int64_t k, int64_t ldc, int sf_layout, uint32_t* status, qg_stream_t stream) {

@@ -111,6 +111,9 @@ cudaError_t launch_quantize_mxfp4(const void* x, bool bf16, int64_t rows, int64_
 cudaError_t launch_repack_nvfp4(const uint8_t* sq, const uint8_t* ssf, int src_layout,
                                 uint8_t* dq, uint8_t* dsf, int dst_layout, int64_t rows,
                                 int64_t k, cudaStream_t stream);
+cudaError_t launch_repack_mx(bool fp4, const uint8_t* sq, const uint8_t* ssf, int src_layout,
+                             uint8_t* dq, uint8_t* dsf, int dst_layout, int64_t rows, int64_t k,
+                             cudaStream_t stream);
 cudaError_t launch_e2m1_cvt_selftest(unsigned long long* out, cudaStream_t stream);
 cudaError_t launch_wait_timeout_selftest(uint64_t timeout_ns, uint32_t* status,
                                          cudaStream_t stream);

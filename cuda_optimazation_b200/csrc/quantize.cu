@@ -246,6 +246,57 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// MX formats (one ue8m0 scale per 32 K elements): a block is 16 value bytes
+// (MXFP4, nibble order flipped between REF_LINEAR and the MMA layouts) or 32
+// (MXFP8, bytes unchanged); one thread per block.
+template <bool kFp4>
+__global__ void __launch_bounds__(256)
+    mx_repack_kernel(const uint8_t* sq, const uint8_t* ssf, int src_layout, uint8_t* dq,
+                     uint8_t* dsf, int dst_layout, int64_t rows, int64_t k) {
+  constexpr int kVec = kFp4 ? 1 : 2;  // uint4 per block
+  const int64_t sfk = k / 32;
+  const int64_t nblocks = rows * sfk;
+  const int64_t row_blocks = (rows + 127) / 128;
+  const int64_t sf_blocks = (sfk + 3) / 4;
+  const bool swap = kFp4 && ((src_layout == 0) != (dst_layout == 0));
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < nblocks;
+       b += stride) {
+#pragma unroll
+    for (int v = 0; v < kVec; ++v) {
+      uint4 w = reinterpret_cast<const uint4*>(sq)[b * kVec + v];
+      if (swap) {
+        w.x = ((w.x >> 4) & 0x0f0f0f0fu) | ((w.x << 4) & 0xf0f0f0f0u);
+        w.y = ((w.y >> 4) & 0x0f0f0f0fu) | ((w.y << 4) & 0xf0f0f0f0u);
+        w.z = ((w.z >> 4) & 0x0f0f0f0fu) | ((w.z << 4) & 0xf0f0f0f0u);
+        w.w = ((w.w >> 4) & 0x0f0f0f0fu) | ((w.w << 4) & 0xf0f0f0f0u);
+      }
+      reinterpret_cast<uint4*>(dq)[b * kVec + v] = w;
+    }
+    const int64_t row = b / sfk, sc = b - row * sfk;
+    const int64_t so =
+        src_layout == 0 ? b : mma_scale_offset(row, sc, row_blocks, sf_blocks, src_layout);
+    const int64_t d =
+        dst_layout == 0 ? b : mma_scale_offset(row, sc, row_blocks, sf_blocks, dst_layout);
+    dsf[d] = ssf[so];
+  }
+}
+
+static int grid_for(int64_t work_items, int threads);
+
+cudaError_t launch_repack_mx(bool fp4, const uint8_t* sq, const uint8_t* ssf, int src_layout,
+                             uint8_t* dq, uint8_t* dsf, int dst_layout, int64_t rows, int64_t k,
+                             cudaStream_t stream) {
+  const int grid = grid_for(rows * (k / 32), 256);
+  if (fp4)
+    mx_repack_kernel<true><<<grid, 256, 0, stream>>>(sq, ssf, src_layout, dq, dsf, dst_layout,
+                                                     rows, k);
+  else
+    mx_repack_kernel<false><<<grid, 256, 0, stream>>>(sq, ssf, src_layout, dq, dsf, dst_layout,
+                                                      rows, k);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ self test
 __global__ void wait_timeout_selftest_kernel(uint64_t timeout_ns, uint32_t* status) {
   __shared__ __align__(8) uint64_t bar;

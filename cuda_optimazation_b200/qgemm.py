@@ -48,6 +48,7 @@ SIGNATURES = {
     "qg_quantize_mxfp4": (_I32, [_VP, _I32, _I64, _I64, _I32, _VP, _VP, _VP]),
     "qg_gemm_mxfp4": (_I32, [_VP, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64, _I64, _I32, _VP,
                              _VP]),
+    "qg_repack_mx": (_I32, [_I32, _VP, _VP, _I32, _VP, _VP, _I32, _I64, _I64, _VP]),
     "qg_repack_nvfp4": (_I32, [_VP, _VP, _I32, _VP, _VP, _I32, _I64, _I64, _VP]),
     "qg_gemm_nvfp4": (_I32, [_VP, _VP, _VP, _VP, _VP, _VP, _VP, _I32, _I64, _I64, _I64, _I64,
                              _I32, _VP, _VP]),
@@ -221,6 +222,22 @@ def repack_nvfp4(src: Nvfp4Result, dst_layout: int,
                                _stream(stream))
     _check(rc, "qg_repack_nvfp4")
     return Nvfp4Result(q, sf, src.tensor_scale, src.rows, src.k, dst_layout)
+
+
+def repack_mx(src, dst_layout: int, stream: Optional[torch.cuda.Stream] = None):
+    """Re-lay an ``Mxfp4Result`` or ``Mxfp8Result`` (REF_LINEAR <-> MMA <->
+    MMA_KMAJOR)."""
+    dev = src.quantized.device
+    bits = 4 if isinstance(src, Mxfp4Result) else 8
+    q = torch.empty_like(src.quantized)
+    nsf = (src.rows * (src.k // 32) if dst_layout == LAYOUT_REF_LINEAR
+           else sm1xx_scale_storage_size(src.rows, src.k, 32))
+    sf = torch.empty(nsf, dtype=torch.uint8, device=dev)
+    rc = lib().qg_repack_mx(bits, src.quantized.data_ptr(), src.block_scales.data_ptr(),
+                            src.layout, q.data_ptr(), sf.data_ptr(), dst_layout, src.rows, src.k,
+                            _stream(stream))
+    _check(rc, "qg_repack_mx")
+    return type(src)(q, sf, src.rows, src.k, dst_layout)
 
 
 def gemm_nvfp4_raw(a_q, a_sf, a_ts, b_q, b_sf, b_ts, c, m, n, k, sf_layout=LAYOUT_MMA,

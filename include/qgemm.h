@@ -141,6 +141,18 @@ int qg_quantize_mxfp4(const void* x, int x_dtype, int64_t rows, int64_t k, int l
 int qg_repack_nvfp4(const void* src_q, const void* src_sf, int src_layout, void* dst_q,
                     void* dst_sf, int dst_layout, int64_t rows, int64_t k, qg_stream_t stream);
 
+/* Re-lay an MX operand (one ue8m0 scale per 32 K elements) between layouts:
+ * elem_bits 4 (MXFP4: nibble order flipped between REF_LINEAR and the MMA
+ * layouts) or 8 (MXFP8: value bytes unchanged).  rows x k, k % 32 == 0,
+ * value buffers 16-byte aligned; source and destination must not alias.
+ * Used by the quantised-weight file tool (cuda_optimazation_b200/weights.py)
+ * so stored weights load in either layout without re-quantising.  No
+ * reference counterpart (the reference stores no quantised weights;
+ * Nvfp4ReferenceResult, nvfp4_reference.cuh:18-22, is its in-memory form). */
+int qg_repack_mx(int elem_bits, const void* src_q, const void* src_sf, int src_layout,
+                 void* dst_q, void* dst_sf, int dst_layout, int64_t rows, int64_t k,
+                 qg_stream_t stream);
+
 /* NVFP4 x NVFP4 block-scaled GEMM on tcgen05 (kind::mxf4nvf4, block16):
  *   C[m, n] = (a_ts * b_ts) * sum_k a(m,k) sfa(m,k/16) b(n,k) sfb(n,k/16)
  * a_q / b_q in the MMA nibble order (M*K/2 and N*K/2 bytes), scales in
