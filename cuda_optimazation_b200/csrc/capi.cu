@@ -143,6 +143,14 @@ int gemm_variant(bool fp4, int64_t m) {
   return fp4 ? 0 : 2;
 }
 
+bool pair_epi8() {
+  static const bool v = [] {
+    const char* e = std::getenv("QG_PAIR_EPI");
+    return !(e && std::strcmp(e, "4") == 0);
+  }();
+  return v;
+}
+
 // `gather` (fused column-parallel output gather): this GPU computes the
 // columns [col0, col0 + n) of a C with row stride ldc and stores them into
 // every buffer of c_ranks (nranks of them, peer buffers IPC-mapped); only the
@@ -240,7 +248,11 @@ int gemm_common(int fmt, const void* a_q, const void* a_sf, const float* a_ts, c
   if (pair) {
     const int64_t pairs = num_sms() / 2;
     const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
-    e = launch_gemm_pair(p, fmt, rq ? 2 : (c_dtype == QG_DTYPE_BF16 ? 1 : 0), grid, stream);
+    // bf16 through TMA stores: the eight-warp epilogue (kind 3), unless
+    // QG_PAIR_EPI=4 asks for the four-warp one (A/B measurements).
+    const int out_kind = rq ? 2
+                            : (c_dtype == QG_DTYPE_BF16 ? (p.n_out > 0 && pair_epi8() ? 3 : 1) : 0);
+    e = launch_gemm_pair(p, fmt, out_kind, grid, stream);
   } else {
     const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
     e = variant == 2 ? launch_gemm_blockscaled(p, fp4, c_dtype == QG_DTYPE_BF16, grid, stream)

@@ -148,11 +148,12 @@ __device__ __forceinline__ void stage_scales(const uint8_t* ssfa, const uint8_t*
 // kOut: 0 fp32 C, 1 bf16 C, 2 NVFP4 output (values + e4m3 block scales,
 // requantised in the epilogue as the reference's tc6 store_tile does,
 // GEMMsm110/include/backends/tc6_nvfp4.cuh:460-503).
-// Threads per CTA: 11 warps; the NVFP4-output epilogue adds four more
-// epilogue warps (11..14, one per TMEM lane quadrant).
+// Threads per CTA: 11 warps; the NVFP4-output epilogue (kOut 2) and the
+// bf16 TMA-store epilogue (kOut 3) add four more epilogue warps (11..14, one
+// per TMEM lane quadrant).
 template <int kOut>
 constexpr int pair_threads() {
-  return kOut == 2 ? 480 : 352;
+  return kOut >= 2 ? 480 : 352;
 }
 
 template <int kFmt, int kOut>
@@ -160,7 +161,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
     gemm_pair_kernel(const __grid_constant__ GemmParams p) {
   using Cfg = PairCfg<kFmt>;
   constexpr bool kFp4 = kFmt != kFmtMxfp8;
-  constexpr bool kOutBf16 = kOut == 1;
+  constexpr bool kOutBf16 = kOut == 1 || kOut == 3;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -191,7 +192,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
       mbar_init(&empty_bar[s], Cfg::kIssuers);
     }
     mbar_init(acc_full, Cfg::kIssuers);
-    for (int i = 0; i < Cfg::kIssuers; ++i) mbar_init(&acc_empty[i], kOut == 2 ? 16 : 8);
+    for (int i = 0; i < Cfg::kIssuers; ++i) mbar_init(&acc_empty[i], kOut >= 2 ? 16 : 8);
     for (int i = 0; i < Cfg::kIssuers; ++i) mbar_init(&drain_bar[i], 1);
     *abort_flag = 0u;
     fence_barrier_init();
@@ -518,6 +519,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
               if (col0 + 16 * g < p.n) p.rq_sf[so + g] = static_cast<uint8_t>(sbits[g]);
           }
         }
+      } else if constexpr (kOut == 3) {
+        // bf16 through TMA stores with eight epilogue warps (2-5, 11-14; two
+        // per TMEM lane quadrant).  For each issuer's 128-column half a warp
+        // loads its 64 columns and hands the half back at once, then
+        // converts, stages the 64 x 32 box in its own swizzled 4 KB buffer
+        // and TMA-stores it to each destination: the next tile's MMAs start
+        // while this tile's output is still being written.
+        const int sub = warp >= 11 ? 1 : 0;
+        const int row0 = mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM + quad * 32;
+        uint8_t* box = epi_smem + (quad * 2 + sub) * 4096;
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          const int tb = 2 * h + sub;
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(t_row + tb * 64, r0);
+          tmem_ld_32x32b_x32(t_row + tb * 64 + 32, r1);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster_relaxed(h ? acc_empty_leader1 : acc_empty_leader0);
+          uint4 v[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t* src = c < 4 ? r0 + c * 8 : r1 + (c - 4) * 8;
+            v[c] = make_uint4(
+                bf16x2_bits(__uint_as_float(src[0]) * alpha, __uint_as_float(src[1]) * alpha),
+                bf16x2_bits(__uint_as_float(src[2]) * alpha, __uint_as_float(src[3]) * alpha),
+                bf16x2_bits(__uint_as_float(src[4]) * alpha, __uint_as_float(src[5]) * alpha),
+                bf16x2_bits(__uint_as_float(src[6]) * alpha, __uint_as_float(src[7]) * alpha));
+          }
+          if (lane == 0) tma_store_wait_read<0>();  // the box's previous store has read it
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(box + lane * 128 + ((c ^ (lane & 7)) * 16)) = v[c];
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && !(p.diag & 8u)) {
+            for (int d = 0; d < p.n_out; ++d)
+              tma_store_2d(&p.tm_out[d], box, n0 + tmem_block(tb) * 64, row0);
+            tma_store_commit();
+          }
+        }
       } else if (Cfg::kEpiBytes > 0 && kOutBf16 && p.n_out > 0) {
         // TMEM -> registers -> bf16 in a swizzled shared-memory box -> TMA
         // store (coalesced, asynchronous, clipped at the matrix edge) to each
@@ -666,7 +710,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
     }
   }
 
-  if (Cfg::kEpiBytes > 0 && warp >= 2 && warp <= 5 && (threadIdx.x % 32) == 0)
+  if (Cfg::kEpiBytes > 0 && ((warp >= 2 && warp <= 5) || warp >= 11) && (threadIdx.x % 32) == 0)
     tma_store_wait_all<0>();  // output stores done before shared memory is released
   tc_fence_before();
   cluster_sync();  // the leader's MMAs into both TMEMs are drained
@@ -687,18 +731,22 @@ static cudaError_t launch_pair_one(const GemmParams& p, int grid, cudaStream_t s
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  kern<<<grid, kOut == 2 ? pair_threads<kOut>() : Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  kern<<<grid, kOut >= 2 ? pair_threads<kOut>() : Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   return cudaGetLastError();
 }
 
 cudaError_t launch_gemm_pair(const GemmParams& p, int fmt, int out_kind, int grid,
                              cudaStream_t stream) {
   if (fmt == kFmtNvfp4) {
+    if (out_kind == 3) return launch_pair_one<kFmtNvfp4, 3>(p, grid, stream);
     if (out_kind == 2) return launch_pair_one<kFmtNvfp4, 2>(p, grid, stream);
     return out_kind == 1 ? launch_pair_one<kFmtNvfp4, 1>(p, grid, stream)
                          : launch_pair_one<kFmtNvfp4, 0>(p, grid, stream);
   }
   if (out_kind == 2) return cudaErrorInvalidValue;
+  if (out_kind == 3)
+    return fmt == kFmtMxfp4 ? launch_pair_one<kFmtMxfp4, 3>(p, grid, stream)
+                            : launch_pair_one<kFmtMxfp8, 3>(p, grid, stream);
   if (fmt == kFmtMxfp4)
     return out_kind == 1 ? launch_pair_one<kFmtMxfp4, 1>(p, grid, stream)
                          : launch_pair_one<kFmtMxfp4, 0>(p, grid, stream);

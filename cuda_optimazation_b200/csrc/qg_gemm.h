@@ -85,7 +85,8 @@ int skinny_mma_n(int64_t m);
 cudaError_t launch_gemm_blockscaled(const GemmParams& p, bool fp4, bool out_bf16, int grid,
                                     cudaStream_t stream);
 // fmt: 0 MXFP8, 1 NVFP4, 2 MXFP4.  out_kind: 0 fp32 C, 1 bf16 C, 2 NVFP4
-// output (rq_* fields; NVFP4 only).
+// output (rq_* fields; NVFP4 only), 3 bf16 C through TMA stores (n_out > 0)
+// with eight epilogue warps.
 cudaError_t launch_gemm_pair(const GemmParams& p, int fmt, int out_kind, int grid,
                              cudaStream_t stream);
 int pair_sf_chunks_per_stage(int fmt);
