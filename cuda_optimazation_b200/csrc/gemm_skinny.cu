@@ -434,6 +434,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       // is a wait, eight MMAs and a commit, with descriptors and scale
       // columns stepped by constants.
       const uint32_t idesc = make_idesc_block_scaled(Cfg::kBM, kN, 1u, 0u, 0u, 0u);
+      const bool skip_mma = (p.diag & 2u) != 0;
       const uint64_t wdesc0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
       const uint64_t xdesc0 = make_smem_desc(smem_u32(smem + Cfg::kWBytes), 16, 1024, kSwizzle128B);
       constexpr uint64_t kStageDesc = Cfg::kStageBytes >> 4;
@@ -468,6 +469,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
           tc_fence_after();
 #pragma unroll
           for (int i = 0; i < Cfg::kMmaPerStage; ++i) {
+            if (skip_mma) break;
             // MMA i: box i / 4, 32-byte K step (i % 4) inside the 128-byte row.
             const uint64_t wo = static_cast<uint64_t>((i / 4) * (Cfg::kWBox >> 4) + (i % 4) * 2);
             const uint64_t xo = static_cast<uint64_t>((i / 4) * (Cfg::kXBox >> 4) + (i % 4) * 2);
@@ -520,9 +522,11 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
         b[4 * c] = w.x; b[4 * c + 1] = w.y; b[4 * c + 2] = w.z; b[4 * c + 3] = w.w;
       }
       const uint32_t col = Cfg::kTmemSfBase + stage * Cfg::kSfStageCols;
-      tmem_st_32x32b<4 * Cfg::kSfChunks>(t_quad + col, a);
-      tmem_st_32x32b<4 * Cfg::kSfChunks>(t_quad + col + 4 * Cfg::kSfChunks, b);
-      tmem_wait_st();
+      if (!(p.diag & 1u)) {
+        tmem_st_32x32b<4 * Cfg::kSfChunks>(t_quad + col, a);
+        tmem_st_32x32b<4 * Cfg::kSfChunks>(t_quad + col + 4 * Cfg::kSfChunks, b);
+        tmem_wait_st();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sf_ready[stage]);

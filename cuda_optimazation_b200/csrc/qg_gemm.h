@@ -74,8 +74,10 @@ struct SkinnyParams {
   int num_tiles, num_k_blocks;
   uint32_t* status;
   uint64_t timeout_ns;
-  // Diagnostics (QG_DIAG_FLAGS): bit 6 writes %globaltimer stamps of CTA 0's
-  // roles into an unused partial slice.
+  // Diagnostics (QG_DIAG_FLAGS; results are wrong when bits 0-1 are set):
+  // bit 0 skips the scale staging (stagers still wait and arrive), bit 1 the
+  // MMAs (the issuer still waits and commits); bit 6 writes %globaltimer
+  // stamps of CTA (diag >> 16)'s roles into an unused partial slice.
   uint32_t diag;
 };
 cudaError_t launch_gemm_skinny(const SkinnyParams& p, int grid, cudaStream_t stream);
