@@ -6,11 +6,13 @@
 // activation rows its N side (16 / 32 / 64 / 128).  The reference has no
 // kernel for this shape (its harness only runs square problems,
 // GEMMquant_sm110/src/quant_gemm_bench.cu:3038-3079); BASELINE config 4 names
-// it.  The weights are streamed once from HBM; every CTA takes an equal,
-// contiguous range of (weight-tile, K-block) units ("stream-K"), so the
-// 224 x 32 units of N = 28672, K = 8192 spread evenly over 148 SMs.  A tile
-// that one CTA owns is scaled and written to C by that CTA; a tile split
-// between CTAs is summed by the last of them to finish (see the epilogue).
+// it.  The weights are streamed once from HBM.  Work is (weight-tile,
+// K-block) units: every CTA owns floor(T / G) whole tiles, and the units of
+// the remaining T mod G tiles are spread evenly over all CTAs (stream-K), so
+// the 224 x 16 units of N = 28672, K = 8192 split into one whole tile plus
+// ~8 units per CTA on 148 SMs.  A tile that one CTA owns is scaled and
+// written to C by that CTA; a tile split between CTAs is summed by the last
+// of them to finish (see the epilogue), while the whole tiles stream.
 // The activation quantisation runs in the same cooperative grid (see
 // quantize_phase), so a call is one launch: no memset, quantiser, reduction
 // or finishing kernel.
@@ -70,43 +72,83 @@ struct SkinnyCfg {
   static constexpr int kThreads = 320;
 };
 
-// Walk of one CTA's unit range: a "segment" is a run of K-blocks of one tile.
+// Work of one CTA.  With T tiles over G CTAs, every CTA owns w = T / G
+// whole tiles (the last T - (T mod G) tiles, contiguous per CTA) and an
+// equal contiguous share of the units (tile, K block) of the first T mod G
+// tiles, the "split region" (stream-K).  A split tile is shared by at most a
+// few neighbouring CTAs and summed by the last of them to finish it.
 struct UnitRange {
-  int u0, u1, nkb;
+  int nkb;
+  int split_tiles, split_units;  // the split region: tiles [0, split_tiles)
+  int su0, su1;                  // this CTA's units of it
+  int wt0, wn;                   // this CTA's whole tiles [wt0, wt0 + wn)
+  __device__ __forceinline__ void init(int num_tiles, int num_kb, int c, int g) {
+    nkb = num_kb;
+    wn = num_tiles / g;
+    split_tiles = num_tiles - wn * g;
+    split_units = split_tiles * nkb;
+    su0 = static_cast<int>(static_cast<int64_t>(split_units) * c / g);
+    su1 = static_cast<int>(static_cast<int64_t>(split_units) * (c + 1) / g);
+    wt0 = split_tiles + c * wn;
+  }
+  __device__ __forceinline__ int units() const { return su1 - su0 + wn * nkb; }
+  // CTA owning split-region unit u, and the first split tile of CTA c.
+  __device__ __forceinline__ int contributor(int64_t u, int g) const {
+    return static_cast<int>(((u + 1) * g - 1) / split_units);
+  }
+  __device__ __forceinline__ int first_split_tile(int c, int g) const {
+    return static_cast<int>(static_cast<int64_t>(split_units) * c / g / nkb);
+  }
 };
 
-// Order in which a CTA walks its range: the segment of its LAST tile first,
-// then the segment of its first tile, then the whole tiles between.  Both
-// segments a CTA shares with a neighbour are therefore finished early by
-// both neighbours, so the fixup of a split tile overlaps the streaming of
-// whole tiles instead of trailing the kernel.
+// Order in which a CTA walks its work: the split segments first -- the one
+// of its LAST split tile, then the one of its first, then any split tiles
+// between (whole within the range) -- and the whole tiles last.  The split
+// tiles' fixups (the last contributor sums the partial slices) therefore
+// overlap the streaming of the whole tiles instead of trailing the kernel,
+// whose last segments are stored straight to C.
 struct SegCursor {
-  int tile_lo, tile_hi, u0, u1, nkb;
+  int nkb, su0, su1, wt0, wn;
+  int tile_lo, tile_hi, nsplit;
   int i, t, kb, kb_end;  // segment index, its tile, current / end K block
   __device__ __forceinline__ void init(const UnitRange& r) {
-    u0 = r.u0;
-    u1 = r.u1;
     nkb = r.nkb;
-    tile_lo = u0 / nkb;
-    tile_hi = (u1 - 1) / nkb;
+    su0 = r.su0;
+    su1 = r.su1;
+    wt0 = r.wt0;
+    wn = r.wn;
+    if (su1 > su0) {
+      tile_lo = su0 / nkb;
+      tile_hi = (su1 - 1) / nkb;
+      nsplit = tile_hi - tile_lo + 1;
+    } else {
+      tile_lo = tile_hi = -1;
+      nsplit = 0;
+    }
     i = 0;
-    enter();
+    if (nseg() > 0) enter();
   }
-  __device__ __forceinline__ int nseg() const { return tile_hi - tile_lo + 1; }
+  __device__ __forceinline__ int nseg() const { return nsplit + wn; }
+  __device__ __forceinline__ bool split(int s) const { return s < nsplit; }
   __device__ __forceinline__ int tile_of(int s) const {
+    if (s >= nsplit) return wt0 + (s - nsplit);
     if (tile_hi == tile_lo) return tile_lo;
     return s == 0 ? tile_hi : (s == 1 ? tile_lo : tile_lo + s - 1);
   }
+  __device__ __forceinline__ int kb_lo(int s) const {
+    const int tt = tile_of(s);
+    return (s < nsplit && tt == tile_lo) ? su0 - tt * nkb : 0;
+  }
+  __device__ __forceinline__ int kb_hi(int s) const {
+    const int tt = tile_of(s);
+    return (s < nsplit && tt == tile_hi) ? su1 - tt * nkb : nkb;
+  }
   __device__ __forceinline__ void enter() {
     t = tile_of(i);
-    kb = (t == tile_lo) ? u0 - t * nkb : 0;
-    kb_end = (t == tile_hi) ? u1 - t * nkb : nkb;
+    kb = kb_lo(i);
+    kb_end = kb_hi(i);
   }
-  __device__ __forceinline__ bool seg_first() const {
-    return kb == ((t == tile_lo) ? u0 - t * nkb : 0);
-  }
-  __device__ __forceinline__ bool seg_last() const { return kb + 1 == kb_end; }
-  // Step to the next unit; false past the end of the range.
+  // Step to the next unit; false past the end of the work.
   __device__ __forceinline__ bool next() {
     if (++kb < kb_end) return true;
     if (++i >= nseg()) return false;
@@ -319,11 +361,8 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
 
   if (threadIdx.x == 0) trace(p, 0);
   if (threadIdx.x == 0) trace_cta(p, 768 + blockIdx.x);
-  const int64_t units = static_cast<int64_t>(p.num_tiles) * p.num_k_blocks;
   UnitRange ur;
-  ur.u0 = static_cast<int>(units * blockIdx.x / gridDim.x);
-  ur.u1 = static_cast<int>(units * (blockIdx.x + 1) / gridDim.x);
-  ur.nkb = p.num_k_blocks;
+  ur.init(p.num_tiles, p.num_k_blocks, static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x));
 
   bool quant_ok = true;
   if (warp >= 2) {
@@ -384,7 +423,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
         ok = false;
       SegCursor cur;
       cur.init(ur);
-      bool more = ok;
+      bool more = ok && cur.nseg() > 0;
       for (int g = 0; more; ++g) {
         if (!dep_done && g == Cfg::kStages) {
           release_deferred(cur, true);
@@ -447,8 +486,8 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       order.init(ur);
       for (int seg = 0; ok && seg < order.nseg(); ++seg) {
         const int t = order.tile_of(seg);
-        const int kb_lo = (t == order.tile_lo) ? ur.u0 - t * ur.nkb : 0;
-        const int kb_hi = (t == order.tile_hi) ? ur.u1 - t * ur.nkb : ur.nkb;
+        const int kb_lo = order.kb_lo(seg);
+        const int kb_hi = order.kb_hi(seg);
         const int buf = seg & 1;
         if (!mbar_wait_bounded(&acc_empty[buf], ((seg >> 1) & 1) ^ 1u, p.timeout_ns, abort_flag,
                                p.status, kDevTimeoutMma)) {
@@ -504,7 +543,8 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
     const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     int stage = 0;
     uint32_t phase = 0;
-    for (int u = ur.u0; quant_ok && u < ur.u1; ++u) {
+    const int my_units = ur.units();
+    for (int u = 0; quant_ok && u < my_units; ++u) {
       bool ok = true;
       if (lane == 0)
         ok = mbar_wait_bounded(&full_bar[stage], phase, p.timeout_ns, abort_flag, p.status,
@@ -547,10 +587,8 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
     const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     if (quad == 0 && lane == 0) trace(p, 3);
     const float alpha = __ldcg(p.x_ts) * (p.w_ts ? *p.w_ts : 1.0f);
-    const int64_t units_all = static_cast<int64_t>(p.num_tiles) * ur.nkb;
-    const int64_t grid = gridDim.x;
-    auto contributor = [&](int64_t u) { return static_cast<int>(((u + 1) * grid - 1) / units_all); };
-    auto first_tile = [&](int c) { return static_cast<int>(units_all * c / grid / ur.nkb); };
+    const int grid = static_cast<int>(gridDim.x);
+    auto first_tile = [&](int c) { return ur.first_split_tile(c, grid); };
     auto store_c = [&](int m, int n, float v) {
       if (p.out_bf16)
         reinterpret_cast<__nv_bfloat16*>(p.c)[static_cast<int64_t>(m) * p.ldc + n] =
@@ -575,8 +613,12 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       const int col = quad * 32 + lane;
       const int n = t * Cfg::kBM + col;
       const bool n_ok = n < p.n;
-      const int cf = contributor(static_cast<int64_t>(t) * ur.nkb);
-      const int cl = contributor(static_cast<int64_t>(t + 1) * ur.nkb - 1);
+      // Contributors of a split tile (whole tiles: this CTA alone).
+      const bool split = order.split(seg);
+      const int cf = split ? ur.contributor(static_cast<int64_t>(t) * ur.nkb, grid)
+                           : static_cast<int>(blockIdx.x);
+      const int cl = split ? ur.contributor(static_cast<int64_t>(t + 1) * ur.nkb - 1, grid)
+                           : static_cast<int>(blockIdx.x);
       float* mine = p.part + static_cast<int64_t>(blockIdx.x * 2 + (t == my_first ? 0 : 1)) *
                                  p.m * Cfg::kBM;
       // TMEM reads queue behind the MMAs already issued for the next
