@@ -638,6 +638,8 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       float* dstf = whole ? reinterpret_cast<float*>(p.c) + n : mine + col;
       __nv_bfloat16* dstb = reinterpret_cast<__nv_bfloat16*>(p.c) + n;
       const int mrows = p.m;
+      const int n_tail = t * Cfg::kBM + quad * 32;
+      const bool bf16_tail = bf16_dst && seg == order.nseg() - 1 && p.vec_ok && n_tail + 32 <= p.n;
 #pragma unroll
       for (int gc = 0; gc < kN / kGroup; ++gc) {
         uint32_t r[kGroup];
@@ -653,6 +655,30 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
         }
         if (gc == 0 && quad == 0 && lane == 0) trace(p, 110 + seg);
         if (!st_ok) continue;
+        if (bf16_tail) {
+          // Final segment (a whole tile): the stage ring is idle (every load
+          // has been consumed by the MMAs this wait covered), so this warp
+          // transposes its 32 columns x kGroup rows through it and writes C
+          // in 16-byte row pieces: 8 lanes' worth of stores per row instead
+          // of one 2-byte store per lane and row.
+          uint8_t* tbuf = smem + quad * (kGroup * 64);
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < kGroup; ++j)
+            *reinterpret_cast<__nv_bfloat16*>(tbuf + j * 64 + lane * 2) =
+                __float2bfloat16_rn(__uint_as_float(r[j]) * scale);
+          __syncwarp();
+          const int c16 = (lane & 3) * 16;
+          uint8_t* crow = reinterpret_cast<uint8_t*>(p.c) + static_cast<int64_t>(n_tail) * 2 + c16;
+#pragma unroll
+          for (int it = 0; it < kGroup / 8; ++it) {
+            const int row = it * 8 + (lane >> 2);
+            const int mm = gc * kGroup + row;
+            const uint4 v = *reinterpret_cast<const uint4*>(tbuf + row * 64 + c16);
+            if (mm < mrows) *reinterpret_cast<uint4*>(crow + static_cast<int64_t>(mm) * p.ldc * 2) = v;
+          }
+          continue;
+        }
         if (bf16_dst) {
 #pragma unroll
           for (int j = 0; j < kGroup; ++j)
@@ -670,18 +696,23 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       }
       if (quad == 0 && lane == 0) trace(p, 100 + seg);
       if (cf == cl) continue;
-      __threadfence();
+      // Publish the slice and count this contributor with one acquire-release
+      // atomic from lane 0: the warp barrier before it orders every lane's
+      // slice stores ahead of the release (fence cumulativity), the one after
+      // it orders every lane's slice reads behind the acquire.  Two full
+      // fences here each cost ~2 us while the weight stream loads the memory
+      // system.
       if (quad == 0 && lane == 0) trace(p, 300 + 4 * seg);
       __syncwarp();
       uint32_t old = 0;
-      if (lane == 0) old = atomicAdd(&p.cnt[t * 4 + quad], 1u);
+      if (lane == 0) old = atom_add_acq_rel_gpu(&p.cnt[t * 4 + quad], 1u);
       old = __shfl_sync(0xffffffffu, old, 0);
+      __syncwarp();
       if (quad == 0 && lane == 0) trace(p, 301 + 4 * seg);
       if (old != static_cast<uint32_t>(cl - cf)) continue;
-      __threadfence();
       if (quad == 0 && lane == 0) trace(p, 302 + 4 * seg);
       // Sum pass: a lane takes 8 adjacent columns of one row, a warp
-      // instruction 8 rows x 32 columns; 4 steps x 2 contributors x 32 bytes
+      // instruction 8 rows x 32 columns; 4 steps x 3 contributors x 32 bytes
       // are in flight per lane before the adds (in contributor order), and
       // each step ends in one 16-byte (bf16) or two (fp32) stores per lane.
       {
@@ -697,13 +728,18 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
 #pragma unroll
             for (int e = 0; e < 8; ++e) acc[i][e] = 0.0f;
 #pragma unroll 1
-          for (int c = cf; c <= cl; c += 2) {
-            const bool two = c + 1 <= cl;
+          for (int c = cf; c <= cl; c += 3) {
+            // Up to three contributors' loads in flight at once (a split
+            // tile has two or three): one memory round per 32 rows.
+            const bool two = c + 1 <= cl, three = c + 2 <= cl;
             const float* s0 = p.part + (c * 2 + (t == first_tile(c) ? 0 : 1)) * slice + quad * 32 + c8;
             const float* s1 = two ? p.part + ((c + 1) * 2 + (t == first_tile(c + 1) ? 0 : 1)) * slice +
                                         quad * 32 + c8
                                   : s0;
-            float4 v0[4][2], v1[4][2];
+            const float* s2 = three ? p.part + ((c + 2) * 2 + (t == first_tile(c + 2) ? 0 : 1)) * slice +
+                                          quad * 32 + c8
+                                    : s0;
+            float4 v0[4][2], v1[4][2], v2[4][2];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int m = m0 + i * 8 + sub;
@@ -714,6 +750,8 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
                               : make_float4(0.f, 0.f, 0.f, 0.f);
                 v1[i][h] = ok && two ? __ldcg(reinterpret_cast<const float4*>(s1 + m * Cfg::kBM) + h)
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                v2[i][h] = ok && three ? __ldcg(reinterpret_cast<const float4*>(s2 + m * Cfg::kBM) + h)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
               }
             }
 #pragma unroll
@@ -725,6 +763,10 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
                 if (two) {
                   acc[i][4 * h] += v1[i][h].x; acc[i][4 * h + 1] += v1[i][h].y;
                   acc[i][4 * h + 2] += v1[i][h].z; acc[i][4 * h + 3] += v1[i][h].w;
+                }
+                if (three) {
+                  acc[i][4 * h] += v2[i][h].x; acc[i][4 * h + 1] += v2[i][h].y;
+                  acc[i][4 * h + 2] += v2[i][h].z; acc[i][4 * h + 3] += v2[i][h].w;
                 }
               }
           }

@@ -124,6 +124,13 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   return v;
 }
 
+// Atomic add with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // One thread per CTA: publish this CTA's prior global writes (generic and
 // async proxy), count it in *ctr and wait, bounded, until `expected` CTAs
 // have arrived.  On timeout records `code` and raises *abort_flag.
