@@ -86,6 +86,14 @@ struct UnitRange {
     nkb = num_kb;
     wn = num_tiles / g;
     split_tiles = num_tiles - wn * g;
+    // Every CTA must own at least one split unit when there is a split
+    // region (the contributor count of a split tile assumes it): with fewer
+    // split units than CTAs, fall back to stream-K over all units (the host
+    // launches at most num_tiles * num_kb CTAs).
+    if (split_tiles > 0 && split_tiles * nkb < g) {
+      wn = 0;
+      split_tiles = num_tiles;
+    }
     split_units = split_tiles * nkb;
     su0 = static_cast<int>(static_cast<int64_t>(split_units) * c / g);
     su1 = static_cast<int>(static_cast<int64_t>(split_units) * (c + 1) / g);

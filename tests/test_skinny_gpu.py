@@ -101,3 +101,14 @@ def test_skinny_workspace_reuse_and_determinism(qlib, oracle):
     # Counters are left zero (the trailing grid-arrival words included).
     fresh = qlib.gemm_nvfp4_skinny(xs[0], W, torch.float32)
     assert torch.equal(fresh, outs[0])
+
+
+@pytest.mark.parametrize("m,n,k", [(16, 19968, 1024),   # 156 tiles: too few split units, all stream-K
+                                   (32, 51200, 1024),   # 400 tiles: 2 whole tiles per CTA + split rest
+                                   (64, 38016, 512)])   # 297 tiles, one unit each: all stream-K
+def test_skinny_schedules(qlib, oracle, m, n, k):
+    """Both work decompositions (whole tiles + stream-K remainder, and pure
+    stream-K when the remainder has fewer units than CTAs), sampled columns
+    in every weight tile."""
+    cols = np.unique(np.concatenate([np.arange(0, n, 61), np.arange(n - 128, n)]))
+    run_case(qlib, oracle, m, n, k, torch.bfloat16, cols=cols)
