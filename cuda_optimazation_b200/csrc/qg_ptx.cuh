@@ -139,8 +139,11 @@ __device__ __forceinline__ bool grid_arrive_wait(uint32_t* ctr, uint32_t expecte
                                                  volatile uint32_t* abort_flag, uint32_t* status,
                                                  uint32_t code) {
   asm volatile("fence.proxy.async.global;" ::: "memory");
-  __threadfence();
-  atomicAdd(ctr, 1u);
+  // One release reduction publishes the CTA's writes (ordered before it by
+  // the caller's CTA barrier; release is cumulative) and counts the arrival:
+  // a full fence followed by the atomic costs one more memory round trip,
+  // ~2 us while the weight stream loads the memory system.
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
   const uint64_t t0 = globaltimer_ns();
   while (ld_acquire_gpu(ctr) < expected) {
     if (*abort_flag) return false;
