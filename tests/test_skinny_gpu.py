@@ -103,6 +103,24 @@ def test_skinny_workspace_reuse_and_determinism(qlib, oracle):
     assert torch.equal(fresh, outs[0])
 
 
+def test_skinny_workspace_shared_across_shapes(qlib, oracle):
+    """One workspace sized for the largest call serves smaller m and k: the
+    activation scales left by a larger call (rows >= m, columns >= k/16) are
+    never rewritten and must not change the smaller call's result."""
+    n = 4096
+    ws = qlib.skinny_workspace(128, n, 2048, "cuda")
+    out = {}
+    for m, k in ((128, 2048), (16, 1056), (64, 2048), (16, 1056)):
+        xw = oracle.normal(n * k, 11, 0.0, 0.02).reshape(n, k)
+        W = qlib.make_nvfp4(torch.from_numpy(xw).cuda())
+        x = activations(oracle, m, k, 3).cuda()
+        got = qlib.gemm_nvfp4_skinny(x, W, torch.float32, workspace=ws)
+        fresh = qlib.gemm_nvfp4_skinny(x, W, torch.float32)
+        assert torch.equal(got, fresh), (m, k)
+        out.setdefault((m, k), []).append(got)
+    assert torch.equal(*out[(16, 1056)])
+
+
 @pytest.mark.parametrize("m,n,k", [(16, 19968, 1024),   # 156 tiles: too few split units, all stream-K
                                    (32, 51200, 1024),   # 400 tiles: 2 whole tiles per CTA + split rest
                                    (64, 38016, 512)])   # 297 tiles, one unit each: all stream-K
