@@ -131,14 +131,15 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v
   return old;
 }
 
-// One thread per CTA: publish this CTA's prior global writes (generic and
-// async proxy), count it in *ctr and wait, bounded, until `expected` CTAs
-// have arrived.  On timeout records `code` and raises *abort_flag.
+// One thread per CTA: publish this CTA's prior global writes (generic
+// proxy; writers whose data a TMA load reads fence the async proxy
+// themselves, and so does the thread that issues those loads), count it in
+// *ctr and wait, bounded, until `expected` CTAs have arrived.  On timeout
+// records `code` and raises *abort_flag.
 __device__ __forceinline__ bool grid_arrive_wait(uint32_t* ctr, uint32_t expected,
                                                  uint64_t timeout_ns,
                                                  volatile uint32_t* abort_flag, uint32_t* status,
                                                  uint32_t code) {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
   // One release reduction publishes the CTA's writes (ordered before it by
   // the caller's CTA barrier; release is cumulative) and counts the arrival:
   // a full fence followed by the atomic costs one more memory round trip,
@@ -153,7 +154,6 @@ __device__ __forceinline__ bool grid_arrive_wait(uint32_t* ctr, uint32_t expecte
       return false;
     }
   }
-  asm volatile("fence.proxy.async.global;" ::: "memory");
   return true;
 }
 
