@@ -64,3 +64,39 @@ def test_gather_and_ipc_argument_validation_without_gpu(qlib):
     assert L.qg_ipc_import(None, None) == qlib.ERR_ARG
     assert L.qg_ipc_close(ctypes.c_void_p(4096)) == qlib.ERR_ARG  # never imported
     assert qlib.IPC_HANDLE_BYTES == 72 and qlib.MAX_RANKS == 8
+
+
+def test_new_entry_points_validate_without_gpu(qlib):
+    """MXFP4 quantizer / GEMM, MX repack, NVFP4-output GEMM and the e2m1
+    self test reject bad arguments before any CUDA call (fake, aligned
+    addresses are never dereferenced)."""
+    L = qlib.lib()
+    a, mis = 4096, 4104  # 16-byte aligned / misaligned fake device addresses
+    # qg_quantize_mxfp4(x, dtype, rows, k, layout, q, sf, stream)
+    assert L.qg_quantize_mxfp4(None, 0, 1, 32, 1, a, a, None) == qlib.ERR_ARG
+    assert L.qg_quantize_mxfp4(a, 9, 1, 32, 1, a, a, None) == qlib.ERR_DTYPE
+    assert L.qg_quantize_mxfp4(a, 0, 1, 32, 5, a, a, None) == qlib.ERR_LAYOUT
+    assert L.qg_quantize_mxfp4(a, 0, 1, 48, 1, a, a, None) == qlib.ERR_SHAPE
+    assert L.qg_quantize_mxfp4(mis, 0, 1, 32, 1, a, a, None) == qlib.ERR_ALIGN
+    # qg_gemm_mxfp4(a_q, a_sf, b_q, b_sf, c, c_dtype, m, n, k, ldc, sf_layout, status, stream)
+    assert L.qg_gemm_mxfp4(None, a, a, a, a, 1, 256, 256, 256, 256, 1, None, None) == qlib.ERR_ARG
+    assert L.qg_gemm_mxfp4(a, a, a, a, a, 3, 256, 256, 256, 256, 1, None, None) == qlib.ERR_DTYPE
+    assert L.qg_gemm_mxfp4(a, a, a, a, a, 1, 256, 256, 256, 256, 0, None, None) == qlib.ERR_LAYOUT
+    assert L.qg_gemm_mxfp4(a, a, a, a, a, 1, 256, 256, 48, 256, 1, None, None) == qlib.ERR_SHAPE
+    assert L.qg_gemm_mxfp4(mis, a, a, a, a, 1, 256, 256, 256, 256, 1, None, None) == qlib.ERR_ALIGN
+    # qg_repack_mx(bits, src_q, src_sf, src_layout, dst_q, dst_sf, dst_layout, rows, k, stream)
+    assert L.qg_repack_mx(4, None, a, 0, a, a, 1, 128, 64, None) == qlib.ERR_ARG
+    assert L.qg_repack_mx(6, a, a, 0, a, a, 1, 128, 64, None) == qlib.ERR_DTYPE
+    assert L.qg_repack_mx(4, a, a, 3, a, a, 1, 128, 64, None) == qlib.ERR_LAYOUT
+    assert L.qg_repack_mx(8, a, a, 0, a, a, 1, 128, 48, None) == qlib.ERR_SHAPE
+    assert L.qg_repack_mx(4, mis, a, 0, a, a, 1, 128, 64, None) == qlib.ERR_ALIGN
+    # qg_gemm_nvfp4_requant(..., out_ts, out_q, out_sf, out_layout, out_amax, m, n, k, ...)
+    assert L.qg_gemm_nvfp4_requant(a, a, None, a, a, None, None, None, a, 0, None, 128, 128, 128,
+                                   1, None, None) == qlib.ERR_ARG
+    assert L.qg_gemm_nvfp4_requant(a, a, None, a, a, None, None, a, a, 4, None, 128, 128, 128,
+                                   1, None, None) == qlib.ERR_LAYOUT
+    assert L.qg_gemm_nvfp4_requant(a, a, None, a, a, None, None, a, a, 0, None, 128, 40, 128,
+                                   1, None, None) == qlib.ERR_SHAPE
+    assert L.qg_gemm_nvfp4_requant(a, a, None, a, a, None, None, mis, a, 0, None, 128, 128, 128,
+                                   1, None, None) == qlib.ERR_ALIGN
+    assert L.qg_selftest_e2m1_cvt(None, None) == qlib.ERR_ARG
