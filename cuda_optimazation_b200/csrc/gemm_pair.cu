@@ -10,11 +10,11 @@
 // loads its own 128 rows of A and its own 128-row half of B; the leader CTA
 // (rank 0) issues tcgen05.mma.cta_group::2, which reads A and B from both
 // CTAs' shared memory and accumulates rows [0,128) in the leader's TMEM and
-// rows [128,256) in the peer's.  Two leader threads (warps 1 and
-// 10) issue M = 256, N = 128 MMAs into the two halves of the accumulator:
-// measured, one issuing thread spends ~56 ns per MMA plus ~150 ns per stage
-// on waits and commits, more than the 4 x 69 ns the tensor pipe needs for a
-// stage at N = 256, and issues from two warps overlap.
+// rows [128,256) in the peer's.  One leader thread (warp 1) issues
+// M = 256, N = 256 MMAs; a build with QG_PAIR_ISSUERS=2 splits the issue over
+// warps 1 and 10 (N = 128 halves of the accumulator), which re-reads each
+// CTA's A tile from shared memory per half and measured slower once the
+// epilogue hands the accumulator back early (see PairCfg::kIssuers).
 //
 // Scale factors reach TMEM through tcgen05.st from registers, not through
 // tcgen05.cp: copy instructions execute in the tensor pipe in order with the
@@ -30,7 +30,7 @@
 //               bytes and its own scale bytes); the peer's scale loads
 //               complete on its own sf_full barrier.
 //   warp 1      TMEM allocation for the pair; in the leader, MMA issuer 0.
-//   warp 10     in the leader, MMA issuer 1.
+//   warp 10     in the leader, MMA issuer 1 (two-issuer builds only).
 //   warps 2..5  epilogue: each CTA drains its own accumulator rows.
 //   warps 6..9  scale stagers.
 //   warps 11..14 (NVFP4-output kernel only) more epilogue warps.
@@ -79,10 +79,16 @@ struct PairCfg {
   static constexpr int kTmemCols = 512;
   static_assert(kTmemSfBase + kStages * kTmemSfStageCols <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
-  // Two MMA issuers in the leader, each owning one N = 128 half of the
-  // accumulator (a single issuing thread cannot keep the tensor pipe busy
-  // at 4 MMAs per stage).
-  static constexpr int kIssuers = 2;
+  // One MMA issuer with N = 256 MMAs by default: each CTA's tensor core
+  // then reads its A tile once per K step.  Two issuers (N = 128 halves,
+  // QG_PAIR_ISSUERS=2 at build time) read it twice; measured on one box with
+  // the eight-warp epilogue, one issuer is faster in every format (NVFP4
+  // 8192^3 4693 -> 4990 TF/s, MXFP4 5156 -> 5235, MXFP8 2424 -> 2450).
+#ifdef QG_PAIR_ISSUERS
+  static constexpr int kIssuers = QG_PAIR_ISSUERS;
+#else
+  static constexpr int kIssuers = 1;
+#endif
   static constexpr int kIssueN = kBN / kIssuers;
   static constexpr int kThreads = 320 + 32 * (kIssuers - 1);
 };
@@ -465,7 +471,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster_relaxed(h ? acc_empty_leader1 : acc_empty_leader0);
+          // Two issuers: each 128-column half goes back on its own barrier;
+          // one issuer: the accumulator goes back once both halves are read.
+          if (lane == 0 && (Cfg::kIssuers == 2 || h == 1))
+            mbar_arrive_cluster_relaxed(h ? acc_empty_leader1 : acc_empty_leader0);
           const int col0 = n0 + tmem_block(tb) * 64;
           if (!row_ok || col0 >= p.n) continue;
           uint32_t w[8];
@@ -538,7 +547,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster_relaxed(h ? acc_empty_leader1 : acc_empty_leader0);
+          // Two issuers: each 128-column half goes back on its own barrier;
+          // one issuer: the accumulator goes back once both halves are read.
+          if (lane == 0 && (Cfg::kIssuers == 2 || h == 1))
+            mbar_arrive_cluster_relaxed(h ? acc_empty_leader1 : acc_empty_leader0);
           uint4 v[8];
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
