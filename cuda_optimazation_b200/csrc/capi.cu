@@ -13,6 +13,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <new>
 
 #include "../../include/qgemm.h"
 #include "qg_gemm.h"
@@ -171,11 +172,33 @@ struct Requant {
   int layout = 0;
 };
 
+// A GEMM call with everything host-side done: shapes checked, tensor maps
+// encoded, kernel variant and grid chosen.  gemm_launch() enqueues it;
+// qg_plan keeps one to skip the host work on repeated calls.
+struct PreparedGemm {
+  GemmParams p;
+  int fmt = 1;
+  bool fp4 = true, pair = true, out_bf16 = false;
+  int variant = 1, out_kind = 0, grid = 0;
+  void* memset_ptr = nullptr;  // scale padding to clear before each launch
+  size_t memset_bytes = 0;
+};
+
+cudaError_t gemm_launch(const PreparedGemm& g, cudaStream_t stream) {
+  if (g.memset_bytes) {
+    cudaError_t e = cudaMemsetAsync(g.memset_ptr, 0, g.memset_bytes, stream);
+    if (e != cudaSuccess) return e;
+  }
+  if (g.pair) return launch_gemm_pair(g.p, g.fmt, g.out_kind, g.grid, stream);
+  return g.variant == 2 ? launch_gemm_blockscaled(g.p, g.fp4, g.out_bf16, g.grid, stream)
+                        : launch_gemm_solo(g.p, g.fp4, g.out_bf16, g.grid, stream);
+}
+
 // fmt: 0 MXFP8, 1 NVFP4, 2 MXFP4 (pair kernel only).
-int gemm_common(int fmt, const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
-                const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
-                int64_t k, int64_t ldc, int sf_layout, uint32_t* status, cudaStream_t stream,
-                const Gather& gather = Gather(), const Requant& requant = Requant()) {
+int gemm_prepare(int fmt, const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
+                 const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
+                 int64_t k, int64_t ldc, int sf_layout, uint32_t* status, PreparedGemm* out,
+                 const Gather& gather = Gather(), const Requant& requant = Requant()) {
   const bool rq = requant.q != nullptr;
   const bool fp4 = fmt != 0;
   if (!a_q || !a_sf || !b_q || !b_sf || (!c && !rq)) return QG_ERR_ARG;
@@ -199,7 +222,7 @@ int gemm_common(int fmt, const void* a_q, const void* a_sf, const float* a_ts, c
   const int box_a = pair ? tm / 2 : tm;
   const int box_b = pair ? tn / 2 : tn;
   const int chunks = pair ? pair_sf_chunks_per_stage(fmt) : gemm_sf_chunks_per_stage(fp4);
-  GemmParams p;
+  GemmParams& p = out->p;
   std::memset(&p, 0, sizeof(p));
   if (!make_operand_map(&p.tm_a, a_q, m, row_bytes, box_a)) return QG_ERR_CUDA;
   if (!make_operand_map(&p.tm_b, b_q, n, row_bytes, box_b)) return QG_ERR_CUDA;
@@ -228,6 +251,11 @@ int gemm_common(int fmt, const void* a_q, const void* a_sf, const float* a_ts, c
     p.n_out = 1;
   }
   if (rq) {
+    // Padded scale slots of the MMA layouts must read as zero scales.
+    if (requant.layout != QG_LAYOUT_REF_LINEAR && ((m % 128) != 0 || ((n / 16) % 4) != 0)) {
+      out->memset_ptr = requant.sf;
+      out->memset_bytes = static_cast<size_t>(qg_scale_bytes(m, n, 16));
+    }
     p.vec_ok = 0;
     p.n_out = 0;
     p.rq_q = requant.q;
@@ -244,21 +272,32 @@ int gemm_common(int fmt, const void* a_q, const void* a_sf, const float* a_ts, c
   p.timeout_ns = default_timeout_ns();
   p.diag = diag_flags();
   const int64_t tiles = static_cast<int64_t>(p.num_m_tiles) * p.num_n_tiles;
-  cudaError_t e;
+  out->fmt = fmt;
+  out->fp4 = fp4;
+  out->pair = pair;
+  out->variant = variant;
+  out->out_bf16 = c_dtype == QG_DTYPE_BF16;
   if (pair) {
     const int64_t pairs = num_sms() / 2;
-    const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
+    out->grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
     // bf16 through TMA stores: the eight-warp epilogue (kind 3), unless
     // QG_PAIR_EPI=4 asks for the four-warp one (A/B measurements).
-    const int out_kind = rq ? 2
-                            : (c_dtype == QG_DTYPE_BF16 ? (p.n_out > 0 && pair_epi8() ? 3 : 1) : 0);
-    e = launch_gemm_pair(p, fmt, out_kind, grid, stream);
+    out->out_kind = rq ? 2 : (out->out_bf16 ? (p.n_out > 0 && pair_epi8() ? 3 : 1) : 0);
   } else {
-    const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-    e = variant == 2 ? launch_gemm_blockscaled(p, fp4, c_dtype == QG_DTYPE_BF16, grid, stream)
-                            : launch_gemm_solo(p, fp4, c_dtype == QG_DTYPE_BF16, grid, stream);
+    out->grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
   }
-  return e == cudaSuccess ? QG_OK : QG_ERR_CUDA;
+  return QG_OK;
+}
+
+int gemm_common(int fmt, const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
+                const void* b_sf, const float* b_ts, void* c, int c_dtype, int64_t m, int64_t n,
+                int64_t k, int64_t ldc, int sf_layout, uint32_t* status, cudaStream_t stream,
+                const Gather& gather = Gather(), const Requant& requant = Requant()) {
+  PreparedGemm g;
+  const int rc = gemm_prepare(fmt, a_q, a_sf, a_ts, b_q, b_sf, b_ts, c, c_dtype, m, n, k, ldc,
+                              sf_layout, status, &g, gather, requant);
+  if (rc != QG_OK) return rc;
+  return gemm_launch(g, stream) == cudaSuccess ? QG_OK : QG_ERR_CUDA;
 }
 
 }  // namespace
@@ -279,6 +318,11 @@ int num_sms() {
 }  // namespace qg
 
 using namespace qg;
+
+struct qg_plan_st {
+  qg::PreparedGemm gemm;
+  int device = 0;
+};
 
 extern "C" {
 
@@ -414,13 +458,6 @@ int qg_gemm_nvfp4_requant(const void* a_q, const void* a_sf, const float* a_ts, 
       (out_amax && (reinterpret_cast<uintptr_t>(out_amax) & 3u)))
     return QG_ERR_ALIGN;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (out_layout != QG_LAYOUT_REF_LINEAR && m > 0 && ((m % 128) != 0 || ((n / 16) % 4) != 0) &&
-      k >= 32 && (k % 32) == 0 && a_q && a_sf && b_q && b_sf) {
-    // Padded scale slots of the MMA layouts must read as zero scales.
-    if (cudaMemsetAsync(out_sf, 0, static_cast<size_t>(qg_scale_bytes(m, n, 16)), s) !=
-        cudaSuccess)
-      return QG_ERR_CUDA;
-  }
   Requant r;
   r.q = static_cast<uint8_t*>(out_q);
   r.sf = static_cast<uint8_t*>(out_sf);
@@ -429,6 +466,41 @@ int qg_gemm_nvfp4_requant(const void* a_q, const void* a_sf, const float* a_ts, 
   r.layout = out_layout;
   return gemm_common(1, a_q, a_sf, a_ts, b_q, b_sf, b_ts, nullptr, QG_DTYPE_F32, m, n, k, n,
                      sf_layout, status, s, Gather(), r);
+}
+
+int qg_plan_create_gemm(qg_plan* plan, int format, const void* a_q, const void* a_sf,
+                        const float* a_ts, const void* b_q, const void* b_sf, const float* b_ts,
+                        void* c, int c_dtype, int64_t m, int64_t n, int64_t k, int64_t ldc,
+                        int sf_layout, uint32_t* status) {
+  if (!plan) return QG_ERR_ARG;
+  *plan = nullptr;
+  if (format < QG_FORMAT_MXFP8 || format > QG_FORMAT_MXFP4) return QG_ERR_DTYPE;
+  qg_plan_st* pl = new (std::nothrow) qg_plan_st();
+  if (!pl) return QG_ERR_ARG;
+  const int rc = gemm_prepare(format, a_q, a_sf, a_ts, b_q, b_sf, b_ts, c, c_dtype, m, n, k, ldc,
+                              sf_layout, status, &pl->gemm);
+  if (rc != QG_OK || cudaGetDevice(&pl->device) != cudaSuccess) {
+    delete pl;
+    return rc != QG_OK ? rc : QG_ERR_CUDA;
+  }
+  *plan = pl;
+  return QG_OK;
+}
+
+int qg_plan_run(qg_plan plan, qg_stream_t stream) {
+  if (!plan) return QG_ERR_ARG;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return QG_ERR_CUDA;
+  if (dev != plan->device) return QG_ERR_ARG;
+  return gemm_launch(plan->gemm, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? QG_OK
+             : QG_ERR_CUDA;
+}
+
+int qg_plan_destroy(qg_plan plan) {
+  if (!plan) return QG_ERR_ARG;
+  delete plan;
+  return QG_OK;
 }
 
 int qg_gemm_mxfp4(const void* a_q, const void* a_sf, const void* b_q, const void* b_sf, void* c,

@@ -32,6 +32,8 @@ OK, ERR_SHAPE, ERR_ALIGN, ERR_LAYOUT, ERR_DTYPE, ERR_CUDA, ERR_TIMEOUT, ERR_ARG,
 DTYPE_F32, DTYPE_BF16 = 0, 1
 # qg_layout
 LAYOUT_REF_LINEAR, LAYOUT_MMA, LAYOUT_MMA_KMAJOR = 0, 1, 2
+# qg_format
+FORMAT_MXFP8, FORMAT_NVFP4, FORMAT_MXFP4 = 0, 1, 2
 
 _VP, _I64, _I32, _U64 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint64
 
@@ -65,6 +67,10 @@ SIGNATURES = {
     "qg_ipc_import": (_I32, [_VP, _VP]),
     "qg_ipc_close": (_I32, [_VP]),
     "qg_read_status": (_I32, [_VP, _VP, _VP]),
+    "qg_plan_create_gemm": (_I32, [_VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I32, _I64,
+                                   _I64, _I64, _I64, _I32, _VP]),
+    "qg_plan_run": (_I32, [_VP, _VP]),
+    "qg_plan_destroy": (_I32, [_VP]),
     "qg_selftest_e2m1_cvt": (_I32, [_VP, _VP]),
     "qg_selftest_wait_timeout": (_I32, [_U64, _VP, _VP]),
 }
@@ -327,6 +333,53 @@ def gemm_nvfp4_requant(a: Nvfp4Result, b: Nvfp4Result, out_ts: torch.Tensor,
                            b.block_scales, b.tensor_scale, out_ts, q, sf, m, n, k, out_layout,
                            a.layout, out_amax, status, stream)
     return Nvfp4Result(q, sf, out_ts, m, n, out_layout)
+
+
+class GemmPlan:
+    """A ``qg_plan``: one GEMM call C = A . B^T bound to fixed buffers, its
+    host work (checks, tensor-map encodes, kernel choice) done once;
+    ``run()`` only enqueues the kernel and reads the operands' current
+    contents.  The tensors are kept alive by the plan."""
+
+    def __init__(self, a, b, out: torch.Tensor, status: Optional[torch.Tensor] = None):
+        if type(a) is not type(b) or a.k != b.k or a.layout != b.layout:
+            raise ValueError("operands must share format, K and layout")
+        fmt = {Nvfp4Result: FORMAT_NVFP4, Mxfp8Result: FORMAT_MXFP8,
+               Mxfp4Result: FORMAT_MXFP4}[type(a)]
+        ats = a.tensor_scale if fmt == FORMAT_NVFP4 else None
+        bts = b.tensor_scale if fmt == FORMAT_NVFP4 else None
+        self._keep = (a, b, out, status)
+        self._h = ctypes.c_void_p()
+        rc = lib().qg_plan_create_gemm(ctypes.byref(self._h), fmt, a.quantized.data_ptr(),
+                                       a.block_scales.data_ptr(), _ptr(ats), b.quantized.data_ptr(),
+                                       b.block_scales.data_ptr(), _ptr(bts), out.data_ptr(),
+                                       _dtype_code(out), a.rows, b.rows, a.k, out.stride(0),
+                                       a.layout, _ptr(status))
+        _check(rc, "qg_plan_create_gemm")
+        self.out = out
+
+    def run(self, stream=None) -> torch.Tensor:
+        if not self._h:
+            raise RuntimeError("plan is closed")
+        _check(lib().qg_plan_run(self._h, _stream(stream)), "qg_plan_run")
+        return self.out
+
+    def close(self) -> None:
+        if self._h:
+            lib().qg_plan_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def skinny_workspace(m: int, n: int, k: int, device) -> torch.Tensor:

@@ -212,6 +212,27 @@ int qg_gemm_mxfp4(const void* a_q, const void* a_sf, const void* b_q, const void
                   int c_dtype, int64_t m, int64_t n, int64_t k, int64_t ldc, int sf_layout,
                   uint32_t* status, qg_stream_t stream);
 
+/* ---- Plans: the host work of a GEMM call done once --------------------
+ * A plan binds one GEMM call -- operands, output, shapes, layout -- and
+ * does its host work once: argument checks, TMA tensor-map encodes, kernel
+ * and grid choice.  qg_plan_run() then only enqueues the kernel, for loops
+ * that repeat the same call (a decode step, a layer) on buffers whose
+ * contents change between runs.  A plan lives in host memory (no device
+ * allocation), belongs to the device current at creation (run it with that
+ * device current) and reads the operands at run time, not at creation.
+ * format: QG_FORMAT_NVFP4 (a_ts / b_ts as qg_gemm_nvfp4), QG_FORMAT_MXFP8,
+ * QG_FORMAT_MXFP4 (tensor scales ignored); other arguments and rules as
+ * the matching qg_gemm_* entry point.  No reference counterpart (the
+ * reference's runners re-create their state per launch). */
+typedef struct qg_plan_st* qg_plan;
+typedef enum { QG_FORMAT_MXFP8 = 0, QG_FORMAT_NVFP4 = 1, QG_FORMAT_MXFP4 = 2 } qg_format;
+int qg_plan_create_gemm(qg_plan* plan, int format, const void* a_q, const void* a_sf,
+                        const float* a_ts, const void* b_q, const void* b_sf, const float* b_ts,
+                        void* c, int c_dtype, int64_t m, int64_t n, int64_t k, int64_t ldc,
+                        int sf_layout, uint32_t* status);
+int qg_plan_run(qg_plan plan, qg_stream_t stream);
+int qg_plan_destroy(qg_plan plan);
+
 /* Decode-shaped NVFP4 GEMM with the activation quantisation fused into the
  * call: x (m x k, bf16 or fp32, m <= 128) is quantised to NVFP4 exactly as
  * qg_quantize_nvfp4 would, then C[m, n] = (ts_x * w_ts) * x_q . w_q^T with the

@@ -100,3 +100,21 @@ def test_new_entry_points_validate_without_gpu(qlib):
     assert L.qg_gemm_nvfp4_requant(a, a, None, a, a, None, None, mis, a, 0, None, 128, 128, 128,
                                    1, None, None) == qlib.ERR_ALIGN
     assert L.qg_selftest_e2m1_cvt(None, None) == qlib.ERR_ARG
+
+
+def test_plan_argument_validation_without_gpu(qlib):
+    import ctypes
+    L = qlib.lib()
+    h = ctypes.c_void_p()
+    a = 4096
+    assert L.qg_plan_create_gemm(None, 1, a, a, None, a, a, None, a, 1, 256, 256, 256, 256, 1,
+                                 None) == qlib.ERR_ARG
+    assert L.qg_plan_create_gemm(ctypes.byref(h), 7, a, a, None, a, a, None, a, 1, 256, 256, 256,
+                                 256, 1, None) == qlib.ERR_DTYPE
+    assert L.qg_plan_create_gemm(ctypes.byref(h), 1, None, a, None, a, a, None, a, 1, 256, 256,
+                                 256, 256, 1, None) == qlib.ERR_ARG
+    assert L.qg_plan_create_gemm(ctypes.byref(h), 0, a, a, None, a, a, None, a, 1, 256, 256, 48,
+                                 256, 1, None) == qlib.ERR_SHAPE
+    assert not h.value  # no plan on failure
+    assert L.qg_plan_run(None, None) == qlib.ERR_ARG
+    assert L.qg_plan_destroy(None) == qlib.ERR_ARG
