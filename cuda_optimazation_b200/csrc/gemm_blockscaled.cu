@@ -314,12 +314,16 @@ template <bool kFp4, bool kOutBf16>
 static cudaError_t launch_one(const GemmParams& p, int grid, cudaStream_t stream) {
   using Cfg = TileCfg<kFp4>;
   auto kern = gemm_blockscaled_kernel<kFp4, kOutBf16>;
-  static bool attr_done = false;  // per template instance; attribute is per function
-  if (!attr_done) {
+  // The attribute belongs to the function in each device's context.
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return cudaErrorInvalidDevice;
+  if (!attr_done[dev]) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    attr_done[dev] = true;
   }
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   return cudaGetLastError();

@@ -736,12 +736,16 @@ template <int kFmt, int kOut>
 static cudaError_t launch_pair_one(const GemmParams& p, int grid, cudaStream_t stream) {
   using Cfg = PairCfg<kFmt>;
   auto kern = gemm_pair_kernel<kFmt, kOut>;
-  static bool attr_done = false;
-  if (!attr_done) {
+  // The attribute belongs to the function in each device's context.
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return cudaErrorInvalidDevice;
+  if (!attr_done[dev]) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    attr_done[dev] = true;
   }
   kern<<<grid, kOut >= 2 ? pair_threads<kOut>() : Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   return cudaGetLastError();

@@ -830,12 +830,16 @@ template <int kN>
 static cudaError_t launch_skinny_n(const SkinnyParams& p, int grid, cudaStream_t stream) {
   using Cfg = SkinnyCfg<kN>;
   auto kern = gemm_skinny_kernel<kN>;
-  static bool attr_done = false;
-  if (!attr_done) {
+  // The attribute belongs to the function in each device's context.
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return cudaErrorInvalidDevice;
+  if (!attr_done[dev]) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    attr_done[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

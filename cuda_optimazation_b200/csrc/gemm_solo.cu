@@ -382,12 +382,16 @@ template <bool kFp4, bool kOutBf16>
 static cudaError_t launch_solo_one(const GemmParams& p, int grid, cudaStream_t stream) {
   using Cfg = SoloCfg<kFp4>;
   auto kern = gemm_solo_kernel<kFp4, kOutBf16>;
-  static bool attr_done = false;
-  if (!attr_done) {
+  // The attribute belongs to the function in each device's context.
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return cudaErrorInvalidDevice;
+  if (!attr_done[dev]) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    attr_done[dev] = true;
   }
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   return cudaGetLastError();

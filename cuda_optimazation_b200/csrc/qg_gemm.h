@@ -7,6 +7,9 @@
 
 namespace qg {
 
+// Devices a process may drive (per-device launch state is kept in arrays).
+constexpr int kMaxDevices = 64;
+
 struct GemmParams {
   CUtensorMap tm_a;    // uint8 [rows][K bytes], box 128 B x kBM, SWIZZLE_128B
   CUtensorMap tm_b;    // uint8 [rows][K bytes], box 128 B x kBN, SWIZZLE_128B
