@@ -11,7 +11,8 @@
 //   3 warm-up + 10 timed launches between CUDA events (:43-44, :1282-1304);
 //   exit status non-zero on a mismatch or a CUDA error (:17-27).
 // Added forms:
-//   quant_gemm_sm110_bench M N K backend [--seed S] [--out-dtype bf16|fp32]
+//   quant_gemm_sm110_bench M N K backend [--gpus 1] [--dist normal] [--seed S]
+//                          [--out-dtype bf16|fp32]
 //   quant_gemm_sm110_bench --m=M --n=N --k=K [--iterations=I] [--swizzle=S]
 //     -- the CUTLASS example 72b command line the sweep runner shells out to
 //     (GEMMquant_sm110/build_and_run.sh:151-176); prints "Disposition:",
@@ -539,7 +540,7 @@ void write_row(std::ofstream& csv, const Row& r, const Options& o) {
 
 void usage(const char* p) {
   std::cerr << "Usage: " << p << " [N] [backend]\n"
-            << "       " << p << " M N K backend [--seed S] [--out-dtype bf16|fp32]\n"
+            << "       " << p << " M N K backend [--gpus 1] [--dist normal] [--seed S] [--out-dtype bf16|fp32]\n"
             << "       " << p << " --m=M --n=N --k=K [--iterations=I] [--swizzle=S]\n"
             << "backends: all|nvfp4_q1_native_fp4_mainloop|mxfp8_q0_tcgen05_block_scaled|"
                "nvfp4_skinny_q0|nvfp4_q0_tc6_fused_epilogue|mxfp4_q0_tcgen05_block_scaled\n"
@@ -559,6 +560,18 @@ bool parse(int argc, char** argv, Options* o) {
     else if (a.rfind("--swizzle=", 0) == 0) {}  // raster hint of the CUTLASS CLI; not used
     else if (a == "--seed" && i + 1 < argc) o->seed = std::strtoull(argv[++i], nullptr, 10);
     else if (a == "--out-dtype" && i + 1 < argc) o->out_bf16 = std::string(argv[++i]) == "bf16";
+    else if (a == "--dist" && i + 1 < argc) {
+      // Inputs are N(0, 1) (weights N(0, 0.02) where stated); no other law.
+      if (std::string(argv[++i]) != "normal") return false;
+    } else if (a == "--gpus" && i + 1 < argc) {
+      // One GPU per process here; the N-sharded multi-GPU runs are
+      // bench.py --workload colpar under torchrun (one process per GPU).
+      if (std::atoi(argv[++i]) != 1) {
+        std::cerr << "--gpus: this binary runs on one GPU; for the column-parallel split use "
+                     "torchrun ... bench.py --gpus P --workload colpar\n";
+        return false;
+      }
+    }
     else if (a == "-h" || a == "--help") return false;
     else pos.push_back(a);
   }

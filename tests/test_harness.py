@@ -27,7 +27,8 @@ def test_bad_arguments_exit_nonzero(binary):
 @pytest.mark.parametrize("args", [["256", "all"], ["1024", "all"],
                                   ["512", "1024", "768", "nvfp4_q1_native_fp4_mainloop",
                                    "--out-dtype", "bf16"],
-                                  ["64", "4096", "2048", "nvfp4_skinny_q0"],
+                                  ["64", "4096", "2048", "nvfp4_skinny_q0", "--gpus", "1",
+                                   "--dist", "normal", "--seed", "7"],
                                   ["512", "768", "1024", "nvfp4_q0_tc6_fused_epilogue"],
                                   ["384", "640", "1024", "mxfp4_q0_tcgen05_block_scaled",
                                    "--out-dtype", "bf16"]])
@@ -66,3 +67,13 @@ def test_cutlass_cli_form_mxfp4_name(binary, tmp_path):
     assert r.returncode == 0, r.stdout + r.stderr
     assert "Backend: mxfp4_q0_tcgen05_block_scaled" in r.stdout
     assert "Disposition: Passed" in r.stdout
+
+
+def test_option_validation_without_gpu(binary):
+    """--dist accepts only the harness's normal law and --gpus only 1 (the
+    multi-GPU split is the column-parallel bench); both fail before any GPU
+    call."""
+    for extra in (["--dist", "uniform"], ["--gpus", "8"]):
+        r = subprocess.run([str(binary), "256", "256", "256", "nvfp4_q1_native_fp4_mainloop",
+                            *extra], capture_output=True, text=True, timeout=60)
+        assert r.returncode != 0 and "Usage" in r.stderr
