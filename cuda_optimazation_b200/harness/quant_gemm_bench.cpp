@@ -32,6 +32,7 @@
 // applies the north-star tolerance: relative Frobenius error <= 1e-5 and
 // |err| <= 1e-3 * ||row||_2 for fp32 output, plus the bf16 rounding bound
 // for bf16 output.
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -81,6 +82,7 @@ struct Options {
   bool cutlass_cli = false;
   int iterations = kRepeat;
   bool square = true;  // N form: CSV column N = n
+  bool reference = true;  // time the cuBLAS reference GEMM
 };
 
 std::vector<float> normal(size_t count, uint64_t seed, float stddev = 1.0f) {
@@ -525,22 +527,72 @@ Row run_requant(const Options& o) {
   return r;
 }
 
-void write_row(std::ofstream& csv, const Row& r, const Options& o) {
-  const double peak_tflops = r.precision.rfind("mxfp8", 0) == 0 ? 4500.0 : 9000.0;
+// The rate reference: a cuBLAS bf16 tensor-core GEMM of the same M x N x K
+// (C = A . B^T, fp32 accumulate), timed like the backends -- the reference
+// harness divides by a cuBLAS tensor-core GEMM timed in the same run
+// (GEMMquant_sm110/src/quant_gemm_bench.cu:1522-1530).  0 when unavailable.
+double cublas_bf16_gflops(const Options& o) {
+  const int64_t m = o.m, n = o.n, k = o.k;
+  void *a = dalloc(m * k * 2), *b = dalloc(n * k * 2), *c = dalloc(m * n * 2);
+  // Seeded values in [-1, 1) (a constant fill lowers the tensor cores' power
+  // draw and flatters the reference's clocks).
+  auto fill = [&](void* dst, int64_t count, uint64_t seed) {
+    std::vector<uint16_t> h(count);
+    uint64_t x = seed * 0x9e3779b97f4a7c15ull + 1;
+    for (auto& v : h) {
+      x ^= x << 13, x ^= x >> 7, x ^= x << 17;
+      const float f = static_cast<float>(static_cast<int64_t>(x >> 40) - (1 << 23)) / (1 << 23);
+      uint32_t bits;
+      std::memcpy(&bits, &f, 4);
+      v = static_cast<uint16_t>(bits >> 16);
+    }
+    CHECK_CUDA(cudaMemcpy(dst, h.data(), count * 2, cudaMemcpyHostToDevice));
+  };
+  fill(a, m * k, o.seed);
+  fill(b, n * k, o.seed ^ 0xbb67ae85ull);
+  double gflops = 0.0;
+  cublasHandle_t h = nullptr;
+  if (cublasCreate(&h) == CUBLAS_STATUS_SUCCESS) {
+    const float alpha = 1.0f, beta = 0.0f;
+    // Row-major C[m][n] = A[m][k] . B[n][k]^T is column-major C^T = B . A^T.
+    auto gemm = [&] {
+      return cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(n), static_cast<int>(m),
+                          static_cast<int>(k), &alpha, b, CUDA_R_16BF, static_cast<int>(k), a,
+                          CUDA_R_16BF, static_cast<int>(k), &beta, c, CUDA_R_16BF,
+                          static_cast<int>(n), CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    };
+    if (gemm() == CUBLAS_STATUS_SUCCESS) {
+      const float ms = time_launches([&] { gemm(); }, o.iterations);
+      gflops = 2.0 * m * n * k / (ms * 1e6);
+    }
+    cublasDestroy(h);
+  }
+  for (void* p : {a, b, c}) cudaFree(p);
+  return gflops;
+}
+
+void write_row(std::ofstream& csv, const Row& r, const Options& o, double ref_gflops) {
+  const double peak_tflops = r.precision.rfind("mxfp8", 0) == 0 ? 4500.0 : 9000.0;  // dense
+  const double ratio = ref_gflops > 0.0 ? r.gflops / ref_gflops : 0.0;
   std::cout << r.backend << ": " << r.ms << " ms, " << r.gflops << " GFLOP/s, matched="
-            << r.matched << " (relative Frobenius " << r.frob << ")\n";
+            << r.matched << " (relative Frobenius " << r.frob << "), ratio to cuBLAS bf16 "
+            << ratio << "\n";
   std::cout << "backend_id=" << r.backend << std::setprecision(17) << " time_ms=" << r.ms
             << " work_unit=flop rate_per_second=" << r.gflops * 1e9
-            << " reference_rate_per_second=0 matched=" << r.matched << "\n";
+            << " reference_rate_per_second=" << ref_gflops * 1e9 << " matched=" << r.matched
+            << "\n";
   csv << std::setprecision(17) << r.backend << ',' << r.version << ','
-      << (o.square ? o.n : o.m) << ',' << r.precision << ",host block-scaled reference (sampled rows),"
-      << r.ms << ',' << r.gflops << ",0," << (r.matched ? 1 : 0) << ',' << r.gflops / 1e3 << ','
+      << (o.square ? o.n : o.m) << ',' << r.precision
+      << ",cuBLAS bf16 tensor-core GEMM (rate); host block-scaled oracle (check),"
+      << r.ms << ',' << r.gflops << ',' << ratio << ',' << (r.matched ? 1 : 0) << ','
+      << r.gflops / 1e3 << ','
       << 100.0 * r.gflops / 1e3 / peak_tflops << ",1," << o.m << ',' << o.n << ',' << o.k << '\n';
 }
 
 void usage(const char* p) {
   std::cerr << "Usage: " << p << " [N] [backend]\n"
             << "       " << p << " M N K backend [--gpus 1] [--dist normal] [--seed S] [--out-dtype bf16|fp32]\n"
+            << "       (any form) --no-reference skips the cuBLAS bf16 rate reference\n"
             << "       " << p << " --m=M --n=N --k=K [--iterations=I] [--swizzle=S]\n"
             << "backends: all|nvfp4_q1_native_fp4_mainloop|mxfp8_q0_tcgen05_block_scaled|"
                "nvfp4_skinny_q0|nvfp4_q0_tc6_fused_epilogue|mxfp4_q0_tcgen05_block_scaled\n"
@@ -560,6 +612,7 @@ bool parse(int argc, char** argv, Options* o) {
     else if (a.rfind("--swizzle=", 0) == 0) {}  // raster hint of the CUTLASS CLI; not used
     else if (a == "--seed" && i + 1 < argc) o->seed = std::strtoull(argv[++i], nullptr, 10);
     else if (a == "--out-dtype" && i + 1 < argc) o->out_bf16 = std::string(argv[++i]) == "bf16";
+    else if (a == "--no-reference") o->reference = false;
     else if (a == "--dist" && i + 1 < argc) {
       // Inputs are N(0, 1) (weights N(0, 0.02) where stated); no other law.
       if (std::string(argv[++i]) != "normal") return false;
@@ -628,6 +681,9 @@ int main(int argc, char** argv) {
   std::cout << "GPU: " << prop.name << " (sm_" << prop.major << prop.minor << ")\n"
             << "M=" << o.m << " N=" << o.n << " K=" << o.k << ", backend=" << o.backend << '\n'
             << "Benchmark policy: warmup=" << kWarmup << ", timed repeats=" << o.iterations << '\n';
+  const double ref_gflops = o.reference ? cublas_bf16_gflops(o) : 0.0;
+  if (o.reference)
+    std::cout << "reference: cuBLAS bf16 tensor-core GEMM " << ref_gflops << " GFLOP/s\n";
   std::ofstream csv("quant_sm110_benchmark.csv");
   csv << "BackendId,Version,N,Precision,Reference,TimeMs,GFLOPS,RatioToReference,Matched,"
          "TFLOPS,PctPeak,GPUs,M,NCols,K\n";
@@ -635,17 +691,17 @@ int main(int argc, char** argv) {
   auto want = [&](const char* b) { return o.backend == "all" || o.backend == b; };
   if (want("nvfp4_q1_native_fp4_mainloop")) {
     Row r = run_nvfp4(o);
-    write_row(csv, r, o);
+    write_row(csv, r, o, ref_gflops);
     all_ok &= r.matched;
   }
   if (want("mxfp8_q0_tcgen05_block_scaled")) {
     Row r = run_mxfp8(o);
-    write_row(csv, r, o);
+    write_row(csv, r, o, ref_gflops);
     all_ok &= r.matched;
   }
   if (want("mxfp4_q0_tcgen05_block_scaled")) {
     Row r = run_mxfp4(o);
-    write_row(csv, r, o);
+    write_row(csv, r, o, ref_gflops);
     all_ok &= r.matched;
   }
   if (want("nvfp4_q0_tc6_fused_epilogue")) {
@@ -654,13 +710,13 @@ int main(int argc, char** argv) {
       all_ok = false;
     } else {
       Row r = run_requant(o);
-      write_row(csv, r, o);
+      write_row(csv, r, o, ref_gflops);
       all_ok &= r.matched;
     }
   }
   if (want("nvfp4_skinny_q0")) {
     Row r = run_skinny(o);
-    write_row(csv, r, o);
+    write_row(csv, r, o, ref_gflops);
     all_ok &= r.matched;
   }
   return all_ok ? EXIT_SUCCESS : EXIT_FAILURE;

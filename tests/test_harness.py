@@ -41,6 +41,8 @@ def test_csv_rows_matched(binary, tmp_path, args):
         assert f.readline().strip().split(",")[:9] == HEADER
     assert rows and all(row["Matched"] == "1" for row in rows)
     assert all(float(row["GFLOPS"]) > 0 for row in rows)
+    # Rates relative to a cuBLAS bf16 GEMM timed in the same run.
+    assert all(float(row["RatioToReference"]) > 0 for row in rows)
     assert re.search(r"backend_id=\S+ time_ms=\S+ work_unit=flop rate_per_second=\S+ "
                      r"reference_rate_per_second=\S+ matched=1", r.stdout)
 
