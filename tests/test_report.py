@@ -56,3 +56,32 @@ def test_sweep_small(qlib, tmp_path):
     assert all(r["Status"] == "ok" and r["Matched"] == "1" for r in rows), rows
     with out.open() as f:
         assert f.readline().strip().split(",") == RUNNER_HEADER
+
+
+def test_sweep_rows_from_a_stand_in_harness(tmp_path):
+    """The sweep's row assembly on CPU: a stand-in harness writes the
+    harness CSV (or fails for one backend); rows carry the runner's header,
+    Status ok / failed, and the rate ratio to the given reference."""
+    fake = tmp_path / "fake_bench"
+    fake.write_text(
+        "#!/usr/bin/env python3\n"
+        "import sys\n"
+        "b = sys.argv[4]\n"
+        "if b.startswith('mxfp8'):\n"
+        "    sys.exit(3)\n"
+        "open('quant_sm110_benchmark.csv', 'w').write(\n"
+        "    'BackendId,Version,N,Precision,Reference,TimeMs,GFLOPS,RatioToReference,Matched\\n'\n"
+        "    f'{b},v,{sys.argv[1]},nvfp4->bf16,r,0.5,2000,0,1\\n')\n")
+    fake.chmod(0o755)
+    out = tmp_path / "sweep.csv"
+    rows = report.sweep(256, 2, out, binary=fake, reference_gflops=1000.0)
+    assert len(rows) == 2 * len(report.BACKENDS)
+    with out.open() as f:
+        got = list(csv.DictReader(f))
+    assert list(got[0].keys()) == RUNNER_HEADER
+    ok = [r for r in got if r["Status"] == "ok"]
+    bad = [r for r in got if r["Status"] != "ok"]
+    assert {r["BackendId"] for r in bad} == {"mxfp8_q0_tcgen05_block_scaled"}
+    assert all(r["Matched"] == "0" and r["Reason"] for r in bad)
+    assert all(float(r["RatioToReference"]) == 2.0 and r["Matched"] == "1" for r in ok)
+    assert {r["Trial"] for r in got} == {"0", "1"}
