@@ -37,7 +37,7 @@ ROOT = Path(__file__).resolve().parent
 WORKLOADS = {
     "nvfp4_8192": dict(fmt="nvfp4", m=8192, n=8192, k=8192, out="bf16", cfg=1),
     # the same GEMM with the output requantised to NVFP4 in the epilogue
-    # (the reference's tc6 fused epilogue; SURVEY next-step f1)
+    # (the reference's tc6 fused epilogue, GEMMsm110/include/backends/tc6_nvfp4.cuh:460-503)
     "nvfp4_8192_requant": dict(fmt="nvfp4", m=8192, n=8192, k=8192, out="nvfp4", cfg=1),
     # MXFP4 (e2m1, ue8m0 per 32 K; the reference's CUTLASS 72a rows) at 8192^3
     "mxfp4_8192": dict(fmt="mxfp4", m=8192, n=8192, k=8192, out="bf16", cfg=1),
