@@ -56,19 +56,23 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not needs_build():
         return OUT
     OBJ.mkdir(exist_ok=True)
-    objs = []
-    for src in sources():
+    from concurrent.futures import ThreadPoolExecutor
+
+    def compile_one(src: Path) -> str:
         obj = OBJ / (src.stem + ".o")
         cmd = [nvcc(), *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
         r = subprocess.run(cmd, capture_output=True, text=True)
-        log = OBJ / (src.stem + ".ptxas.txt")
-        log.write_text(r.stdout + r.stderr)
+        (OBJ / (src.stem + ".ptxas.txt")).write_text(r.stdout + r.stderr)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)
             raise RuntimeError(f"nvcc failed on {src.name}")
         if verbose:
             sys.stdout.write(r.stderr)
-        objs.append(str(obj))
+        return str(obj)
+
+    # One nvcc per translation unit, in parallel (each is single-threaded).
+    with ThreadPoolExecutor(max_workers=max(1, min(len(sources()), os.cpu_count() or 1))) as ex:
+        objs = list(ex.map(compile_one, sources()))
     tmp = OUT.with_suffix(".so.tmp")
     cmd = [nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", str(tmp),
            *objs, "-lcudart_static", "-lrt", "-lpthread", "-ldl"]

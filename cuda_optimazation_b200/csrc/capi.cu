@@ -111,46 +111,30 @@ uint64_t default_timeout_ns() {
   return t;
 }
 
-// QG_DIAG_FLAGS: diagnostic switches of the pair kernel (see GemmParams).
-uint32_t diag_flags() {
-  static const uint32_t f = [] {
-    const char* e = std::getenv("QG_DIAG_FLAGS");
-    return e ? static_cast<uint32_t>(std::strtoul(e, nullptr, 0)) : 0u;
-  }();
-  return f;
-}
-
 // GEMM kernel variant: 0 = single CTA with tcgen05.st scale staging,
 // 1 = CTA pair with tcgen05.st staging, 2 = single CTA with tcgen05.cp scale
-// copies.  Measured on B200 (8192^3 NVFP4 / 4096x14336x4096 MXFP8): NVFP4 is
-// fastest on the pair (4.0 PF/s vs 3.9 single, 3.1 with copies), MXFP8, with
-// only 3 scale copies per stage, on 2 (2.1 PF/s vs 2.0 pair).  Problems of
-// at most 128 rows use the single CTA (the pair's 256-row tile would be half
-// empty).  QG_GEMM_VARIANT=solo|pair|1cta overrides for A/B runs.
+// copies.  Measured on B200 (8192^3 NVFP4 / 4096x14336x4096 MXFP8): the pair
+// kernel wins whenever a 256-row tile is filled (NVFP4 8192^3 4.6 vs 3.9 PF/s
+// solo; MXFP8 2.34 vs 2.06 PF/s 1-CTA); problems of at most 128 rows use one
+// CTA per tile (the pair's 256-row tile would be half empty).  A build with
+// -DQG_GEMM_VARIANT=<0|1|2> forces one variant for A/B measurements; the
+// shipped library has no runtime switch.
 int gemm_variant(bool fp4, int64_t m) {
-  static const int forced = [] {
-    const char* e = std::getenv("QG_GEMM_VARIANT");
-    if (!e) return -1;
-    if (std::strcmp(e, "solo") == 0) return 0;
-    if (std::strcmp(e, "pair") == 0) return 1;
-    if (std::strcmp(e, "1cta") == 0) return 2;
-    return -1;
-  }();
-  if (forced >= 0) return forced;
-  // Measured on B200: the pair kernel wins whenever a 256-row tile is
-  // filled (NVFP4 8192^3 4.6 vs 3.9 PF/s solo; MXFP8 4096x14336x4096 2.34 vs
-  // 2.06 PF/s 1-CTA); small M stays on one CTA per tile.
+#ifdef QG_GEMM_VARIANT
+  return QG_GEMM_VARIANT;
+#endif
   if (m > 128) return 1;
   return fp4 ? 0 : 2;
 }
 
-bool pair_epi8() {
-  static const bool v = [] {
-    const char* e = std::getenv("QG_PAIR_EPI");
-    return !(e && std::strcmp(e, "4") == 0);
-  }();
-  return v;
-}
+// The bf16 TMA-store epilogue of the pair kernel runs on eight warps; a
+// build with -DQG_PAIR_EPI4 selects the older four-warp form (A/B runs).
+constexpr bool kPairEpi8 =
+#ifdef QG_PAIR_EPI4
+    false;
+#else
+    true;
+#endif
 
 // `gather` (fused column-parallel output gather): this GPU computes the
 // columns [col0, col0 + n) of a C with row stride ldc and stores them into
@@ -270,7 +254,6 @@ int gemm_prepare(int fmt, const void* a_q, const void* a_sf, const float* a_ts, 
   p.b_ts = fmt == 1 ? b_ts : nullptr;
   p.status = status;
   p.timeout_ns = default_timeout_ns();
-  p.diag = diag_flags();
   const int64_t tiles = static_cast<int64_t>(p.num_m_tiles) * p.num_n_tiles;
   out->fmt = fmt;
   out->fp4 = fp4;
@@ -280,9 +263,8 @@ int gemm_prepare(int fmt, const void* a_q, const void* a_sf, const float* a_ts, 
   if (pair) {
     const int64_t pairs = num_sms() / 2;
     out->grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
-    // bf16 through TMA stores: the eight-warp epilogue (kind 3), unless
-    // QG_PAIR_EPI=4 asks for the four-warp one (A/B measurements).
-    out->out_kind = rq ? 2 : (out->out_bf16 ? (p.n_out > 0 && pair_epi8() ? 3 : 1) : 0);
+    // bf16 through TMA stores: the eight-warp epilogue (kind 3).
+    out->out_kind = rq ? 2 : (out->out_bf16 ? (p.n_out > 0 && kPairEpi8 ? 3 : 1) : 0);
   } else {
     out->grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
   }
@@ -616,7 +598,6 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   p.num_k_blocks = static_cast<int>((row_bytes + 255) / 256);  // 512 of K per stage
   p.status = status;
   p.timeout_ns = default_timeout_ns();
-  p.diag = diag_flags();
   const int64_t units = static_cast<int64_t>(p.num_tiles) * p.num_k_blocks;
   int64_t grid = units < num_sms() ? units : num_sms();
   if (grid > skinny_max_ctas()) grid = skinny_max_ctas();

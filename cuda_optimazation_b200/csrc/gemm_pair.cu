@@ -231,7 +231,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
       int stage = 0, kb = 0, tile = pair;
       uint32_t phase = 0;
       int mt = tile % p.num_m_tiles, nt = tile / p.num_m_tiles;
-      const bool skip_loads = (p.diag & 4u) != 0;
+      const bool skip_loads = (kDiag & 4u) != 0;
       for (int g = 0; g < total_kb; ++g) {
         if (g > 0) {
           if (++stage == Cfg::kStages) {
@@ -303,7 +303,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
           kFp4 ? make_idesc_block_scaled(2 * Cfg::kBM, Cfg::kIssueN, 1u,
                                          kFmt == kFmtMxfp4 ? 1u : 0u, 0u, 0u)
                : make_idesc_block_scaled(2 * Cfg::kBM, Cfg::kIssueN, 0u, 1u, 0u, 0u);
-      const bool skip_mma = (p.diag & 2u) != 0;
+      const bool skip_mma = (kDiag & 2u) != 0;
       // B rows [h * kIssueN / 2, +kIssueN / 2) of each CTA's 128-row half.
       const uint64_t adesc0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
       const uint64_t bdesc0 =
@@ -380,7 +380,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
     const int quad = warp % 4;
     const int stager_kb = total_kb;
     const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
-    const bool no_wait = (p.diag & 32u) != 0, skip_st = (p.diag & 1u) != 0;
+    const bool no_wait = (kDiag & 32u) != 0, skip_st = (kDiag & 1u) != 0;
     int stage = 0;
     uint32_t phase = 0;
     for (int g = 0; g < stager_kb; ++g) {
@@ -448,7 +448,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
       mbar_try_wait(acc_full, it & 1);
       tc_fence_after();
       const int row = mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM + quad * 32 + lane;
-      const bool row_ok = row < p.m && !(p.diag & 8u);
+      const bool row_ok = row < p.m && !(kDiag & 8u);
       const int n0 = nt * Cfg::kBN;
       if constexpr (kOut == 2) {
         // NVFP4 output.  Each lane owns one output row, so a 16-column block
@@ -568,7 +568,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
             *reinterpret_cast<uint4*>(box + lane * 128 + ((c ^ (lane & 7)) * 16)) = v[c];
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0 && !(p.diag & 8u)) {
+          if (lane == 0 && !(kDiag & 8u)) {
             for (int d = 0; d < p.n_out; ++d)
               tma_store_2d(&p.tm_out[d], box, n0 + tmem_block(tb) * 64, row0);
             tma_store_commit();
@@ -612,50 +612,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0 && !(p.diag & 8u)) {
+          if (lane == 0 && !(kDiag & 8u)) {
             for (int d = 0; d < p.n_out; ++d)
               tma_store_2d(&p.tm_out[d], box, n0 + tmem_block(q) * 64, row0);
             tma_store_commit();
           }
         }
-      } else if (kOutBf16 && p.vec_ok && n0 + Cfg::kBN <= p.n) {
-        // Full tile: the whole accumulator row goes to registers as bf16,
-        // the accumulator is handed back, then 16-byte stores.
-        uint32_t packed[Cfg::kBN / 2];
-#pragma unroll
-        for (int cc = 0; cc < Cfg::kBN / 32; ++cc) {
-          // Two 16-column loads in flight per wait.
-          uint32_t r0[16], r1[16];
-          tmem_ld_32x32b_x16(t_row + cc * 32, r0);
-          tmem_ld_32x32b_x16(t_row + cc * 32 + 16, r1);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            packed[cc * 16 + j] = bf16x2_bits(__uint_as_float(r0[2 * j]) * alpha,
-                                              __uint_as_float(r0[2 * j + 1]) * alpha);
-            packed[cc * 16 + 8 + j] = bf16x2_bits(__uint_as_float(r1[2 * j]) * alpha,
-                                                  __uint_as_float(r1[2 * j + 1]) * alpha);
-          }
-          if ((Cfg::kIssuers == 2 && cc == Cfg::kBN / 64 - 1) || cc == Cfg::kBN / 32 - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0)
-              mbar_arrive_cluster_relaxed(cc == Cfg::kBN / 32 - 1 ? acc_empty_leader1
-                                                                  : acc_empty_leader0);
-          }
-        }
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.c) +
-                                                row * p.ldc + n0);
-#pragma unroll
-          for (int v = 0; v < Cfg::kBN / 8; ++v) {
-            const int pv = 4 * (tmem_block(v / 8) * 8 + v % 8);
-            dst[v] = make_uint4(packed[pv], packed[pv + 1], packed[pv + 2], packed[pv + 3]);
-          }
-        }
       } else {
-        // fp32 output or a ragged tile: 32 columns at a time, accumulator
-        // handed back after the last TMEM read.
+        // fp32 output, or bf16 C that TMA cannot store (unaligned rows):
+        // 32 columns at a time, accumulator handed back after the last TMEM
+        // read.
 #pragma unroll 1
         for (int cc = 0; cc < Cfg::kBN / 32; ++cc) {
           uint32_t r[32];

@@ -165,14 +165,14 @@ struct SegCursor {
   }
 };
 
-// Diagnostic stamp (QG_DIAG_FLAGS bit 6): CTA (diag >> 16) writes %globaltimer into
+// Diagnostic stamp (kDiag bit 6): CTA (kDiag >> 16) writes %globaltimer into
 // slot `i` of the last (never used by a launched CTA) partial slice pair.
 __device__ __forceinline__ void trace_cta(const SkinnyParams& p, int i) {
-  if (p.diag & 64u)
+  if (kDiag & 64u)
     reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * 2 * p.m * 128)[i] = globaltimer_ns();
 }
 __device__ __forceinline__ void trace(const SkinnyParams& p, int i) {
-  if ((p.diag & 64u) && blockIdx.x == (p.diag >> 16) && i < 512)
+  if ((kDiag & 64u) && blockIdx.x == (kDiag >> 16) && i < 512)
     reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * 2 * p.m * 128)[i] = globaltimer_ns();
 }
 
@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       // is a wait, eight MMAs and a commit, with descriptors and scale
       // columns stepped by constants.
       const uint32_t idesc = make_idesc_block_scaled(Cfg::kBM, kN, 1u, 0u, 0u, 0u);
-      const bool skip_mma = (p.diag & 2u) != 0;
+      const bool skip_mma = (kDiag & 2u) != 0;
       const uint64_t wdesc0 = make_smem_desc(smem_u32(smem), 16, 1024, kSwizzle128B);
       const uint64_t xdesc0 = make_smem_desc(smem_u32(smem + Cfg::kWBytes), 16, 1024, kSwizzle128B);
       constexpr uint64_t kStageDesc = Cfg::kStageBytes >> 4;
@@ -570,7 +570,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
         b[4 * c] = w.x; b[4 * c + 1] = w.y; b[4 * c + 2] = w.z; b[4 * c + 3] = w.w;
       }
       const uint32_t col = Cfg::kTmemSfBase + stage * Cfg::kSfStageCols;
-      if (!(p.diag & 1u)) {
+      if (!(kDiag & 1u)) {
         tmem_st_32x32b<4 * Cfg::kSfChunks>(t_quad + col, a);
         tmem_st_32x32b<4 * Cfg::kSfChunks>(t_quad + col + 4 * Cfg::kSfChunks, b);
         tmem_wait_st();
@@ -639,7 +639,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       // the unrolled epilogue competes for instruction cache with four other
       // roles, and a fetch miss under the weight stream costs microseconds.
       const bool whole = cf == cl;
-      const bool st_ok = !(p.diag & 8u) && (!whole || n_ok);
+      const bool st_ok = !(kDiag & 8u) && (!whole || n_ok);
       const float scale = whole ? alpha : 1.0f;
       const bool bf16_dst = whole && p.out_bf16;
       const int64_t stride = whole ? p.ldc : Cfg::kBM;

@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(320, 1)
         uint8_t* sb = sa + Cfg::kABytes;
         uint8_t* ssfa = sb + Cfg::kBBytes;
         uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
-        if (p.diag & 4u) {
+        if (kDiag & 4u) {
           mbar_arrive(&full_bar[stage]);
           continue;
         }
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t sfb_col = sfa_col + Cfg::kSfaCols;
           const uint64_t adesc = make_smem_desc(smem_u32(sa), 16, 1024, kSwizzle128B);
           const uint64_t bdesc = make_smem_desc(smem_u32(sb), 16, 1024, kSwizzle128B);
-          if (!(p.diag & 2u)) {
+          if (!(kDiag & 2u)) {
 #pragma unroll
             for (int j = 0; j < Cfg::kMmaPerStage; ++j) {
               const uint64_t koff = static_cast<uint64_t>(j * 2);  // +32 B of K
@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(320, 1)
       const uint8_t* ssfa = smem + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
       const uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
       const uint32_t sfa_col = Cfg::kTmemSfBase + stage * Cfg::kTmemSfStageCols;
-      if (!(p.diag & 1u)) {
+      if (!(kDiag & 1u)) {
         stage_scales_solo<kFp4>(ssfa, ssfb, t_quad, sfa_col, sfa_col + Cfg::kSfaCols, lane);
         tmem_wait_st();
       }
@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_try_wait(acc_full, it & 1);
       tc_fence_after();
       const int row = mt * Cfg::kBM + quad * 32 + lane;
-      const bool row_ok = row < p.m && !(p.diag & 8u);
+      const bool row_ok = row < p.m && !(kDiag & 8u);
       const int n0 = nt * Cfg::kBN;
       if (kOutBf16 && p.vec_ok && n0 + Cfg::kBN <= p.n) {
         // Full tile: the whole accumulator row goes to registers as bf16,

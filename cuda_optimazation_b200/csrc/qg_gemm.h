@@ -10,6 +10,18 @@ namespace qg {
 // Devices a process may drive (per-device launch state is kept in arrays).
 constexpr int kMaxDevices = 64;
 
+// Diagnostic switches, fixed when the library is compiled (-DQG_DIAG_FLAGS=...
+// through QG_EXTRA_NVCC); shipped builds have none and the branches vanish.
+// Results are wrong by design when bits 0-3 are set: bit 0 skips the scale
+// staging, bit 1 the MMAs, bit 2 the TMA loads (pair / solo kernels), bit 3
+// the epilogue stores; bit 6 makes the decode GEMM's CTA (kDiag >> 16) write
+// %globaltimer stamps of its roles into an unused partial slice.  Used to
+// attribute kernel time to its parts.
+#ifndef QG_DIAG_FLAGS
+#define QG_DIAG_FLAGS 0u
+#endif
+constexpr uint32_t kDiag = QG_DIAG_FLAGS;
+
 struct GemmParams {
   CUtensorMap tm_a;    // uint8 [rows][K bytes], box 128 B x kBM, SWIZZLE_128B
   CUtensorMap tm_b;    // uint8 [rows][K bytes], box 128 B x kBN, SWIZZLE_128B
@@ -41,10 +53,6 @@ struct GemmParams {
   int rq_row_blocks, rq_sf_blocks;
   uint32_t* status;
   uint64_t timeout_ns;
-  // Diagnostics only (QG_DIAG_FLAGS; results are wrong when set): bit 0
-  // skips scale staging, bit 1 the MMAs, bit 2 the TMA loads, bit 3 the
-  // epilogue stores.  Used to attribute kernel time to its parts.
-  uint32_t diag;
 };
 
 // Decode-shaped NVFP4 GEMM (gemm_skinny.cu): weights W [n][k] on the MMA's M
@@ -77,11 +85,6 @@ struct SkinnyParams {
   int num_tiles, num_k_blocks;
   uint32_t* status;
   uint64_t timeout_ns;
-  // Diagnostics (QG_DIAG_FLAGS; results are wrong when bits 0-1 are set):
-  // bit 0 skips the scale staging (stagers still wait and arrive), bit 1 the
-  // MMAs (the issuer still waits and commits); bit 6 writes %globaltimer
-  // stamps of CTA (diag >> 16)'s roles into an unused partial slice.
-  uint32_t diag;
 };
 cudaError_t launch_gemm_skinny(const SkinnyParams& p, int grid, cudaStream_t stream);
 int skinny_max_ctas();
