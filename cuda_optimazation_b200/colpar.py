@@ -143,7 +143,15 @@ def colpar_gemm_fused(a, b_local, n_total: int, bufs: "GatherBuffers", group=Non
     """Column-parallel GEMM with the all-gather fused into the epilogue:
     this rank's columns go straight into every rank's ``bufs.c``.  Returns
     this rank's full C once every rank's kernel has finished (device
-    synchronise + barrier)."""
+    synchronise + barrier).
+
+    ``bufs.c`` is shared with the peers, whose kernels write into it, so the
+    returned tensor stays valid only until this rank calls again.  The call
+    therefore starts with a device synchronise (this rank's readers of the
+    previous result, on any stream, are done) and a barrier (so are every
+    other rank's) before any kernel writes the next result."""
+    torch.cuda.synchronize()
+    dist.barrier(group=group)
     lo, _ = shard_range(n_total, dist.get_world_size(group), dist.get_rank(group))
     bufs.q.gemm_nvfp4_gather(a, b_local, bufs.ptrs, lo, n_total, status=status)
     torch.cuda.synchronize()

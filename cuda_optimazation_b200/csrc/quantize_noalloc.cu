@@ -102,10 +102,22 @@ __global__ void __launch_bounds__(1024) amax_finalize_kernel(uint32_t* scratch, 
 // Device address of the scratch array, looked up on the first call on each
 // device with that device current; in host code the symbol is only a
 // stand-in, never a device address.  Because the first call does this
-// set-up, make it before any stream capture.
+// set-up, make it before any stream capture.  A device reset reloads the
+// module and moves the array, so a call whose launches fail forgets the
+// cached address and the next call looks it up again.
+std::mutex g_scratch_mu;
+uint32_t* g_scratch_addr[64] = {nullptr};
+
+void forget_scratch_address() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  g_scratch_addr[dev] = nullptr;
+}
+
 uint32_t* scratch_address(int* err) {
-  static std::mutex mu;
-  static uint32_t* addr[64] = {nullptr};
+  auto& mu = g_scratch_mu;
+  auto& addr = g_scratch_addr;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     *err = QG_ERR_CUDA;
@@ -159,14 +171,20 @@ int qg_quantize_nvfp4_noalloc(const void* x, int x_dtype, int64_t rows, int64_t 
     if (cudaMemsetAsync(sf, 0, static_cast<size_t>(qg_scale_bytes(rows, k, 16)), s) != cudaSuccess)
       return QG_ERR_CUDA;
   }
+  // An error left pending by an earlier, unrelated call would be read back
+  // below as this call's launch failure: report it without launching (and
+  // without clearing it, so its owner still sees it).
+  if (cudaPeekAtLastError() != cudaSuccess) return QG_ERR_CUDA;
   const int nparts = static_cast<int>((n + kChunk - 1) / kChunk);
   if (bf16) amax_partial_kernel<true><<<nparts, 256, 0, s>>>(x, n, scratch);
   else amax_partial_kernel<false><<<nparts, 256, 0, s>>>(x, n, scratch);
   amax_finalize_kernel<<<1, 1024, 0, s>>>(scratch, nparts);
-  if (cudaGetLastError() != cudaSuccess) return QG_ERR_CUDA;
-  if (launch_quantize_nvfp4(x, bf16, rows, k, layout, static_cast<uint8_t*>(q),
-                            static_cast<uint8_t*>(sf), ts, scratch + kFinalSlot, s) != cudaSuccess)
+  if (cudaGetLastError() != cudaSuccess ||
+      launch_quantize_nvfp4(x, bf16, rows, k, layout, static_cast<uint8_t*>(q),
+                            static_cast<uint8_t*>(sf), ts, scratch + kFinalSlot, s) != cudaSuccess) {
+    forget_scratch_address();
     return QG_ERR_CUDA;
+  }
   return QG_OK;
 }
 

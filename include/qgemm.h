@@ -106,9 +106,14 @@ int qg_quantize_nvfp4(const void* x, int x_dtype, int64_t rows, int64_t k, int l
  * exit), which bounds the input to qg_quantize_nvfp4_noalloc_max_elements()
  * = 2^28 elements; larger inputs return QG_ERR_SHAPE.  The array's device
  * address is looked up on the first call on each device, so make that first
- * call before any stream capture.  All calls share the array: calls that may
- * overlap on the GPU race and must be ordered by the caller.  Allocates
- * nothing (no cudaMalloc / cudaFree, no allocating library routine). */
+ * call before any stream capture.  A device reset (cudaDeviceReset) moves
+ * the array: the first call after it fails with QG_ERR_CUDA and forgets the
+ * cached address, and the next call looks it up again.  An error already
+ * pending in the CUDA runtime before the call is reported as QG_ERR_CUDA
+ * without launching and is left pending.  All calls share the array: calls
+ * that may overlap on the GPU race and must be ordered by the caller.
+ * Allocates nothing (no cudaMalloc / cudaFree, no allocating library
+ * routine). */
 int qg_quantize_nvfp4_noalloc(const void* x, int x_dtype, int64_t rows, int64_t k, int layout,
                               void* q, void* sf, float* ts, qg_stream_t stream);
 
@@ -270,8 +275,12 @@ size_t qg_gemm_nvfp4_skinny_workspace_bytes(int64_t m, int64_t n, int64_t k);
  * C[:, col0 : col0 + n_local] = (a_ts*b_ts) * A . B_local^T (B_local: the
  * n_local rows of B this rank owns, NVFP4, MMA layout) and writes those
  * columns into every c_ranks[r].  col0 % 8 == 0, ldc % 8 == 0, buffers
- * 16-byte aligned.  Stream-ordered on this GPU only: the caller orders the
- * ranks (e.g. synchronise + a host barrier) before reading the gathered C. */
+ * 16-byte aligned.  Stream-ordered on this GPU only, and every rank's call
+ * writes into every rank's C, so the caller orders the ranks on both sides:
+ * after the calls (synchronise + a host barrier) before reading the
+ * gathered C, and before the next calls (every rank done reading its C,
+ * on any stream: synchronise + a host barrier), or a fast peer overwrites a
+ * result still being read.  colpar.colpar_gemm_fused does both. */
 #define QG_MAX_RANKS 8
 int qg_gemm_nvfp4_gather(const void* a_q, const void* a_sf, const float* a_ts, const void* b_q,
                          const void* b_sf, const float* b_ts, void* const* c_ranks, int nranks,

@@ -165,6 +165,46 @@ class Oracle:
                                 v, s)
         return v, s
 
+    # -- selected rows of a large operand (sampled-row parity checks)
+    @staticmethod
+    def scale_rows(sf, rows_idx, nrows: int, k: int, sv: int, order: int = 0) -> np.ndarray:
+        """Scale bytes [len(rows_idx), k/sv] of the given rows of an MMA-layout
+        scale buffer (L1, scale_layout.hpp:11-26, in chunk order `order`)."""
+        r = np.asarray(rows_idx, np.int64)[:, None]
+        s = np.arange(k // sv, dtype=np.int64)[None, :]
+        row_blocks, sf_blocks = (nrows + 127) // 128, (k // sv + 3) // 4
+        chunk = (s // 4) * row_blocks + r // 128 if order == 0 else (r // 128) * sf_blocks + s // 4
+        w = r % 128
+        off = chunk * 512 + (w % 32) * 16 + (w // 32) * 4 + s % 4
+        return np.asarray(sf, np.uint8)[off]
+
+    def _luts(self):
+        if not hasattr(self, "_lut"):
+            self._lut = (np.array([self.L.qgo_decode_e2m1(i) for i in range(16)], np.float32),
+                         np.array([self.L.qgo_decode_e4m3_positive(i) for i in range(256)], np.float32),
+                         np.array([self.L.qgo_decode_e4m3(i) for i in range(256)], np.float32),
+                         np.array([self.L.qgo_decode_ue8m0(i) for i in range(256)], np.float32))
+        return self._lut
+
+    def nvfp4_rows(self, q, sf, rows_idx, nrows: int, k: int, order: int = 0):
+        """Logical (values [R*k], scales [R*k/16]) of the given rows of an
+        MMA-layout NVFP4 operand (low nibble first), decoded with the same
+        e2m1 / e4m3 tables as qgo_nvfp4_decode_mma."""
+        e2m1, e4m3p, _, _ = self._luts()
+        qb = np.asarray(q, np.uint8).reshape(nrows, k // 2)[np.asarray(rows_idx)]
+        codes = np.stack([qb & 0xF, qb >> 4], axis=2).reshape(len(rows_idx), k)
+        vals = e2m1[codes]
+        scales = e4m3p[self.scale_rows(sf, rows_idx, nrows, k, 16, order)]
+        return np.ascontiguousarray(vals.ravel()), np.ascontiguousarray(scales.ravel())
+
+    def mxfp8_rows(self, q, sf, rows_idx, nrows: int, k: int, order: int = 0):
+        """Logical (values, scales) of the given rows of an MMA-layout MXFP8
+        operand (e4m3 bytes, ue8m0 per 32)."""
+        _, _, e4m3, ue8m0 = self._luts()
+        qb = np.asarray(q, np.uint8).reshape(nrows, k)[np.asarray(rows_idx)]
+        scales = ue8m0[self.scale_rows(sf, rows_idx, nrows, k, 32, order)]
+        return np.ascontiguousarray(e4m3[qb].ravel()), np.ascontiguousarray(scales.ravel())
+
     # -- O2
     def gemm(self, a, b, sfa, sfb, m, n, k, sv, rows=None, threads=8) -> np.ndarray:
         r0, r1 = (0, m) if rows is None else rows

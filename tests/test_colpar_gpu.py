@@ -67,3 +67,56 @@ def test_fused_gather_two_gpus_matches_single_gpu(tmp_path, m, n, k):
     for r in range(world):
         res = torch.load(tmp_path / f"r{r}.pt")
         assert res["ok"], res
+
+
+def _worker_steps(rank, world, port, m, n, k, result_dir):
+    """Three steps with different A; rank 1 reads each result late (after a
+    half-second sleep).  The entry barrier of colpar_gemm_fused
+    keeps rank 0's next step from overwriting rank 1's buffer before it has
+    read the current one."""
+    import time
+    sys.path.insert(0, str(ROOT))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=120))
+    from cuda_optimazation_b200 import colpar
+    from cuda_optimazation_b200 import qgemm as q
+    dev = torch.device("cuda", rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(22)
+    b = q.make_nvfp4(torch.randn(n, k, generator=gen, device=dev), layout=q.LAYOUT_MMA_KMAJOR)
+    lo, hi = colpar.shard_range(n, world, rank)
+    b_local = colpar.shard_rows(b, lo, hi)
+    bufs = colpar.GatherBuffers(m, n, dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ok, bad = True, []
+    for step in range(3):
+        gen.manual_seed(100 + step)
+        a = q.make_nvfp4(torch.randn(m, k, generator=gen, device=dev), layout=q.LAYOUT_MMA_KMAJOR)
+        ref = q.block_scaled_gemm(a, b, out_dtype=torch.bfloat16)
+        full = colpar.colpar_gemm_fused(a, b_local, n, bufs, status=status)
+        if rank == 1:
+            time.sleep(0.5)
+        got = full.clone()
+        torch.cuda.synchronize()
+        if not torch.equal(got, ref):
+            ok, bad = False, bad + [step]
+    rc, code = q.read_status(status)
+    torch.save({"ok": ok and rc == q.OK, "bad_steps": bad, "code": code},
+               os.path.join(result_dir, f"s{rank}.pt"))
+    dist.barrier()
+    bufs.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_gather_consecutive_steps_with_slow_reader(tmp_path):
+    world = 2
+    mp.spawn(_worker_steps, args=(world, 29811, 1024, 2048, 1024, str(tmp_path)), nprocs=world,
+             join=True)
+    for r in range(world):
+        res = torch.load(tmp_path / f"s{r}.pt")
+        assert res["ok"], res

@@ -99,6 +99,26 @@ def test_mxfp8(qlib, oracle, m, n, k, out):
     check_gemm(c.float().cpu().numpy(), ref, bf16=(out == torch.bfloat16))
 
 
+@pytest.mark.parametrize("m,out", [(1, torch.float32), (64, torch.float32), (100, torch.bfloat16),
+                                   (128, torch.float32)])
+def test_mxfp8_small_m(qlib, oracle, m, out):
+    """MXFP8 with m <= 128 runs the single-CTA kernel (gemm_blockscaled.cu,
+    tcgen05.cp scale copies) by default; ragged n, several K blocks."""
+    n, k = 1000, 1024
+    a, b, order = mxfp8_case(oracle, m, n, k)
+    dev = torch.device("cuda")
+    t = lambda arr: torch.from_numpy(arr).to(dev)
+    c = torch.full((m, n), float("nan"), dtype=out, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    qlib.gemm_mxfp8_raw(t(a[0]), t(a[1]), t(b[0]), t(b[1]), c, m, n, k, 1, status)
+    rc, code = qlib.read_status(status)
+    assert rc == qlib.OK, code
+    av, asf = oracle.mxfp8_decode(a[0], a[1], m, k, order)
+    bv, bsf = oracle.mxfp8_decode(b[0], b[1], n, k, order)
+    ref = oracle.gemm(av, bv, asf, bsf, m, n, k, 32)
+    check_gemm(c.float().cpu().numpy(), ref, bf16=(out == torch.bfloat16))
+
+
 def test_end_to_end_device_quantize(qlib, oracle):
     """Quantise on the device, GEMM on the device, compare with the oracle's
     quantise + O2 on the same fp32 inputs."""

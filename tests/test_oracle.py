@@ -215,3 +215,21 @@ def test_mxfp4_oracle_known_answers(oracle):
     qm, sm = oracle.mxfp4(x, 0)
     assert qm[0] == (codes[1] << 4) | codes[0]
     assert sm[0] == 125
+
+
+@pytest.mark.parametrize("rows,k,order", [(300, 512, 0), (300, 512, 1), (128, 64, 0), (1000, 2048, 1)])
+def test_row_selected_decode_matches_full_decode(oracle, rows, k, order):
+    """The sampled-row views used by the at-scale GPU parity tests
+    (scale_rows / nvfp4_rows / mxfp8_rows) equal the full decoders' rows."""
+    x = oracle.normal(rows * k, 3).reshape(rows, k)
+    idx = sorted({0, 5, 131 % rows, 299 % rows, rows - 1})
+    q, sf, _ = oracle.nvfp4_mma(x, order)
+    v, s = oracle.nvfp4_decode(q, sf, rows, k, order)
+    v2, s2 = oracle.nvfp4_rows(q, sf, idx, rows, k, order)
+    assert np.array_equal(v.reshape(rows, k)[idx].ravel(), v2)
+    assert np.array_equal(s.reshape(rows, -1)[idx].ravel(), s2)
+    q8, sf8 = oracle.mxfp8(x, order)
+    v8, s8 = oracle.mxfp8_decode(q8, sf8, rows, k, order)
+    v9, s9 = oracle.mxfp8_rows(q8, sf8, idx, rows, k, order)
+    assert np.array_equal(v8.reshape(rows, k)[idx].ravel(), v9)
+    assert np.array_equal(s8.reshape(rows, -1)[idx].ravel(), s9)

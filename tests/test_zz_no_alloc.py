@@ -66,3 +66,34 @@ def test_noalloc_rejects_inputs_over_capacity(qlib):
                                      dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(),
                                      torch.cuda.current_stream().cuda_stream)
     assert rc == qlib.ERR_SHAPE
+
+
+@pytest.mark.parametrize("rows,k,layout", [
+    (3, 1001, 0),            # REF_LINEAR, rows*k not a multiple of 16 (zero-padded last block)
+    (7, 16384 * 5 + 48, 0),  # the last amax slot covers a partial 16384-element chunk
+    (130, 1040, 1),          # MMA layout with padded scale rows and columns
+])
+def test_noalloc_ragged_sizes(qlib, rows, k, layout):
+    L = qlib.lib()
+    g = torch.Generator(device="cuda").manual_seed(rows * 7 + k)
+    x = torch.randn(rows, k, generator=g, device="cuda")
+    (qa, sa, ta), (qb, sb, tb) = _quantize_both(L, x, layout)
+    assert ta == tb
+    assert np.array_equal(qa, qb) and np.array_equal(sa, sb)
+
+
+@pytest.mark.parametrize("specials", [("inf",), ("-inf",), ("nan",), ("nan", "inf", "-inf")])
+def test_noalloc_special_values(qlib, specials):
+    """+-inf and NaN inputs: both entry points reduce the amax the same way
+    (NaN ignored, as std::max in the reference quantizer does) and write the
+    same bytes."""
+    L = qlib.lib()
+    g = torch.Generator(device="cuda").manual_seed(11)
+    for dtype in (torch.float32, torch.bfloat16):
+        x = torch.randn(64, 512, generator=g, device="cuda")
+        for i, sv in enumerate(specials):
+            x.view(-1)[1000 * i + 37] = float(sv)
+        x = x.to(dtype)
+        (qa, sa, ta), (qb, sb, tb) = _quantize_both(L, x, 0)
+        assert ta == tb or (np.isnan(ta) and np.isnan(tb))
+        assert np.array_equal(qa, qb) and np.array_equal(sa, sb)
