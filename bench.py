@@ -2,28 +2,35 @@
 """Benchmark of the B200 block-scaled quantized GEMM (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload auto|nvfp4_8192|nvfp4_256|mxfp8_ffn|colpar]
+                    [--workload auto|colpar|nvfp4_8192|...] [--no-subrecords]
 
-Workloads:
-  nvfp4_8192  NVFP4 M=N=K=8192, bf16 out (configs[1]; the N=1 default)
-  colpar      column-parallel NVFP4 M=16384, N=53248, K=8192: B sharded along
-              N over the ranks, A broadcast once, bf16 output shards; the
-              optional NCCL all-gather is timed separately (the N>1 default)
-  mxfp8_ffn   MXFP8 4096 x 14336 x 4096, bf16 out
-  nvfp4_256   NVFP4 256^3 fp32 out
+Headline workload (every N): the column-parallel NVFP4
+GEMM M=16384, N=53248, K=8192.  B is quantised once and sharded along N over
+the ranks (colpar.shard_rows of one K-major operand), A is quantised once and
+broadcast, every rank runs its local GEMM with no communication; at N = 1 the
+one rank owns all of B.  The output gather (NCCL, and fused into the GEMM
+epilogue over peer memory) is timed separately at N > 1.
+
+At N = 1 the line also carries `subrecords` for the other BASELINE configs,
+each with its own steps, ms, roofline and clocks: NVFP4 8192^3,
+the same GEMM with NVFP4 output (the tc6 row), MXFP4 8192^3, MXFP8
+4096x14336x4096 and the decode GEMM at m = 16, 64, 128
+(configs[3]).
 
 A "step" is one GEMM launch over one problem whose quantised operands are
 already resident in HBM.  `value` is whole-job TFLOP/s (all ranks' FLOPs over
 the max-over-ranks device time of exactly K steps).  `e2e` is the same metric
-through the public API with pinned HOST operands: per step the quantised
-operands are copied host->device, the GEMM runs, and the bf16 result is
-copied back.  The reference arm (--impl reference) times the reference's own
-CPU path (oracle/_ref, else this repo's CPU restatement) on bounded samples.
+through the public API starting from fp32 HOST data, as the reference's CPU
+path does: per step A and B are copied host->device, quantised to NVFP4 on the
+device, multiplied, and the bf16 result is copied back.  The reference arm
+(--impl reference) times the reference's own CPU path (oracle/_ref, else this
+repo's CPU restatement) on the same bounded sample blocks as `cpu_baseline`.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -35,6 +42,7 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 
 WORKLOADS = {
+    "colpar": dict(fmt="nvfp4", m=16384, n=53248, k=8192, out="bf16", cfg=4),
     "nvfp4_8192": dict(fmt="nvfp4", m=8192, n=8192, k=8192, out="bf16", cfg=1),
     # the same GEMM with the output requantised to NVFP4 in the epilogue
     # (the reference's tc6 fused epilogue, GEMMsm110/include/backends/tc6_nvfp4.cuh:460-503)
@@ -43,14 +51,19 @@ WORKLOADS = {
     "mxfp4_8192": dict(fmt="mxfp4", m=8192, n=8192, k=8192, out="bf16", cfg=1),
     "nvfp4_256": dict(fmt="nvfp4", m=256, n=256, k=256, out="fp32", cfg=0),
     "mxfp8_ffn": dict(fmt="mxfp8", m=4096, n=14336, k=4096, out="bf16", cfg=2),
-    "colpar": dict(fmt="nvfp4", m=16384, n=53248, k=8192, out="bf16", cfg=4),
     # decode GEMM with fused activation quantisation; HBM bound
     "skinny_m16": dict(fmt="nvfp4", m=16, n=28672, k=8192, out="bf16", cfg=3, skinny=True),
     "skinny_m64": dict(fmt="nvfp4", m=64, n=28672, k=8192, out="bf16", cfg=3, skinny=True),
     "skinny_m128": dict(fmt="nvfp4", m=128, n=28672, k=8192, out="bf16", cfg=3, skinny=True),
 }
+SUBRECORDS = ["nvfp4_8192", "nvfp4_8192_requant", "mxfp4_8192", "mxfp8_ffn",
+              "skinny_m16", "skinny_m64", "skinny_m128"]
 METRIC = "NVFP4/FP8 GEMM TFLOPS and % of B200 tensor peak (HBM GB/s for skinny M), 1/2/4/8 GPU"
 SEED = 20260817
+L2_BYTES = 126e6
+# Timed regions of the sub-records last at least this long, so the clock
+# sampler sees the GPU under load.
+SUB_MIN_TIMED_S = 0.25
 
 
 def peaks() -> dict:
@@ -65,7 +78,8 @@ def peaks() -> dict:
 
 
 def profile_traffic(kernel_tag: str):
-    """Per-launch DRAM bytes of `kernel_tag` from the committed ncu summary."""
+    """Per-launch DRAM bytes of `kernel_tag` from the committed ncu summary
+    (profiles/traffic_per_launch.txt: tag, bytes, how they were captured)."""
     f = ROOT / "profiles" / "traffic_per_launch.txt"
     if not f.exists():
         return None
@@ -87,6 +101,7 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
+        import torch
         self.index = index
         self.proc = None
         self.lines: list[str] = []
@@ -183,58 +198,137 @@ class ClockSampler:
                 "samples": len(loaded), "power_w_max": pmax}
 
 
-# --------------------------------------------------------------------- ours
-def make_operands(q, torch, w, m_rows, n_rows, dev, gen, b_std=1.0):
-    """Seeded synthetic fp32 inputs quantised on the device (untimed)."""
-    k = w["k"]
-    a = torch.randn(m_rows, k, generator=gen, device=dev, dtype=torch.float32)
-    b = torch.randn(n_rows, k, generator=gen, device=dev, dtype=torch.float32) * b_std
-    if w["fmt"] == "nvfp4":
-        A, B = q.make_nvfp4(a), q.make_nvfp4(b)
-    elif w["fmt"] == "mxfp4":
-        A, B = q.make_mxfp4(a), q.make_mxfp4(b)
+# --------------------------------------------------------------------- config
+def sample_rows(m: int, count: int) -> list:
+    """The reference's sample rows s*131 % m (GEMMsm110/include/gemm_benchmark.cuh:51-53)."""
+    return sorted({(s * 131) % m for s in range(count)} | {m - 1})
+
+
+def sample_cols(n: int, count: int) -> list:
+    """The reference's sample columns s*197 % n (gemm_benchmark.cuh:51-53)."""
+    return sorted({(s * 197) % n for s in range(count)} | {n - 1})
+
+
+def workload_config(name: str, w: dict, world: int, rank: int) -> dict:
+    """The `config` object of the JSON line, identical in both arms."""
+    from_colpar = name == "colpar"
+    m, n_total, k = w["m"], w["n"], w["k"]
+    if from_colpar:
+        lo, hi = shard_range(n_total, world, rank)
+        n_local = hi - lo
     else:
-        A, B = q.make_mxfp8(a), q.make_mxfp8(b)
-    del a, b
-    return A, B
+        n_local = n_total
+    if w.get("skinny"):
+        return {"workload": f"nvfp4_skinny_gemm_m{m}_n{n_total}_k{k}_fused_act_quant",
+                "baseline_config_index": 3, "m": m, "n": n_total, "k": k, "out": "bf16",
+                "parallelism": f"replica{world}" if world > 1 else "single",
+                "l2": "2 alternating 132 MB weight sets vs 126 MB L2",
+                "launch": "each step replays a CUDA graph of one qg_gemm_nvfp4_skinny call"}
+    elem = 1.0 if w["fmt"] == "mxfp8" else 0.5
+    set_bytes = (m + n_local) * k * elem
+    out_bytes = m * n_local * {"bf16": 2, "fp32": 4, "nvfp4": 0.5625}[w["out"]]
+    nsets = 1 if set_bytes + out_bytes > 3 * L2_BYTES else 3
+    return {
+        "workload": f"{w['fmt']}_gemm_{m}x{n_total}x{k}_{w['out']}out",
+        "baseline_config_index": w["cfg"], "m": m, "n": n_total, "k": k,
+        "n_per_rank": n_local, "out": w["out"],
+        "parallelism": (f"colpar{world} (B sharded along N, A broadcast)" if from_colpar
+                        else (f"replica{world}" if world > 1 else "single")),
+        "l2": (f"{nsets} rotating operand set(s) ({set_bytes / 1e6:.0f} MB each) + "
+               f"{out_bytes / 1e6:.0f} MB output per step vs 126 MB L2"),
+        "operand_sets": nsets,
+    }
 
 
-def run_ours(args, w, rank, world, dist, torch):
+def shard_range(n: int, world: int, rank: int, align: int = 256):
+    """Same split as colpar.shard_range (importable without torch)."""
+    blocks = (n + align - 1) // align
+    per, extra = blocks // world, blocks % world
+    b0 = rank * per + min(rank, extra)
+    b1 = b0 + per + (1 if rank < extra else 0)
+    return min(n, b0 * align), min(n, b1 * align)
+
+
+def timed(torch, stream, fn, steps, dist=None):
+    """Device time (ms) of exactly `steps` calls of fn(i), events on the
+    launching stream at the two ends only (a record between steps costs
+    ~2.6 us of device time), barrier + synchronise on both sides; max over
+    ranks."""
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record(stream)
+    for i in range(steps):
+        fn(i)
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t = torch.tensor([ev[0].elapsed_time(ev[1])], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------- ours
+def run_gemm(args, name, w, rank, world, dist, torch, steps, headline=True):
+    """One GEMM workload: operands quantised on the device (untimed), the
+    timed region, and for the headline the e2e leg, the gather legs (N > 1)
+    and the sample the CPU checker compares against."""
+    from cuda_optimazation_b200 import colpar as cp
     from cuda_optimazation_b200 import qgemm as q
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
-    torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream()
-    m, k = w["m"], w["k"]
-    n_total = w["n"]
-    colpar = args.workload_name == "colpar"
-    from cuda_optimazation_b200 import colpar as cp
-    if colpar:
-        lo, hi = cp.shard_range(n_total, world, rank)
-        n = hi - lo
-    else:
-        n = n_total
-    out_dtype = torch.bfloat16 if w["out"] == "bf16" else torch.float32
+    cfg = workload_config(name, w, world, rank)
+    m, n_total, k = w["m"], w["n"], w["k"]
+    is_colpar = name == "colpar"
+    lo, hi = shard_range(n_total, world, rank) if is_colpar else (0, n_total)
+    n = hi - lo
+    nsets = cfg["operand_sets"]
     requant = w["out"] == "nvfp4"
-    gen = torch.Generator(device=dev)
+    out_dtype = torch.bfloat16 if w["out"] == "bf16" else torch.float32
     b_std = 0.02 if w["fmt"] == "mxfp8" else 1.0
-    # Operand sets rotate between steps so no step finds its inputs in L2.
-    set_bytes = (m + n) * k * (1.0 if w["fmt"] == "mxfp8" else 0.5)
-    out_bytes = m * n * {"bf16": 2, "fp32": 4, "nvfp4": 0.5625}[w["out"]]
-    nsets = 1 if set_bytes + out_bytes > 3 * 126e6 else 3
-    sets = []
+    layout = q.LAYOUT_MMA_KMAJOR if is_colpar else q.LAYOUT_MMA
+    quant = {"nvfp4": lambda x: q.make_nvfp4(x, layout), "mxfp4": lambda x: q.make_mxfp4(x, layout),
+             "mxfp8": lambda x: q.make_mxfp8(x, layout)}[w["fmt"]]
+    gen = torch.Generator(device=dev)
+    sets, check = [], None
+    rows_s, cols_s = sample_rows(m, 16), sample_cols(n_total, 4096)
     for s in range(nsets):
-        if colpar:
-            # A identical on every rank (seeded), B: this rank's N-slice.
-            gen.manual_seed(SEED + s)
-            A, _ = make_operands(q, torch, dict(w, n=0), m, 1, dev, gen)
-            gen.manual_seed(SEED + 1000 + s * 97 + rank)
-            _, B = make_operands(q, torch, w, 1, n, dev, gen, b_std)
-        else:
-            gen.manual_seed(SEED + s)
-            A, B = make_operands(q, torch, w, m, n, dev, gen, b_std)
+        # A: identical on every rank (same seed), quantised once.  B: the
+        # whole seeded B quantised once (one tensor scale), this rank keeps
+        # its N-shard -- what a checkpoint loader does.
+        gen.manual_seed(SEED + s)
+        xa = torch.randn(m, k, generator=gen, device=dev)
+        A = quant(xa)
+        gen.manual_seed((SEED ^ 0xBB67AE85) + s)
+        xb = torch.randn(n_total, k, generator=gen, device=dev)
+        if b_std != 1.0:
+            xb *= b_std
+        B_full = quant(xb)
+        B = cp.shard_rows(B_full, lo, hi) if is_colpar else B_full
+        if s == 0 and headline and w["fmt"] == "nvfp4" and not requant and world == 1:
+            # What the CPU checker needs (N = 1 only): the fp32 sample rows
+            # of A and of B (= output columns), the tensors' amax, and the
+            # quantised bytes of those rows.
+            ri = torch.tensor(rows_s, device=dev)
+            ci = torch.tensor(cols_s, device=dev)
+            check = {"rows": rows_s, "cols": cols_s, "m": m, "n": n_total, "k": k,
+                     "bf16": w["out"] == "bf16",
+                     "layout_order": 1 if is_colpar else 0,
+                     "xa_rows": xa[ri].cpu().numpy(), "xb_rows": xb[ci].cpu().numpy(),
+                     "amax_a": float(xa.abs().max().item()), "amax_b": float(xb.abs().max().item()),
+                     "ts_a": float(A.tensor_scale.item()), "ts_b": float(B_full.tensor_scale.item()),
+                     "qa_rows": A.quantized.view(m, k // 2)[ri].cpu().numpy(),
+                     "sfa": A.block_scales.cpu().numpy(),
+                     "qb_rows": B_full.quantized.view(n_total, k // 2)[ci].cpu().numpy(),
+                     "sfb": B_full.block_scales.cpu().numpy()}
+        del xa, xb
         sets.append((A, B))
-    if colpar and world > 1:
-        # A is broadcast once from rank 0 (untimed).
+    if is_colpar and world > 1:
+        # A is broadcast once from rank 0 (untimed); every rank already holds
+        # the same bytes, the broadcast is the deployment's data path.
         for A, _ in sets:
             cp.broadcast_operand([A.quantized, A.block_scales, A.tensor_scale], src=0)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -248,163 +342,187 @@ def run_ours(args, w, rank, world, dist, torch):
         C = torch.empty(m, n, dtype=out_dtype, device=dev)
     torch.cuda.synchronize()
 
-    def gemm_into(aq, asf, ats, bq, bsf, bts, dst, layout):
-        if requant:
-            q.gemm_nvfp4_requant_raw(aq, asf, ats, bq, bsf, bts, out_ts, dst[:qbytes],
-                                     dst[qbytes:], m, n, k, q.LAYOUT_REF_LINEAR, layout,
-                                     status=status)
-        elif w["fmt"] == "nvfp4":
-            q.gemm_nvfp4_raw(aq, asf, ats, bq, bsf, bts, dst, m, n, k, layout, status)
-        elif w["fmt"] == "mxfp4":
-            q.gemm_mxfp4_raw(aq, asf, bq, bsf, dst, m, n, k, layout, status)
-        else:
-            q.gemm_mxfp8_raw(aq, asf, bq, bsf, dst, m, n, k, layout, status)
-
     def step(i):
         A, B = sets[i % nsets]
         if requant:
-            gemm_into(A.quantized, A.block_scales, A.tensor_scale, B.quantized, B.block_scales,
-                      B.tensor_scale, C, A.layout)
+            q.gemm_nvfp4_requant_raw(A.quantized, A.block_scales, A.tensor_scale, B.quantized,
+                                     B.block_scales, B.tensor_scale, out_ts, C[:qbytes],
+                                     C[qbytes:], m, n, k, q.LAYOUT_REF_LINEAR, A.layout,
+                                     status=status)
         else:
             q.block_scaled_gemm(A, B, out=C, status=status)
 
-    flops_rank = 2.0 * m * n * k
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
     rc, code = q.read_status(status)
     if rc != q.OK:
-        raise SystemExit(f"device status {code} during warm-up")
-
+        raise SystemExit(f"{name}: device status {code} during warm-up")
+    est_ms = timed(torch, stream, step, 2, dist) / 2
+    if not headline:
+        steps = max(steps, math.ceil(SUB_MIN_TIMED_S * 1e3 / max(est_ms, 1e-3)))
     with ClockSampler(dev.index) as clocks:
-        # keep the GPU busy briefly before the timed region so the sampler has
-        # loaded samples even for short K
+        # keep the GPU busy briefly before the timed region so the sampler
+        # sees it loaded even for short K
         for i in range(args.warmup):
             step(i)
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
-        # Events only around the K steps: an event record between steps costs
-        # ~2.6 us of device time, which a ~30 us decode step would carry.
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-        ev[0].record(stream)
-        for i in range(args.steps):
-            step(i)
-        ev[-1].record(stream)
-        torch.cuda.synchronize()
-        if dist:
-            dist.barrier()
-    total_ms = ev[0].elapsed_time(ev[-1])
-    # Average launch time over the timed region (one GEMM launch per step).
-    launch_ms = [total_ms / args.steps]
+        total_ms = timed(torch, stream, step, steps, dist)
     rc, code = q.read_status(status)
     if rc != q.OK:
-        raise SystemExit(f"device status {code} in the timed region")
-    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
-    ms_per_step = total_ms / args.steps
-    flops_job = 2.0 * m * n_total * k if colpar else flops_rank * world
-    value_tflops = flops_job * args.steps / (total_ms * 1e-3) / 1e12
+        raise SystemExit(f"{name}: device status {code} in the timed region")
+    ms_per_step = total_ms / steps
+    flops_rank = 2.0 * m * n * k
+    flops_job = 2.0 * m * n_total * k if is_colpar else flops_rank * world
+    value = flops_job * steps / (total_ms * 1e-3) / 1e12
 
-    # ---- optional all-gather of the bf16 output shards (colpar, N > 1)
-    gather = None
-    if colpar and world > 1 and not args.no_allgather:
-        # colpar.gather_columns: NCCL all-gather of the shards + placement
-        # into the full [M, N] matrix.
-        for _ in range(2):
-            full = cp.gather_columns(C, n_total)
-        torch.cuda.synchronize()
-        dist.barrier()
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = max(3, min(args.steps, 10))
-        g0.record(stream)
-        for _ in range(reps):
-            full = cp.gather_columns(C, n_total)
-        g1.record(stream)
-        torch.cuda.synchronize()
-        gt = torch.tensor([g0.elapsed_time(g1) / reps], dtype=torch.float64, device=dev)
-        dist.all_reduce(gt, op=dist.ReduceOp.MAX)
-        gms = float(gt.item())
-        recv = (n_total - n) * m * C.element_size()
-        gather = {"ms": gms, "recv_bytes_per_rank": recv, "gbs_per_rank": recv / (gms * 1e-3) / 1e9,
-                  "gemm_plus_gather_tflops": flops_job / ((ms_per_step + gms) * 1e-3) / 1e12}
-        del full
-        # The same gather fused into the GEMM: every tile is TMA-stored into
-        # every rank's full C over peer memory (CUDA IPC), overlapping NVLink
-        # with the math.  Device time per step, max over ranks.
-        if w["fmt"] == "nvfp4":
-            bufs = cp.GatherBuffers(m, n_total, dev)
-            A, B = sets[0]
-            for _ in range(2):
-                q.gemm_nvfp4_gather(A, B, bufs.ptrs, lo, n_total, status=status)
-            torch.cuda.synchronize()
-            dist.barrier()
-            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            f0.record(stream)
-            for _ in range(reps):
-                q.gemm_nvfp4_gather(A, B, bufs.ptrs, lo, n_total, status=status)
-            f1.record(stream)
-            torch.cuda.synchronize()
-            dist.barrier()
-            rc, code = q.read_status(status)
-            if rc != q.OK:
-                raise SystemExit(f"device status {code} in the fused gather")
-            ft = torch.tensor([f0.elapsed_time(f1) / reps], dtype=torch.float64, device=dev)
-            dist.all_reduce(ft, op=dist.ReduceOp.MAX)
-            fms = float(ft.item())
-            gather["fused"] = {"ms_per_step": fms,
-                               "tflops": flops_job / (fms * 1e-3) / 1e12,
-                               "kernel": "gemm_pair_kernel, epilogue TMA stores to all ranks"}
-            bufs.close()
+    pk = peaks()
+    ratio = 2.0 if w["fmt"] == "mxfp8" else 4.0
+    peak_tflops = pk["bf16_tflops"] * ratio
+    # This rank's launches over the timed region (the max over ranks is in
+    # ms_per_step); one GEMM launch per step.
+    achieved = flops_rank / (ms_per_step * 1e-3) / 1e12
+    tag = {"colpar": f"colpar_n{n}", "nvfp4_8192": "gemm_nvfp4_nvfp4_8192"}.get(
+        name, f"gemm_{w['fmt']}_{name}")
+    rec = {
+        "value": round(value, 2), "unit": "TFLOP/s", "steps": steps,
+        "ms_per_step": round(ms_per_step, 5), "dtype": w["fmt"], "config": cfg,
+        "pct_peak": round(100.0 * value / world / peak_tflops, 2),
+        "roofline": {
+            "bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak_tflops, 1),
+            "unit": "TFLOP/s", "frac": round(achieved / peak_tflops, 4),
+            "traffic": profile_traffic(tag),
+            "traffic_source": "profiles/traffic_per_launch.txt (ncu dram__bytes_read+write of one launch)",
+            "peak_basis": f"{pk['source']} cuBLAS bf16 burst {pk['bf16_tflops']} TF/s x {ratio:g} "
+                          f"(dense {w['fmt']} : bf16 tensor rate on B200); nominal "
+                          f"{9000 if ratio == 4 else 4500} TF/s -> frac "
+                          f"{achieved / (9000 if ratio == 4 else 4500):.4f}",
+            "algorithmic_flop_per_launch": flops_rank,
+            "kernel": "gemm_pair_kernel (cta_group::2, one launch per step)",
+        },
+        "gpu_launches": steps,
+        "clocks": clocks.summary(),
+    }
+    if not headline:
+        return rec
 
-    # ---- end to end through the public API with host buffers
-    A0, B0 = sets[0]
-    host = {name: t_.cpu().pin_memory() for name, t_ in
-            (("aq", A0.quantized), ("asf", A0.block_scales), ("bq", B0.quantized),
-             ("bsf", B0.block_scales))}
-    hts = [A0.tensor_scale.cpu().pin_memory() if hasattr(A0, "tensor_scale") else None,
-           B0.tensor_scale.cpu().pin_memory() if hasattr(B0, "tensor_scale") else None]
-    hout = [torch.empty_like(C, device="cpu").pin_memory() for _ in range(2)]
-    # Two device buffer sets so step i's host->device copies (copy-in
-    # stream) and step i-1's device->host read of the result (copy-out
-    # stream) overlap step i's GEMM, as a serving loop would run them; every
-    # step still moves its full inputs in and its full result out.
-    dA = [{name: torch.empty_like(h, device=dev) for name, h in host.items()} for _ in range(2)]
-    dts = [[None if h is None else torch.empty_like(h, device=dev) for h in hts] for _ in range(2)]
-    dC = [torch.empty_like(C) for _ in range(2)]
-    h2d = sum(h.numel() * h.element_size() for h in host.values()) + \
-        sum(h.numel() * 4 for h in hts if h is not None)
-    d2h = hout[0].numel() * hout[0].element_size()
+    # ---- output gather legs (column-parallel, N > 1)
+    if is_colpar and world > 1 and not args.no_allgather:
+        rec["allgather"] = gather_legs(args, torch, dist, q, cp, sets, step, C, m, n_total, lo,
+                                       n, flops_job, ms_per_step, status, stream, dev)
+
+    # ---- end to end through the public API from fp32 host data
+    rec["e2e"] = e2e_leg(args, torch, dist, q, cp, w, dev, stream, m, n, k, b_std, layout,
+                         flops_job, world)
+    rec["_check"] = check
+    if check is not None:
+        step(0)  # C holds set 0's product for the checker
+        torch.cuda.synchronize()
+        ri = torch.tensor(check["rows"], device=dev)
+        ci = torch.tensor(check["cols"], device=dev)
+        check["c"] = C[ri][:, ci].float().cpu().numpy()
+    return rec
+
+
+def gather_legs(args, torch, dist, q, cp, sets, step, C, m, n_total, lo, n, flops_job,
+                ms_per_step, status, stream, dev):
+    """NCCL all-gather of the shards (rank-major, no placement copy) and the
+    gather fused into the GEMM epilogue (row-major full C on every rank),
+    each timed on the device (max over ranks); the fused result is compared
+    bit for bit with the shards the NCCL leg moved."""
+    step(0)  # C = set 0's shard
+    torch.cuda.synchronize()
+    world = dist.get_world_size()
+    reps = max(3, min(args.steps, 10))
+    gathered = None
+
+    def nccl_gather(_):
+        nonlocal gathered
+        gathered = cp.gather_columns(C, n_total, rank_major=True)
+
+    for i in range(2):
+        nccl_gather(i)
+    gms = timed(torch, stream, nccl_gather, reps, dist) / reps
+    recv = (n_total - n) * m * C.element_size()
+    out = {"nccl": {"ms": round(gms, 4), "layout": "rank-major [P, M, N/P]",
+                    "recv_bytes_per_rank": recv, "gbs_per_rank": round(recv / (gms * 1e-3) / 1e9, 1),
+                    "gemm_plus_gather_tflops": round(flops_job / ((ms_per_step + gms) * 1e-3) / 1e12, 2)}}
+    bufs = cp.GatherBuffers(m, n_total, dev)
+    A, B = sets[0]
+
+    def fused(_):
+        q.gemm_nvfp4_gather(A, B, bufs.ptrs, lo, n_total, status=status)
+
+    # The timed loop calls the kernel back to back with identical inputs:
+    # each step overwrites the peers' buffers with the same values, so no
+    # reader is disturbed (colpar_gemm_fused orders ranks between steps).
+    for i in range(2):
+        fused(i)
+    fms = timed(torch, stream, fused, reps, dist) / reps
+    rc, code = q.read_status(status)
+    if rc != q.OK:
+        raise SystemExit(f"device status {code} in the fused gather")
+    # Every rank's full C must hold every rank's shard exactly as the local
+    # GEMM wrote it (the shards the NCCL leg gathered).
+    ok = True
+    for r in range(world):
+        a, b = cp.shard_range(n_total, world, r)
+        ok &= bool(torch.equal(bufs.c[:, a:b], gathered[r, :, : b - a]))
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    out["fused"] = {"ms_per_step": round(fms, 4), "tflops": round(flops_job / (fms * 1e-3) / 1e12, 2),
+                    "kernel": "gemm_pair_kernel, epilogue TMA stores to all ranks",
+                    "nvlink_gbs_per_rank": round(recv / (fms * 1e-3) / 1e9, 1)}
+    out["parity"] = ("ok: every rank's fused full C equals the NCCL-gathered local shards bit for bit"
+                     if flag.item() == 1 else "FAIL: fused gather differs from the local shards")
+    bufs.close()
+    return out
+
+
+def e2e_leg(args, torch, dist, q, cp, w, dev, stream, m, n, k, b_std, layout, flops_job, world):
+    """The public API end to end from fp32 host data: per step H2D of A and
+    this rank's B rows (pinned), qg_quantize_nvfp4 of both, the GEMM, D2H of
+    the bf16 result.  Copies, quantisation and the GEMM run on three streams
+    over two buffer sets, as a serving loop would run them; every step still
+    moves its full inputs in and its full result out."""
+    if w["fmt"] != "nvfp4" or w["out"] != "bf16":
+        return None
+    g = torch.Generator(device=dev).manual_seed(SEED + 77)
+    ha = torch.randn(m, k, generator=g, device=dev).cpu().pin_memory()
+    hb = (torch.randn(n, k, generator=g, device=dev) * b_std).cpu().pin_memory()
+    hout = [torch.empty(m, n, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    dA = [torch.empty_like(ha, device=dev) for _ in range(2)]
+    dB = [torch.empty_like(hb, device=dev) for _ in range(2)]
+    dC = [torch.empty(m, n, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    ws = [torch.empty(int(q.lib().qg_quantize_workspace_bytes()), dtype=torch.uint8, device=dev)
+          for _ in range(2)]
+    h2d = (ha.numel() + hb.numel()) * 4
+    d2h = m * n * 2
     s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    ev_in = [torch.cuda.Event() for _ in range(2)]     # inputs of buffer set landed
-    ev_gemm = [torch.cuda.Event() for _ in range(2)]   # GEMM on buffer set done
-    ev_out = [torch.cuda.Event() for _ in range(2)]    # result of buffer set read back
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_gemm = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
     for e_ in ev_gemm + ev_out:
         e_.record(stream)
 
     def e2e_step(i):
         b_ = i % 2
         with torch.cuda.stream(s_in):
-            s_in.wait_event(ev_gemm[b_])            # set b_ free (GEMM i-2 consumed it)
-            for name in host:
-                dA[b_][name].copy_(host[name], non_blocking=True)
-            for d_, h_ in zip(dts[b_], hts):
-                if h_ is not None:
-                    d_.copy_(h_, non_blocking=True)
+            s_in.wait_event(ev_gemm[b_])            # set b_ free (step i-2 consumed it)
+            dA[b_].copy_(ha, non_blocking=True)
+            dB[b_].copy_(hb, non_blocking=True)
             ev_in[b_].record(s_in)
         stream.wait_event(ev_in[b_])
         stream.wait_event(ev_out[b_])               # C[b_] read back (step i-2)
-        gemm_into(dA[b_]["aq"], dA[b_]["asf"], dts[b_][0], dA[b_]["bq"], dA[b_]["bsf"],
-                  dts[b_][1], dC[b_], A0.layout)
+        A = q.make_nvfp4(dA[b_], layout, workspace=ws[b_])
+        B = q.make_nvfp4(dB[b_], layout, workspace=ws[b_])
+        q.block_scaled_gemm(A, B, out=dC[b_])
         ev_gemm[b_].record(stream)
         with torch.cuda.stream(s_out):
             s_out.wait_event(ev_gemm[b_])
             hout[b_].copy_(dC[b_], non_blocking=True)
             ev_out[b_].record(s_out)
 
-    e2e_steps = max(3, min(args.steps, 20))
+    steps = max(3, min(args.steps, 20))
     for i in range(3):
         e2e_step(i)
     torch.cuda.synchronize()
@@ -413,85 +531,35 @@ def run_ours(args, w, rank, world, dist, torch):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     s_in.wait_stream(stream)
-    for i in range(e2e_steps):
+    for i in range(steps):
         e2e_step(i)
     stream.wait_stream(s_out)
     e1.record(stream)
     torch.cuda.synchronize()
-    et = torch.tensor([e0.elapsed_time(e1) / e2e_steps], dtype=torch.float64, device=dev)
+    et = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(et, op=dist.ReduceOp.MAX)
     e2e_ms = float(et.item())
-    rc, code = q.read_status(status)
-    if rc != q.OK:
-        raise SystemExit(f"device status {code} in the e2e region")
-
-    if rank != 0:
-        return None
-    pk = peaks()
-    ratio = 2.0 if w["fmt"] == "mxfp8" else 4.0
-    peak_tflops = pk["bf16_tflops"] * ratio
-    avg_launch_ms = statistics.mean(launch_ms)
-    achieved = flops_rank / (avg_launch_ms * 1e-3) / 1e12
-    tag = f"gemm_{w['fmt']}_{args.workload_name}"
-    line = {
-        "metric": METRIC,
-        "value": round(value_tflops, 2),
-        "unit": "TFLOP/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(ms_per_step, 5),
-        "higher_is_better": True,
-        "scaling": "strong" if colpar else "weak",
-        "vs_baseline": None,
-        "dtype": w["fmt"],
-        "data": "synthetic (seeded torch.randn N(0,1); weights N(0,0.02) for mxfp8), quantised "
-                "on the device before timing",
-        "config": {
-            "workload": f"{w['fmt']}_gemm_{m}x{n_total}x{k}_{w['out']}out",
-            "baseline_config_index": w["cfg"], "m": m, "n": n_total, "k": k,
-            "n_per_rank": n, "out": w["out"],
-            "parallelism": f"colpar{world}" if colpar else (f"replica{world}" if world > 1 else "single"),
-            "l2": (f"{nsets} rotating operand sets ({set_bytes / 1e6:.0f} MB each) + "
-                   f"{out_bytes / 1e6:.0f} MB output per step vs 126 MB L2"),
-        },
-        "pct_peak": round(100.0 * value_tflops / world / peak_tflops, 2),
-        "roofline": {
-            "bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak_tflops, 1),
-            "unit": "TFLOP/s", "frac": round(achieved / peak_tflops, 4),
-            "traffic": profile_traffic(tag),
-            "peak_basis": f"{pk['source']} cuBLAS bf16 burst {pk['bf16_tflops']} TF/s x {ratio:g} "
-                          f"(dense {w['fmt']} : bf16 tensor rate on B200); nominal "
-                          f"{9000 if ratio == 4 else 4500} TF/s -> frac "
-                          f"{achieved / (9000 if ratio == 4 else 4500):.4f}",
-            "algorithmic_flop_per_launch": flops_rank,
-        },
-        "e2e": {"value": round(flops_job / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                "ms_per_step": round(e2e_ms, 4),
-                "pipeline": "H2D, GEMM and D2H on three streams over two buffer sets"},
-        "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
-    }
-    if gather:
-        line["allgather"] = gather
-    if world == 1 and not args.no_cpu_baseline:
-        try:
-            line["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_budget)
-        except ValueError as e:  # the reference's CPU path covers NVFP4 only
-            line["cpu_baseline"] = {"unavailable": str(e)}
-    return line
+    return {"value": round(flops_job / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "ms_per_step": round(e2e_ms, 4), "steps": steps,
+            "work_per_step": "H2D fp32 A and this rank's B rows, qg_quantize_nvfp4 of both, "
+                             "qg_gemm_nvfp4, D2H of the bf16 C"
+                             + ("; at N > 1 each rank quantises its B rows under their own tensor "
+                                "scale (same work; the timed `value` runs shards of one quantised B)"
+                                if world > 1 else ""),
+            "pipeline": "H2D, quantise+GEMM and D2H on three streams over two buffer sets",
+            "gpu_launches_per_step": 5}
 
 
-def run_skinny(args, w, rank, world, dist, torch):
+def run_skinny(args, w, rank, world, dist, torch, steps, headline=True):
     """Decode GEMM: bf16 activations with 0.1% outliers
     x50, pre-quantised NVFP4 weights N(0, 0.02); one step = one
     qg_gemm_nvfp4_skinny call (activation amax + quantise + stream-K GEMM +
-    scale/convert).  Metric: algorithmic HBM bytes / step time."""
+    scale/convert in one cooperative launch).  Metric: algorithmic HBM bytes /
+    step time."""
     from cuda_optimazation_b200 import qgemm as q
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
-    torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream()
     m, n, k = w["m"], w["n"], w["k"]
     gen = torch.Generator(device=dev)
@@ -514,9 +582,9 @@ def run_skinny(args, w, rank, world, dist, torch):
     for i in range(args.warmup):
         call(i)
     torch.cuda.synchronize()
-    # A decode step is ~20 us of GPU work, less than the host needs to issue
-    # one call (tensor-map encodes, 5 launches, Python/ctypes), so each step
-    # is one CUDA-graph replay of the public call, as a decode loop runs it.
+    # A decode step is ~30 us of GPU work, less than the host needs to issue
+    # one call (tensor-map encodes, Python/ctypes), so each step is one
+    # CUDA-graph replay of the public call, as a decode loop runs it.
     graphs = []
     for i in range(2):
         g = torch.cuda.CUDAGraph()
@@ -530,40 +598,40 @@ def run_skinny(args, w, rank, world, dist, torch):
 
     for i in range(args.warmup):
         step(i)
-    torch.cuda.synchronize()
+    est_ms = timed(torch, stream, step, 4, dist) / 4
+    if not headline:
+        steps = max(steps, math.ceil(SUB_MIN_TIMED_S * 1e3 / max(est_ms, 1e-3)))
     with ClockSampler(dev.index) as clocks:
         for i in range(args.warmup):
             step(i)
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
-        # Events only around the K steps: an event record between steps costs
-        # ~2.6 us of device time, which a ~30 us decode step would carry.
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-        ev[0].record(stream)
-        for i in range(args.steps):
-            step(i)
-        ev[-1].record(stream)
-        torch.cuda.synchronize()
-        if dist:
-            dist.barrier()
+        total_ms = timed(torch, stream, step, steps, dist)
     rc, code = q.read_status(status)
     if rc != q.OK:
         raise SystemExit(f"device status {code}")
-    total_ms = ev[0].elapsed_time(ev[-1])
-    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms = float(t.item())
-    ms = total_ms / args.steps
+    ms = total_ms / steps
     bytes_step = n * k * (0.5 + 1 / 16) + m * k * 2 + m * n * 2
-    value = bytes_step * world * args.steps / (total_ms * 1e-3) / 1e9
+    value = bytes_step * world * steps / (total_ms * 1e-3) / 1e9
+    pk = peaks()
+    rec = {
+        "value": round(value, 1), "unit": "GB/s", "steps": steps, "ms_per_step": round(ms, 5),
+        "dtype": "nvfp4", "config": workload_config(f"skinny_m{m}", w, world, rank),
+        "tflops": round(2.0 * m * n * k / (ms * 1e-3) / 1e12, 2),
+        "roofline": {"bound": "hbm", "achieved": round(bytes_step / (ms * 1e-3) / 1e9, 1),
+                     "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(bytes_step / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                     "traffic": profile_traffic(f"gemm_skinny_m{m}"),
+                     "peak_basis": f"{pk['source']} STREAM copy GB/s; achieved counts the whole "
+                                   "fused call (one cooperative launch: activation quantisation + GEMM) as the unit",
+                     "algorithmic_bytes_per_call": int(bytes_step),
+                     "kernel": "gemm_skinny_kernel (one cooperative launch per call)"},
+        "gpu_launches": steps,  # one kernel per call
+        "clocks": clocks.summary(),
+    }
+    if not headline:
+        return rec
 
     # End to end: every step copies its activations in from pinned host
-    # memory and its result out to pinned host memory.  Two buffer sets (and
-    # the two weight sets) alternate so that step i's host->device copy and
-    # step i-1's device->host copy overlap step i's call, on their own
-    # streams, as a serving loop would run them.
+    # memory and its result out to pinned host memory, on their own streams.
     hx = [sets[b][0].cpu().pin_memory() for b in range(2)]
     hout = [torch.empty(m, n, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     dx = [torch.empty_like(sets[b][0]) for b in range(2)]
@@ -584,11 +652,11 @@ def run_skinny(args, w, rank, world, dist, torch):
     def e2e_step(i):
         b = i % 2
         with torch.cuda.stream(s_in):
-            s_in.wait_event(ev_call[b])        # dx[b] consumed by call i-2
+            s_in.wait_event(ev_call[b])
             dx[b].copy_(hx[b], non_blocking=True)
             ev_in[b].record(s_in)
         stream.wait_event(ev_in[b])
-        stream.wait_event(ev_out[b])           # dout[b] read back (step i-2)
+        stream.wait_event(ev_out[b])
         ge[b].replay()
         ev_call[b].record(stream)
         with torch.cuda.stream(s_out):
@@ -600,7 +668,7 @@ def run_skinny(args, w, rank, world, dist, torch):
         e2e_step(i)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = max(4, min(args.steps, 50))
+    reps = max(4, min(steps, 50))
     e0.record(stream)
     s_in.wait_stream(stream)
     for i in range(reps):
@@ -609,38 +677,11 @@ def run_skinny(args, w, rank, world, dist, torch):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / reps
-    rc, code = q.read_status(status)
-    if rc != q.OK:
-        raise SystemExit(f"device status {code} in the e2e region")
-    if rank != 0:
-        return None
-    pk = peaks()
-    return {
-        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4",
-        "data": "synthetic (seeded torch.randn; activations N(0,1) with every 1000th x50, "
-                "weights N(0,0.02)); weights quantised before timing",
-        "config": {"workload": f"nvfp4_skinny_gemm_m{m}_n{n}_k{k}_fused_act_quant",
-                   "baseline_config_index": 3, "m": m, "n": n, "k": k, "out": "bf16",
-                   "parallelism": f"replica{world}" if world > 1 else "single",
-                   "l2": "2 alternating 132 MB weight sets vs 126 MB L2",
-                   "launch": "each step replays a CUDA graph of one qg_gemm_nvfp4_skinny call"},
-        "tflops": round(2.0 * m * n * k / (ms * 1e-3) / 1e12, 2),
-        "roofline": {"bound": "hbm", "achieved": round(bytes_step / (ms * 1e-3) / 1e9, 1),
-                     "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(bytes_step / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
-                     "traffic": profile_traffic(f"gemm_skinny_m{m}"),
-                     "peak_basis": f"{pk['source']} STREAM copy GB/s; achieved counts the whole "
-                                   "fused call (one cooperative launch: activation quantisation + GEMM) as the unit",
-                     "algorithmic_bytes_per_call": int(bytes_step)},
-        "e2e": {"value": round(bytes_step / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "h2d_bytes_per_step": int(m * k * 2), "d2h_bytes_per_step": int(m * n * 2),
-                "ms_per_step": round(e2e_ms, 4),
-                "pipeline": "H2D, call and D2H on three streams over two buffer sets"},
-        "gpu_launches": args.steps,  # one kernel per call
-        "clocks": clocks.summary(),
-    }
+    rec["e2e"] = {"value": round(bytes_step / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                  "h2d_bytes_per_step": int(m * k * 2), "d2h_bytes_per_step": int(m * n * 2),
+                  "ms_per_step": round(e2e_ms, 4),
+                  "pipeline": "H2D, call and D2H on three streams over two buffer sets"}
+    return rec
 
 
 # --------------------------------------------------------------------- CPU
@@ -655,8 +696,15 @@ def _cpu_impl():
         return o, None, "port"
 
 
+def cpu_block(w, threads):
+    """The sample block both CPU legs time: NVFP4 quantise + dequantise of
+    `qrows` rows (single-threaded, as the reference) and O2 over an
+    orows x ocols output block (rows spread over the threads)."""
+    return dict(qrows=min(w["m"], 256), orows=min(w["m"], 16 * threads), ocols=min(w["n"], 512))
+
+
 class _CpuPath:
-    """Cost model of the CPU path, measured on bounded samples.
+    """Cost model of the reference's CPU path, measured on bounded samples.
 
     The job is: quantise A (M rows) and B (N rows) with the NVFP4 quantizer,
     dequantise, and run the double-accumulation O2 GEMM over M x N outputs.
@@ -706,37 +754,87 @@ def cpu_baseline(w, budget_s: float = 20.0) -> dict:
     threads = os.cpu_count() or 1
     m, n, k = w["m"], w["n"], w["k"]
     path = _CpuPath(o, ref, w, threads)
-    qrows, orows, ocols = min(m, 64), min(m, threads), min(n, 256)
-    _, t_s, _, t_out = path.sample(qrows, orows, ocols)
-    # Grow the O2 block toward the time budget.
-    scale = max(1.0, (budget_s * 0.8) / max(t_s, 1e-6))
-    orows = int(min(m, max(orows, (orows * scale) // threads * threads)))
-    qrows = min(m, max(256, orows))
-    t_job, t_s, t_row, t_out = path.sample(qrows, orows, ocols)
+    blk = cpu_block(w, threads)
+    res = [path.sample(**blk)]
+    # Repeat the same block (new inputs) toward the time budget.
+    while sum(r[1] for r in res) < budget_s * 0.8 and len(res) < 50:
+        res.append(path.sample(**blk, seed_offset=len(res)))
+    t_row = statistics.mean(r[2] for r in res)
+    t_out = statistics.mean(r[3] for r in res)
+    t_job = (m + n) * t_row + m * n * t_out
     flops = 2.0 * m * n * k
     return {"value": round(flops / t_job / 1e12, 8), "unit": "TFLOP/s", "cores": threads,
             "kind": kind,
-            "sample": (f"{'oracle/_ref (reference headers)' if ref else 'oracle port'}: NVFP4 "
-                       f"quantise+dequantise of {qrows} rows ({t_row * 1e3:.2f} ms/row, one thread, "
-                       f"as the reference) and O2 GEMM of a {orows}x{ocols} output block "
-                       f"({t_out * 1e6:.2f} us/output on {threads} threads); job time "
-                       f"(M+N)*t_row + M*N*t_out = {t_job:.1f}s"),
+            "sample": (f"{'oracle/_ref (reference headers)' if ref else 'oracle port'}: "
+                       f"{len(res)} samples of NVFP4 quantise+dequantise of {blk['qrows']} rows "
+                       f"({t_row * 1e3:.2f} ms/row, one thread, as the reference) and O2 over a "
+                       f"{blk['orows']}x{blk['ocols']} output block ({t_out * 1e6:.2f} us/output "
+                       f"on {threads} threads); job time (M+N)*t_row + M*N*t_out = {t_job:.1f}s"),
             "job_seconds_extrapolated": round(t_job, 2)}
 
 
-def run_reference_arm(args, w, rank, world):
-    """Time the reference's own CPU implementation on bounded samples of the
-    same workload (rank 0 only); each step is one sample."""
+def cpu_check(chk: dict) -> dict:
+    """The CPU checker on the headline GEMM (rank 0, N = 1): the tensor
+    scales against amax/(448*6) (GEMMsm110/include/requant/nvfp4_reference.cuh:66-74),
+    the quantised bytes of the sampled rows of A and B against O1's block
+    rule under them (nvfp4_reference.cuh:84-111), and the GPU output on the
+    sampled rows x sampled columns against O2
+    (cutlass-gemm-cpp-guide/include/guide/block_scale_reference.hpp:10-37):
+    relative Frobenius <= 1e-5 and per element
+    |err| <= 1e-3 * ||oracle row over the sampled columns||_2, plus 2^-8
+    (relative, per element and Frobenius) for bf16 output rounding."""
+    import numpy as np
+    o, _, _ = _cpu_impl()
+    k, order = chk["k"], chk["layout_order"]
+    out = {"rows": len(chk["rows"]), "cols": len(chk["cols"])}
+    ok = True
+    for tag, amax, ts in (("a", chk["amax_a"], chk["ts_a"]), ("b", chk["amax_b"], chk["ts_b"])):
+        want = np.float32(amax) / np.float32(2688.0) if amax > 0 else np.float32(1.0)
+        ok &= bool(np.float32(ts) == want)
+    views = []
+    for x, qrows, sf, rows, total, ts in (
+            (chk["xa_rows"], chk["qa_rows"], chk["sfa"], chk["rows"], chk["m"], chk["ts_a"]),
+            (chk["xb_rows"], chk["qb_rows"], chk["sfb"], chk["cols"], chk["n"], chk["ts_b"])):
+        lq, lsf = o.nvfp4_with_ts(x, ts)
+        qm, _ = o.linear_to_mma(lq, lsf, len(rows), k, 0)
+        ok &= bool(np.array_equal(qrows.ravel(), qm))
+        ok &= bool(np.array_equal(o.scale_rows(sf, rows, total, k, 16, order).ravel(), lsf))
+        qfull = np.zeros((total, k // 2), np.uint8)
+        qfull[rows] = qrows
+        views.append(o.nvfp4_rows(qfull.ravel(), sf, rows, total, k, order))
+    out["quantizer_bytes"] = "bit-exact" if ok else "MISMATCH"
+    (av, asf), (bv, bsf) = views
+    ref = o.gemm(av, bv, asf, bsf, len(chk["rows"]), len(chk["cols"]), k, 16,
+                 threads=os.cpu_count() or 8)
+    ref = (ref * np.float32(np.float32(chk["ts_a"]) * np.float32(chk["ts_b"]))).astype(np.float64)
+    got = chk["c"].astype(np.float64)
+    err = got - ref
+    frob = float(np.linalg.norm(err) / max(np.linalg.norm(ref), 1e-30))
+    bf16_rel = 2.0 ** -8 if chk["bf16"] else 0.0
+    tol = 1e-3 * np.linalg.norm(ref, axis=1, keepdims=True) + bf16_rel * np.abs(ref)
+    worst = float(np.max(np.abs(err) - tol))
+    gemm_ok = bool(np.isfinite(got).all()) and frob <= 1e-5 + bf16_rel and worst <= 0.0
+    out.update({"frob": frob, "worst_excess": worst,
+                "gemm": "within tolerance" if gemm_ok else "OUT OF TOLERANCE"})
+    out["status"] = "ok" if (ok and gemm_ok) else "FAIL"
+    out["how"] = ("oracle O1 bytes of the sampled rows of A and B (rows s*131 % M, B rows = output "
+                  "columns s*197 % N), O2 on the sampled block vs the GPU's bf16 output")
+    return out
+
+
+def run_reference_arm(args, name, w, rank, world):
+    """Time the reference's own CPU implementation on the same sample block
+    as the cpu_baseline leg (rank 0 only); each step is one sample."""
     if rank != 0:
         return None
     o, ref, kind = _cpu_impl()
     threads = os.cpu_count() or 1
     m, n, k = w["m"], w["n"], w["k"]
     path = _CpuPath(o, ref, w, threads)
-    qrows, orows, ocols = min(m, 64), min(m, 4 * threads), min(n, 512)
+    blk = cpu_block(w, threads)
     for i in range(min(args.warmup, 1)):
-        path.sample(qrows, orows, ocols, seed_offset=i + 1)
-    res = [path.sample(qrows, orows, ocols, seed_offset=i + 100) for i in range(args.steps)]
+        path.sample(**blk, seed_offset=i + 1)
+    res = [path.sample(**blk, seed_offset=i + 100) for i in range(args.steps)]
     t_job = statistics.mean(r[0] for r in res)
     t_step = statistics.mean(r[1] for r in res)
     value = 2.0 * m * n * k / t_job / 1e12
@@ -744,15 +842,15 @@ def run_reference_arm(args, w, rank, world):
         "impl": "reference", "metric": METRIC, "value": round(value, 8), "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(t_step * 1e3, 3), "higher_is_better": True,
-        "scaling": "strong" if args.workload_name == "colpar" else "weak", "vs_baseline": None,
+        "scaling": "strong" if name == "colpar" else "weak", "vs_baseline": None,
         "dtype": w["fmt"], "data": "synthetic (seeded std::mt19937_64 N(0,1))",
-        "config": {"workload": f"{w['fmt']}_gemm_{m}x{n}x{k}_{w['out']}out",
-                   "baseline_config_index": w["cfg"], "m": m, "n": n, "k": k},
+        "config": workload_config(name, w, world, rank),
         "cpu_baseline": {"value": round(value, 8), "unit": "TFLOP/s", "cores": threads,
                          "kind": kind,
-                         "sample": f"per step: NVFP4 quantise+dequantise of {qrows} rows (one "
-                                   f"thread) and O2 over a {orows}x{ocols} output block "
-                                   f"({threads} threads); job time (M+N)*t_row + M*N*t_out"},
+                         "sample": f"per step: NVFP4 quantise+dequantise of {blk['qrows']} rows "
+                                   f"(one thread, as the reference) and O2 over a "
+                                   f"{blk['orows']}x{blk['ocols']} output block ({threads} "
+                                   f"threads); job time (M+N)*t_row + M*N*t_out"},
         "e2e": {"value": round(value, 8), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -761,42 +859,71 @@ def run_reference_arm(args, w, rank, world):
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="auto", choices=["auto", *WORKLOADS])
     ap.add_argument("--no-allgather", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-subrecords", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    if args.workload == "auto":
-        args.workload = "colpar" if world > 1 else "nvfp4_8192"
-    args.workload_name = args.workload
-    w = WORKLOADS[args.workload]
+    name = "colpar" if args.workload == "auto" else args.workload
+    w = WORKLOADS[name]
 
     if args.impl == "reference":
         if w["fmt"] != "nvfp4" or w.get("skinny"):
             line = {"impl": "reference", "unavailable":
-                    "the reference has no CPU path for this workload (MXFP8 / decode GEMM)"}
+                    "the reference has no CPU path for this workload (MXFP8 / MXFP4 / decode GEMM)"}
         else:
-            line = run_reference_arm(args, w, rank, world)
+            line = run_reference_arm(args, name, w, rank, world)
         if line is not None:
             print(json.dumps(line), flush=True)
         return
 
     import torch
     dist = None
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
     if world > 1:
         import torch.distributed as td
-        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         td.init_process_group("nccl", device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0))))
         dist = td
-    line = (run_skinny if w.get("skinny") else run_ours)(args, w, rank, world, dist, torch)
-    if line is not None:
+    runner = run_skinny if w.get("skinny") else run_gemm
+    rec = runner(args, name, w, rank, world, dist, torch, args.steps)
+    check = rec.pop("_check", None)
+    torch.cuda.empty_cache()
+    subs = {}
+    if world == 1 and not args.no_subrecords and name == "colpar":
+        for sname in SUBRECORDS:
+            sw = WORKLOADS[sname]
+            fn = run_skinny if sw.get("skinny") else run_gemm
+            subs[sname] = fn(args, sname, sw, rank, world, dist, torch, args.steps, headline=False)
+            torch.cuda.empty_cache()
+    if rank == 0:
+        line = {"metric": METRIC, "value": rec.pop("value"), "unit": rec.pop("unit"),
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": rec.pop("ms_per_step"), "higher_is_better": True,
+                "scaling": "strong" if name == "colpar" else "weak", "vs_baseline": None,
+                "dtype": rec.pop("dtype"),
+                "data": "synthetic (seeded torch.randn N(0,1); B N(0,0.02) for mxfp8), quantised "
+                        "on the device before timing",
+                "config": rec.pop("config")}
+        line.update(rec)
+        if subs:
+            line["subrecords"] = subs
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_baseline(w, budget_s=args.cpu_budget)
+            except ValueError as e:  # the reference's CPU path covers NVFP4 only
+                line["cpu_baseline"] = {"unavailable": str(e)}
+            if check is not None:
+                line["parity"] = cpu_check(check)
+        elif "allgather" in line:
+            line["parity"] = line["allgather"].get("parity")
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()

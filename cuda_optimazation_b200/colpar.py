@@ -52,9 +52,13 @@ def broadcast_operand(tensors, src: int = 0, group=None) -> None:
         dist.broadcast(t, src, group=group)
 
 
-def gather_columns(c_local: torch.Tensor, n: int, group=None, align: int = ALIGN) -> torch.Tensor:
-    """All-gather the column shards [M, n_r] of every rank into the full
-    [M, N] matrix (rank-major shards padded to the largest, then placed)."""
+def gather_columns(c_local: torch.Tensor, n: int, group=None, align: int = ALIGN,
+                   rank_major: bool = False) -> torch.Tensor:
+    """All-gather the column shards [M, n_r] of every rank.  Returns the full
+    [M, N] matrix (rank-major shards padded to the largest, then placed), or
+    with ``rank_major`` the gathered [P, M, max n_r] buffer itself (shard r
+    in ``[r, :, :n_r]``), which skips the strided placement copy of the
+    whole matrix for consumers that index shards (a row-parallel layer)."""
     world = dist.get_world_size(group)
     sizes = shard_sizes(n, world, align)
     m = c_local.shape[0]
@@ -68,6 +72,8 @@ def gather_columns(c_local: torch.Tensor, n: int, group=None, align: int = ALIGN
         dist.all_gather_into_tensor(buf, c_local.contiguous(), group=group)
     else:  # gloo (CPU ranks) has only the list form
         dist.all_gather(list(buf.unbind(0)), c_local.contiguous(), group=group)
+    if rank_major:
+        return buf
     out = torch.empty(m, n, dtype=c_local.dtype, device=c_local.device)
     for r in range(world):
         a, b = shard_range(n, world, r, align)
