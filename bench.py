@@ -552,7 +552,7 @@ def e2e_leg(args, torch, dist, q, cp, w, dev, stream, m, n, k, b_std, layout, fl
             "gpu_launches_per_step": 5}
 
 
-def run_skinny(args, w, rank, world, dist, torch, steps, headline=True):
+def run_skinny(args, name, w, rank, world, dist, torch, steps, headline=True):
     """Decode GEMM: bf16 activations with 0.1% outliers
     x50, pre-quantised NVFP4 weights N(0, 0.02); one step = one
     qg_gemm_nvfp4_skinny call (activation amax + quantise + stream-K GEMM +

@@ -96,7 +96,7 @@ def build_harness() -> Path:
     HARNESS_BIN.parent.mkdir(exist_ok=True)
     cmd = [nvcc(), "-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
            f"-I{ROOT / 'include'}", str(HARNESS_SRC), "-o", str(HARNESS_BIN),
-           f"-L{PKG}", "-lqgemm_b200", "-lcublas", "-Xlinker", "-rpath=$ORIGIN/.."]
+           f"-L{PKG}", "-lqgemm_b200", "-lcublasLt", "-Xlinker", "-rpath=$ORIGIN/.."]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)

@@ -32,7 +32,8 @@
 // applies the north-star tolerance: relative Frobenius error <= 1e-5 and
 // |err| <= 1e-3 * ||row||_2 for fp32 output, plus the bf16 rounding bound
 // for bf16 output.
-#include <cublas_v2.h>
+#include <cublasLt.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -527,47 +528,83 @@ Row run_requant(const Options& o) {
   return r;
 }
 
-// The rate reference: a cuBLAS bf16 tensor-core GEMM of the same M x N x K
-// (C = A . B^T, fp32 accumulate), timed like the backends -- the reference
-// harness divides by a cuBLAS tensor-core GEMM timed in the same run
-// (GEMMquant_sm110/src/quant_gemm_bench.cu:1522-1530).  0 when unavailable.
-double cublas_bf16_gflops(const Options& o) {
+// Seeded values in [-1, 1) written as `bytes_per` bytes per element by
+// `enc` (a constant fill lowers the tensor cores' power draw and flatters
+// the reference's clocks).
+template <typename Enc>
+void fill_random(void* dst, int64_t count, uint64_t seed, int bytes_per, Enc enc) {
+  std::vector<uint8_t> h(static_cast<size_t>(count) * bytes_per);
+  uint64_t x = seed * 0x9e3779b97f4a7c15ull + 1;
+  for (int64_t i = 0; i < count; ++i) {
+    x ^= x << 13, x ^= x >> 7, x ^= x << 17;
+    const float f = static_cast<float>(static_cast<int64_t>(x >> 40) - (1 << 23)) / (1 << 23);
+    enc(f, &h[static_cast<size_t>(i) * bytes_per]);
+  }
+  CHECK_CUDA(cudaMemcpy(dst, h.data(), h.size(), cudaMemcpyHostToDevice));
+}
+
+// The rate reference of the reference harness: a cuBLASLt e4m3 x e4m3 GEMM
+// with fp32 output and fp32 accumulation, heuristic top-1 algorithm with a
+// 64 MiB workspace, of the same M x N x K, timed like the backends
+// (benchmark_cublaslt_fp8_reference, GEMMquant_sm110/src/quant_gemm_bench.cu:1314-1373;
+// the quant rows' RatioToReference divides by it, :1522-1530).  Row-major
+// C[m][n] = A[m][k] . B[n][k]^T is the column-major C^T = B^T' . A with B
+// transposed: cuBLASLt's "TN" FP8 form.  0 when unavailable.
+double cublaslt_fp8_gflops(const Options& o) {
   const int64_t m = o.m, n = o.n, k = o.k;
-  void *a = dalloc(m * k * 2), *b = dalloc(n * k * 2), *c = dalloc(m * n * 2);
-  // Seeded values in [-1, 1) (a constant fill lowers the tensor cores' power
-  // draw and flatters the reference's clocks).
-  auto fill = [&](void* dst, int64_t count, uint64_t seed) {
-    std::vector<uint16_t> h(count);
-    uint64_t x = seed * 0x9e3779b97f4a7c15ull + 1;
-    for (auto& v : h) {
-      x ^= x << 13, x ^= x >> 7, x ^= x << 17;
-      const float f = static_cast<float>(static_cast<int64_t>(x >> 40) - (1 << 23)) / (1 << 23);
-      uint32_t bits;
-      std::memcpy(&bits, &f, 4);
-      v = static_cast<uint16_t>(bits >> 16);
-    }
-    CHECK_CUDA(cudaMemcpy(dst, h.data(), count * 2, cudaMemcpyHostToDevice));
-  };
-  fill(a, m * k, o.seed);
-  fill(b, n * k, o.seed ^ 0xbb67ae85ull);
+  void *a = dalloc(m * k), *b = dalloc(n * k), *c = dalloc(m * n * 4);
+  auto enc8 = [](float f, uint8_t* out) { *out = __nv_fp8_e4m3(f).__x; };
+  fill_random(a, m * k, o.seed, 1, enc8);
+  fill_random(b, n * k, o.seed ^ 0xbb67ae85ull, 1, enc8);
+  constexpr uint64_t kWorkspaceBytes = 64ull << 20;
+  void* ws = dalloc(kWorkspaceBytes);
   double gflops = 0.0;
-  cublasHandle_t h = nullptr;
-  if (cublasCreate(&h) == CUBLAS_STATUS_SUCCESS) {
+  cublasLtHandle_t lt = nullptr;
+  cublasLtMatmulDesc_t op = nullptr;
+  cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
+  cublasLtMatmulPreference_t pref = nullptr;
+  bool ok = cublasLtCreate(&lt) == CUBLAS_STATUS_SUCCESS &&
+            cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F) == CUBLAS_STATUS_SUCCESS;
+  if (ok) {
+    const cublasOperation_t t = CUBLAS_OP_T, nn = CUBLAS_OP_N;
+    ok = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &t, sizeof(t)) ==
+             CUBLAS_STATUS_SUCCESS &&
+         cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &nn, sizeof(nn)) ==
+             CUBLAS_STATUS_SUCCESS &&
+         // first operand: B as a column-major k x n (ld k), transposed
+         cublasLtMatrixLayoutCreate(&la, CUDA_R_8F_E4M3, k, n, k) == CUBLAS_STATUS_SUCCESS &&
+         // second operand: A as a column-major k x m (ld k)
+         cublasLtMatrixLayoutCreate(&lb, CUDA_R_8F_E4M3, k, m, k) == CUBLAS_STATUS_SUCCESS &&
+         cublasLtMatrixLayoutCreate(&lc, CUDA_R_32F, n, m, n) == CUBLAS_STATUS_SUCCESS &&
+         cublasLtMatmulPreferenceCreate(&pref) == CUBLAS_STATUS_SUCCESS &&
+         cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES,
+                                              &kWorkspaceBytes, sizeof(kWorkspaceBytes)) ==
+             CUBLAS_STATUS_SUCCESS;
+  }
+  cublasLtMatmulHeuristicResult_t heur{};
+  int returned = 0;
+  if (ok)
+    ok = cublasLtMatmulAlgoGetHeuristic(lt, op, la, lb, lc, lc, pref, 1, &heur, &returned) ==
+             CUBLAS_STATUS_SUCCESS &&
+         returned > 0 && heur.state == CUBLAS_STATUS_SUCCESS;
+  if (ok) {
     const float alpha = 1.0f, beta = 0.0f;
-    // Row-major C[m][n] = A[m][k] . B[n][k]^T is column-major C^T = B . A^T.
     auto gemm = [&] {
-      return cublasGemmEx(h, CUBLAS_OP_T, CUBLAS_OP_N, static_cast<int>(n), static_cast<int>(m),
-                          static_cast<int>(k), &alpha, b, CUDA_R_16BF, static_cast<int>(k), a,
-                          CUDA_R_16BF, static_cast<int>(k), &beta, c, CUDA_R_16BF,
-                          static_cast<int>(n), CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+      return cublasLtMatmul(lt, op, &alpha, b, la, a, lb, &beta, c, lc, c, lc, &heur.algo, ws,
+                            kWorkspaceBytes, nullptr);
     };
     if (gemm() == CUBLAS_STATUS_SUCCESS) {
       const float ms = time_launches([&] { gemm(); }, o.iterations);
       gflops = 2.0 * m * n * k / (ms * 1e6);
     }
-    cublasDestroy(h);
   }
-  for (void* p : {a, b, c}) cudaFree(p);
+  if (!ok) std::cerr << "cuBLASLt FP8 reference: no runnable algorithm for this shape\n";
+  if (pref) cublasLtMatmulPreferenceDestroy(pref);
+  for (auto l : {la, lb, lc})
+    if (l) cublasLtMatrixLayoutDestroy(l);
+  if (op) cublasLtMatmulDescDestroy(op);
+  if (lt) cublasLtDestroy(lt);
+  for (void* p : {a, b, c, ws}) cudaFree(p);
   return gflops;
 }
 
@@ -575,7 +612,7 @@ void write_row(std::ofstream& csv, const Row& r, const Options& o, double ref_gf
   const double peak_tflops = r.precision.rfind("mxfp8", 0) == 0 ? 4500.0 : 9000.0;  // dense
   const double ratio = ref_gflops > 0.0 ? r.gflops / ref_gflops : 0.0;
   std::cout << r.backend << ": " << r.ms << " ms, " << r.gflops << " GFLOP/s, matched="
-            << r.matched << " (relative Frobenius " << r.frob << "), ratio to cuBLAS bf16 "
+            << r.matched << " (relative Frobenius " << r.frob << "), ratio to cuBLASLt FP8 "
             << ratio << "\n";
   std::cout << "backend_id=" << r.backend << std::setprecision(17) << " time_ms=" << r.ms
             << " work_unit=flop rate_per_second=" << r.gflops * 1e9
@@ -583,7 +620,7 @@ void write_row(std::ofstream& csv, const Row& r, const Options& o, double ref_gf
             << "\n";
   csv << std::setprecision(17) << r.backend << ',' << r.version << ','
       << (o.square ? o.n : o.m) << ',' << r.precision
-      << ",cuBLAS bf16 tensor-core GEMM (rate); host block-scaled oracle (check),"
+      << ",cuBLASLt FP8 e4m3 GEMM (rate); host block-scaled oracle (check),"
       << r.ms << ',' << r.gflops << ',' << ratio << ',' << (r.matched ? 1 : 0) << ','
       << r.gflops / 1e3 << ','
       << 100.0 * r.gflops / 1e3 / peak_tflops << ",1," << o.m << ',' << o.n << ',' << o.k << '\n';
@@ -592,7 +629,7 @@ void write_row(std::ofstream& csv, const Row& r, const Options& o, double ref_gf
 void usage(const char* p) {
   std::cerr << "Usage: " << p << " [N] [backend]\n"
             << "       " << p << " M N K backend [--gpus 1] [--dist normal] [--seed S] [--out-dtype bf16|fp32]\n"
-            << "       (any form) --no-reference skips the cuBLAS bf16 rate reference\n"
+            << "       (any form) --no-reference skips the cuBLASLt FP8 rate reference\n"
             << "       " << p << " --m=M --n=N --k=K [--iterations=I] [--swizzle=S]\n"
             << "backends: all|nvfp4_q1_native_fp4_mainloop|mxfp8_q0_tcgen05_block_scaled|"
                "nvfp4_skinny_q0|nvfp4_q0_tc6_fused_epilogue|mxfp4_q0_tcgen05_block_scaled\n"
@@ -681,9 +718,9 @@ int main(int argc, char** argv) {
   std::cout << "GPU: " << prop.name << " (sm_" << prop.major << prop.minor << ")\n"
             << "M=" << o.m << " N=" << o.n << " K=" << o.k << ", backend=" << o.backend << '\n'
             << "Benchmark policy: warmup=" << kWarmup << ", timed repeats=" << o.iterations << '\n';
-  const double ref_gflops = o.reference ? cublas_bf16_gflops(o) : 0.0;
+  const double ref_gflops = o.reference ? cublaslt_fp8_gflops(o) : 0.0;
   if (o.reference)
-    std::cout << "reference: cuBLAS bf16 tensor-core GEMM " << ref_gflops << " GFLOP/s\n";
+    std::cout << "reference: cuBLASLt FP8 e4m3 GEMM (fp32 out) " << ref_gflops << " GFLOP/s\n";
   std::ofstream csv("quant_sm110_benchmark.csv");
   csv << "BackendId,Version,N,Precision,Reference,TimeMs,GFLOPS,RatioToReference,Matched,"
          "TFLOPS,PctPeak,GPUs,M,NCols,K\n";
