@@ -83,7 +83,8 @@ struct Options {
   bool cutlass_cli = false;
   int iterations = kRepeat;
   bool square = true;  // N form: CSV column N = n
-  bool reference = true;  // time the cuBLAS reference GEMM
+  bool reference = true;  // time the cuBLASLt FP8 rate reference
+  int gpus = 1;           // nvfp4_colpar_q0: GPUs of this process the N split spans
 };
 
 std::vector<float> normal(size_t count, uint64_t seed, float stddev = 1.0f) {
@@ -107,10 +108,11 @@ float e4m3(uint8_t b) {
   return (b & 0x80) ? -v : v;
 }
 float ue8m0(uint8_t b) { return std::ldexp(1.0f, static_cast<int>(b) - 127); }
-size_t scale_offset(int64_t row, int64_t sfc, int64_t rows, int64_t sf_cols) {
-  const int64_t row_blocks = (rows + 127) / 128;
-  (void)sf_cols;
-  const int64_t chunk = (sfc / 4) * row_blocks + row / 128;  // QG_LAYOUT_MMA
+// Byte of scale (row, sfc) in an MMA-layout buffer: QG_LAYOUT_MMA chunk order
+// (scale_layout.hpp:11-26) or, with kmajor, QG_LAYOUT_MMA_KMAJOR.
+size_t scale_offset(int64_t row, int64_t sfc, int64_t rows, int64_t sf_cols, bool kmajor = false) {
+  const int64_t row_blocks = (rows + 127) / 128, sf_blocks = (sf_cols + 3) / 4;
+  const int64_t chunk = kmajor ? (row / 128) * sf_blocks + sfc / 4 : (sfc / 4) * row_blocks + row / 128;
   const int64_t w = row % 128;
   return static_cast<size_t>(chunk * 512 + (w % 32) * 16 + (w / 32) * 4 + sfc % 4);
 }
@@ -122,7 +124,7 @@ struct HostOperand {  // logical values and scales of one quantised operand
 };
 
 HostOperand fetch_nvfp4(const void* dq, const void* dsf, const float* dts, int64_t rows,
-                        int64_t k) {
+                        int64_t k, bool kmajor = false) {
   std::vector<uint8_t> q(rows * k / 2), sf(qg_scale_bytes(rows, k, 16));
   CHECK_CUDA(cudaMemcpy(q.data(), dq, q.size(), cudaMemcpyDeviceToHost));
   CHECK_CUDA(cudaMemcpy(sf.data(), dsf, sf.size(), cudaMemcpyDeviceToHost));
@@ -136,7 +138,8 @@ HostOperand fetch_nvfp4(const void* dq, const void* dsf, const float* dts, int64
     o.v[i] = e2m1((i & 1) ? (b >> 4) : (b & 15));  // low nibble first
   }
   for (int64_t r = 0; r < rows; ++r)
-    for (int64_t c = 0; c < k / 16; ++c) o.s[r * (k / 16) + c] = e4m3(sf[scale_offset(r, c, rows, k / 16)]);
+    for (int64_t c = 0; c < k / 16; ++c)
+      o.s[r * (k / 16) + c] = e4m3(sf[scale_offset(r, c, rows, k / 16, kmajor)]);
   return o;
 }
 
@@ -398,6 +401,267 @@ Row run_skinny(const Options& o) {
   return r;
 }
 
+// Column-parallel NVFP4 GEMM over the first P GPUs of this process
+// (nvfp4_colpar_q0; BASELINE config 5, M=16384 N=53248 K=8192 at P = 1..8).
+// A and B are quantised once on GPU 0 (one tensor scale each, K-major scale
+// chunks so a run of whole 128-row blocks is contiguous); GPU r receives A
+// and the B rows [lo_r, hi_r) (256-row aligned, the split of
+// colpar.shard_range) by peer copies.  A step is one
+// qg_gemm_nvfp4_gather launch per GPU: each GPU computes its columns and its
+// epilogue stores them into every GPU's full bf16 C over NVLink (peer
+// access), so after the step every GPU holds all of C.  The rate is the
+// whole job's FLOPs over the slowest GPU's device time; the GEMM without the
+// gather (each GPU writing only its own C) is printed beside it.  The check
+// runs on the full C of the first and the last GPU.
+Row run_colpar(const Options& o) {
+  const int64_t m = o.m, n = o.n, k = o.k;
+  const int P = o.gpus;
+  int ndev = 0;
+  CHECK_CUDA(cudaGetDeviceCount(&ndev));
+  if (ndev < P) {
+    std::cerr << "nvfp4_colpar_q0: --gpus " << P << " but " << ndev << " GPU(s) visible\n";
+    std::exit(EXIT_FAILURE);
+  }
+  for (int i = 0; i < P; ++i)
+    for (int j = 0; j < P; ++j)
+      if (i != j) {
+        int can = 0;
+        CHECK_CUDA(cudaDeviceCanAccessPeer(&can, i, j));
+        if (!can) {
+          std::cerr << "nvfp4_colpar_q0: GPU " << i << " cannot access GPU " << j << "\n";
+          std::exit(EXIT_FAILURE);
+        }
+        CHECK_CUDA(cudaSetDevice(i));
+        const cudaError_t e = cudaDeviceEnablePeerAccess(j, 0);
+        if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) CHECK_CUDA(e);
+        (void)cudaGetLastError();
+      }
+  // Quantise once on GPU 0.
+  CHECK_CUDA(cudaSetDevice(0));
+  auto ha = normal(m * k, o.seed), hb = normal(n * k, o.seed ^ 0xbb67ae85ull);
+  float *da = static_cast<float*>(dalloc(m * k * 4)), *db = static_cast<float*>(dalloc(n * k * 4));
+  CHECK_CUDA(cudaMemcpy(da, ha.data(), m * k * 4, cudaMemcpyHostToDevice));
+  CHECK_CUDA(cudaMemcpy(db, hb.data(), n * k * 4, cudaMemcpyHostToDevice));
+  const size_t asf_bytes = qg_scale_bytes(m, k, 16), bsf_bytes = qg_scale_bytes(n, k, 16);
+  void *aq0 = dalloc(m * k / 2), *asf0 = dalloc(asf_bytes);
+  void *bq0 = dalloc(n * k / 2), *bsf0 = dalloc(bsf_bytes);
+  float *ats0 = static_cast<float*>(dalloc(4)), *bts0 = static_cast<float*>(dalloc(4));
+  void* ws = dalloc(qg_quantize_workspace_bytes());
+  CHECK_QG(qg_quantize_nvfp4(da, QG_DTYPE_F32, m, k, QG_LAYOUT_MMA_KMAJOR, aq0, asf0, ats0, ws, nullptr));
+  CHECK_QG(qg_quantize_nvfp4(db, QG_DTYPE_F32, n, k, QG_LAYOUT_MMA_KMAJOR, bq0, bsf0, bts0, ws, nullptr));
+  CHECK_CUDA(cudaDeviceSynchronize());
+  // Shards: 256-row blocks spread over the GPUs, the first ones one more.
+  const int64_t blocks = (n + 255) / 256, per = blocks / P, extra = blocks % P;
+  const int64_t chunk_row = ((k / 16 + 3) / 4) * 512;  // scale bytes of one 128-row block
+  struct Gpu {
+    void *aq, *asf, *bq, *bsf, *c, *c_own;
+    float *ats, *bts;
+    uint32_t* status;
+    int64_t lo, hi;
+    cudaEvent_t e0, e1;
+  };
+  std::vector<Gpu> g(P);
+  std::vector<void*> c_ranks(P);
+  for (int r = 0; r < P; ++r) {
+    const int64_t b0 = r * per + std::min<int64_t>(r, extra), b1 = b0 + per + (r < extra ? 1 : 0);
+    g[r].lo = std::min(n, b0 * 256), g[r].hi = std::min(n, b1 * 256);
+    CHECK_CUDA(cudaSetDevice(r));
+    const int64_t rows = g[r].hi - g[r].lo;
+    g[r].aq = dalloc(m * k / 2), g[r].asf = dalloc(asf_bytes);
+    g[r].bq = dalloc(std::max<int64_t>(rows, 1) * k / 2);
+    g[r].bsf = dalloc(std::max<int64_t>((rows + 127) / 128, 1) * chunk_row);
+    g[r].ats = static_cast<float*>(dalloc(4)), g[r].bts = static_cast<float*>(dalloc(4));
+    g[r].c = dalloc(m * n * 2), g[r].c_own = dalloc(m * n * 2);
+    g[r].status = static_cast<uint32_t*>(dalloc(4));
+    CHECK_CUDA(cudaMemset(g[r].status, 0, 4));
+    CHECK_CUDA(cudaMemset(g[r].c, 0xff, m * n * 2));  // NaN pattern: unwritten columns fail the check
+    CHECK_CUDA(cudaMemcpyPeer(g[r].aq, r, aq0, 0, m * k / 2));
+    CHECK_CUDA(cudaMemcpyPeer(g[r].asf, r, asf0, 0, asf_bytes));
+    CHECK_CUDA(cudaMemcpyPeer(g[r].ats, r, ats0, 0, 4));
+    CHECK_CUDA(cudaMemcpyPeer(g[r].bts, r, bts0, 0, 4));
+    if (rows > 0) {
+      CHECK_CUDA(cudaMemcpyPeer(g[r].bq, r, static_cast<uint8_t*>(bq0) + g[r].lo * k / 2, 0,
+                                rows * k / 2));
+      CHECK_CUDA(cudaMemcpyPeer(g[r].bsf, r, static_cast<uint8_t*>(bsf0) + (g[r].lo / 128) * chunk_row,
+                                0, ((rows + 127) / 128) * chunk_row));
+    }
+    CHECK_CUDA(cudaEventCreate(&g[r].e0));
+    CHECK_CUDA(cudaEventCreate(&g[r].e1));
+    c_ranks[r] = g[r].c;
+  }
+  for (int r = 0; r < P; ++r) {
+    CHECK_CUDA(cudaSetDevice(r));
+    CHECK_CUDA(cudaDeviceSynchronize());
+  }
+  // One step: every GPU with a non-empty shard launches its GEMM; `gather`
+  // stores into every GPU's C, otherwise into this GPU's own buffer only.
+  auto step = [&](bool gather) {
+    for (int r = 0; r < P; ++r) {
+      if (g[r].hi <= g[r].lo) continue;
+      CHECK_CUDA(cudaSetDevice(r));
+      void* own = g[r].c_own;
+      CHECK_QG(qg_gemm_nvfp4_gather(g[r].aq, g[r].asf, g[r].ats, g[r].bq, g[r].bsf, g[r].bts,
+                                    gather ? c_ranks.data() : &own, gather ? P : 1, g[r].lo, m,
+                                    g[r].hi - g[r].lo, k, n, QG_LAYOUT_MMA_KMAJOR, g[r].status,
+                                    nullptr));
+    }
+  };
+  // Device time of `repeat` steps per GPU (events on each GPU's stream);
+  // the slowest GPU's average.
+  auto time_steps = [&](bool gather, int repeat) {
+    for (int i = 0; i < kWarmup; ++i) step(gather);
+    for (int r = 0; r < P; ++r) {
+      CHECK_CUDA(cudaSetDevice(r));
+      CHECK_CUDA(cudaDeviceSynchronize());
+    }
+    for (int r = 0; r < P; ++r) {
+      CHECK_CUDA(cudaSetDevice(r));
+      CHECK_CUDA(cudaEventRecord(g[r].e0));
+    }
+    for (int i = 0; i < repeat; ++i) step(gather);
+    float worst = 0.0f;
+    for (int r = 0; r < P; ++r) {
+      CHECK_CUDA(cudaSetDevice(r));
+      CHECK_CUDA(cudaEventRecord(g[r].e1));
+    }
+    for (int r = 0; r < P; ++r) {
+      CHECK_CUDA(cudaSetDevice(r));
+      CHECK_CUDA(cudaEventSynchronize(g[r].e1));
+      float ms = 0.0f;
+      CHECK_CUDA(cudaEventElapsedTime(&ms, g[r].e0, g[r].e1));
+      worst = std::max(worst, ms / repeat);
+    }
+    return worst;
+  };
+  Row r;
+  r.backend = "nvfp4_colpar_q0";
+  r.version = "column-parallel tcgen05 GEMM, epilogue all-gather over NVLink (" +
+              std::to_string(P) + " GPU" + (P > 1 ? "s" : "") + ", B200)";
+  r.precision = "nvfp4->bf16";
+  const float gemm_ms = time_steps(false, o.iterations);
+  r.ms = time_steps(true, o.iterations);
+  r.gflops = 2.0 * m * n * k / (r.ms * 1e6);
+  for (int i = 0; i < P; ++i) {
+    CHECK_CUDA(cudaSetDevice(i));
+    CHECK_QG(qg_read_status(g[i].status, nullptr, nullptr));
+  }
+  std::cout << "nvfp4_colpar_q0: " << P << " GPU(s), GEMM only " << gemm_ms << " ms ("
+            << 2.0 * m * n * k / (gemm_ms * 1e9) << " TFLOP/s), GEMM + all-gather into every "
+            << "GPU's C " << r.ms << " ms\n";
+  CHECK_CUDA(cudaSetDevice(0));
+  auto A = fetch_nvfp4(aq0, asf0, ats0, m, k, true), B = fetch_nvfp4(bq0, bsf0, bts0, n, k, true);
+  r.matched = true;
+  double frob_worst = 0.0;
+  for (int i : {0, P - 1}) {
+    CHECK_CUDA(cudaSetDevice(i));
+    double frob = 0.0;
+    r.matched &= check_rows(A, B, fetch_c(g[i].c, m * n, true), m, n, true, &frob);
+    frob_worst = std::max(frob_worst, frob);
+  }
+  r.frob = frob_worst;
+  for (int i = 0; i < P; ++i) {
+    CHECK_CUDA(cudaSetDevice(i));
+    for (void* p : {g[i].aq, g[i].asf, g[i].bq, g[i].bsf, g[i].c, g[i].c_own,
+                    static_cast<void*>(g[i].ats), static_cast<void*>(g[i].bts),
+                    static_cast<void*>(g[i].status)})
+      cudaFree(p);
+    cudaEventDestroy(g[i].e0);
+    cudaEventDestroy(g[i].e1);
+  }
+  CHECK_CUDA(cudaSetDevice(0));
+  for (void* p : {static_cast<void*>(da), static_cast<void*>(db), aq0, asf0, bq0, bsf0,
+                  static_cast<void*>(ats0), static_cast<void*>(bts0), ws})
+    cudaFree(p);
+  return r;
+}
+
+// The vendor library's Blackwell NVFP4 GEMM on the same operands, as a
+// same-box comparison for nvfp4_q1_native_fp4_mainloop (backend
+// cublaslt_nvfp4_library; not part of `all`).  The reference compares its
+// FP4 rows with CUTLASS example 72b (GEMMquant_sm110/build_and_run.sh:38-75),
+// whose source is not on this machine; cuBLASLt's block-scaled FP4 GEMM
+// (e2m1 data, one ue4m3 scale per 16 K elements, fp32 accumulate, bf16
+// output) is the library kernel of the same operation here.  The operands
+// are this library's NVFP4 bytes in the K-major chunk layout (element 2i in
+// the low nibble; 128-row x 4-scale tiles, row tiles outer), which is the
+// tiled scale layout cuBLASLt reads; the two tensor scales go in as alpha.
+// Checked like every row against the host oracle.
+Row run_cublaslt_nvfp4(const Options& o) {
+  const int64_t m = o.m, n = o.n, k = o.k;
+  auto ha = normal(m * k, o.seed), hb = normal(n * k, o.seed ^ 0xbb67ae85ull);
+  float *da = static_cast<float*>(dalloc(m * k * 4)), *db = static_cast<float*>(dalloc(n * k * 4));
+  CHECK_CUDA(cudaMemcpy(da, ha.data(), m * k * 4, cudaMemcpyHostToDevice));
+  CHECK_CUDA(cudaMemcpy(db, hb.data(), n * k * 4, cudaMemcpyHostToDevice));
+  void *aq = dalloc(m * k / 2), *asf = dalloc(qg_scale_bytes(m, k, 16));
+  void *bq = dalloc(n * k / 2), *bsf = dalloc(qg_scale_bytes(n, k, 16));
+  float *ats = static_cast<float*>(dalloc(4)), *bts = static_cast<float*>(dalloc(4));
+  void* ws = dalloc(qg_quantize_workspace_bytes());
+  CHECK_QG(qg_quantize_nvfp4(da, QG_DTYPE_F32, m, k, QG_LAYOUT_MMA_KMAJOR, aq, asf, ats, ws, nullptr));
+  CHECK_QG(qg_quantize_nvfp4(db, QG_DTYPE_F32, n, k, QG_LAYOUT_MMA_KMAJOR, bq, bsf, bts, ws, nullptr));
+  float ta = 1.0f, tb = 1.0f;
+  CHECK_CUDA(cudaMemcpy(&ta, ats, 4, cudaMemcpyDeviceToHost));
+  CHECK_CUDA(cudaMemcpy(&tb, bts, 4, cudaMemcpyDeviceToHost));
+  void* dc = dalloc(m * n * 2);
+  constexpr uint64_t kWorkspaceBytes = 64ull << 20;
+  void* lws = dalloc(kWorkspaceBytes);
+  Row r;
+  r.backend = "cublaslt_nvfp4_library";
+  r.version = "cuBLASLt block-scaled FP4 (e2m1, ue4m3/16), vendor library";
+  r.precision = "nvfp4->bf16";
+  cublasLtHandle_t lt = nullptr;
+  cublasLtMatmulDesc_t op = nullptr;
+  cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
+  cublasLtMatmulPreference_t pref = nullptr;
+  cublasLtMatmulHeuristicResult_t heur{};
+  int returned = 0;
+  const cublasOperation_t t = CUBLAS_OP_T, nn = CUBLAS_OP_N;
+  const int32_t mode = CUBLASLT_MATMUL_MATRIX_SCALE_VEC16_UE4M3;
+  // First operand: B as a column-major k x n (ld k), transposed; its scales
+  // are B's.  Second: A as a column-major k x m; its scales are A's.
+  const void* sf_first = bsf;
+  const void* sf_second = asf;
+  bool ok = cublasLtCreate(&lt) == CUBLAS_STATUS_SUCCESS &&
+            cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F) == CUBLAS_STATUS_SUCCESS &&
+            cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &t, sizeof(t)) == 0 &&
+            cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &nn, sizeof(nn)) == 0 &&
+            cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_A_SCALE_MODE, &mode, sizeof(mode)) == 0 &&
+            cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_B_SCALE_MODE, &mode, sizeof(mode)) == 0 &&
+            cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_A_SCALE_POINTER, &sf_first, sizeof(sf_first)) == 0 &&
+            cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_B_SCALE_POINTER, &sf_second, sizeof(sf_second)) == 0 &&
+            cublasLtMatrixLayoutCreate(&la, CUDA_R_4F_E2M1, k, n, k) == CUBLAS_STATUS_SUCCESS &&
+            cublasLtMatrixLayoutCreate(&lb, CUDA_R_4F_E2M1, k, m, k) == CUBLAS_STATUS_SUCCESS &&
+            cublasLtMatrixLayoutCreate(&lc, CUDA_R_16BF, n, m, n) == CUBLAS_STATUS_SUCCESS &&
+            cublasLtMatmulPreferenceCreate(&pref) == CUBLAS_STATUS_SUCCESS &&
+            cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES,
+                                                 &kWorkspaceBytes, sizeof(kWorkspaceBytes)) == 0 &&
+            cublasLtMatmulAlgoGetHeuristic(lt, op, la, lb, lc, lc, pref, 1, &heur, &returned) ==
+                CUBLAS_STATUS_SUCCESS &&
+            returned > 0 && heur.state == CUBLAS_STATUS_SUCCESS;
+  const float alpha = ta * tb, beta = 0.0f;
+  auto gemm = [&] {
+    return cublasLtMatmul(lt, op, &alpha, bq, la, aq, lb, &beta, dc, lc, dc, lc, &heur.algo, lws,
+                          kWorkspaceBytes, nullptr);
+  };
+  if (ok) ok = gemm() == CUBLAS_STATUS_SUCCESS;
+  if (ok) {
+    r.ms = time_launches([&] { gemm(); }, o.iterations);
+    r.gflops = 2.0 * m * n * k / (r.ms * 1e6);
+    auto A = fetch_nvfp4(aq, asf, ats, m, k, true), B = fetch_nvfp4(bq, bsf, bts, n, k, true);
+    r.matched = check_rows(A, B, fetch_c(dc, m * n, true), m, n, true, &r.frob);
+  } else {
+    std::cerr << "cuBLASLt NVFP4: no runnable algorithm for this shape\n";
+  }
+  if (pref) cublasLtMatmulPreferenceDestroy(pref);
+  for (auto l : {la, lb, lc})
+    if (l) cublasLtMatrixLayoutDestroy(l);
+  if (op) cublasLtMatmulDescDestroy(op);
+  if (lt) cublasLtDestroy(lt);
+  for (void* p : {static_cast<void*>(da), static_cast<void*>(db), aq, asf, bq, bsf,
+                  static_cast<void*>(ats), static_cast<void*>(bts), ws, dc, lws})
+    cudaFree(p);
+  return r;
+}
+
 // Host form of the NVFP4 block rule the requantising epilogue follows
 // (make_nvfp4_reference, GEMMsm110/include/requant/nvfp4_reference.cuh:76-112):
 // s = smallest e4m3 code >= max|x / ts| / 6, q = e2m1 round-to-nearest-even
@@ -609,7 +873,8 @@ double cublaslt_fp8_gflops(const Options& o) {
 }
 
 void write_row(std::ofstream& csv, const Row& r, const Options& o, double ref_gflops) {
-  const double peak_tflops = r.precision.rfind("mxfp8", 0) == 0 ? 4500.0 : 9000.0;  // dense
+  const int gpus = r.backend == "nvfp4_colpar_q0" ? o.gpus : 1;
+  const double peak_tflops = (r.precision.rfind("mxfp8", 0) == 0 ? 4500.0 : 9000.0) * gpus;  // dense
   const double ratio = ref_gflops > 0.0 ? r.gflops / ref_gflops : 0.0;
   std::cout << r.backend << ": " << r.ms << " ms, " << r.gflops << " GFLOP/s, matched="
             << r.matched << " (relative Frobenius " << r.frob << "), ratio to cuBLASLt FP8 "
@@ -623,16 +888,18 @@ void write_row(std::ofstream& csv, const Row& r, const Options& o, double ref_gf
       << ",cuBLASLt FP8 e4m3 GEMM (rate); host block-scaled oracle (check),"
       << r.ms << ',' << r.gflops << ',' << ratio << ',' << (r.matched ? 1 : 0) << ','
       << r.gflops / 1e3 << ','
-      << 100.0 * r.gflops / 1e3 / peak_tflops << ",1," << o.m << ',' << o.n << ',' << o.k << '\n';
+      << 100.0 * r.gflops / 1e3 / peak_tflops << ',' << gpus << ',' << o.m << ',' << o.n << ',' << o.k << '\n';
 }
 
 void usage(const char* p) {
   std::cerr << "Usage: " << p << " [N] [backend]\n"
-            << "       " << p << " M N K backend [--gpus 1] [--dist normal] [--seed S] [--out-dtype bf16|fp32]\n"
+            << "       " << p << " M N K backend [--gpus P] [--dist normal] [--seed S] [--out-dtype bf16|fp32]\n"
+            << "       (--gpus P > 1 with nvfp4_colpar_q0 only: B split along N over GPUs 0..P-1)\n"
             << "       (any form) --no-reference skips the cuBLASLt FP8 rate reference\n"
             << "       " << p << " --m=M --n=N --k=K [--iterations=I] [--swizzle=S]\n"
             << "backends: all|nvfp4_q1_native_fp4_mainloop|mxfp8_q0_tcgen05_block_scaled|"
-               "nvfp4_skinny_q0|nvfp4_q0_tc6_fused_epilogue|mxfp4_q0_tcgen05_block_scaled\n"
+               "nvfp4_skinny_q0|nvfp4_q0_tc6_fused_epilogue|mxfp4_q0_tcgen05_block_scaled|"
+               "nvfp4_colpar_q0|cublaslt_nvfp4_library (the last two not part of all)\n"
             << "Invoked under a name containing \"mxfp4\" (e.g. cutlass_72a_mxfp4_bf16_b200),\n"
             << "the --m/--n/--k form runs MXFP4 (the CUTLASS 72a MXFP4 runner's binary).\n";
 }
@@ -654,13 +921,10 @@ bool parse(int argc, char** argv, Options* o) {
       // Inputs are N(0, 1) (weights N(0, 0.02) where stated); no other law.
       if (std::string(argv[++i]) != "normal") return false;
     } else if (a == "--gpus" && i + 1 < argc) {
-      // One GPU per process here; the N-sharded multi-GPU runs are
-      // bench.py --workload colpar under torchrun (one process per GPU).
-      if (std::atoi(argv[++i]) != 1) {
-        std::cerr << "--gpus: this binary runs on one GPU; for the column-parallel split use "
-                     "torchrun ... bench.py --gpus P --workload colpar\n";
-        return false;
-      }
+      // GPUs the nvfp4_colpar_q0 split spans (one process driving P GPUs);
+      // every other backend runs on one GPU.
+      o->gpus = std::atoi(argv[++i]);
+      if (o->gpus < 1 || o->gpus > QG_MAX_RANKS) return false;
     }
     else if (a == "-h" || a == "--help") return false;
     else pos.push_back(a);
@@ -688,8 +952,16 @@ bool parse(int argc, char** argv, Options* o) {
     return false;
   }
   const std::string& b = o->backend;
+  if (o->gpus > 1 && b != "nvfp4_colpar_q0") {
+    std::cerr << "--gpus > 1: only nvfp4_colpar_q0 spans several GPUs\n";
+    return false;
+  }
+  if (b == "nvfp4_colpar_q0" && (o->n % 8 != 0 || o->k % 32 != 0)) {
+    std::cerr << "nvfp4_colpar_q0 needs N % 8 == 0 and K % 32 == 0\n";
+    return false;
+  }
   return o->m > 0 && o->n > 0 && o->k > 0 &&
-         (b == "all" || b == "nvfp4_q1_native_fp4_mainloop" ||
+         (b == "all" || b == "nvfp4_colpar_q0" || b == "cublaslt_nvfp4_library" || b == "nvfp4_q1_native_fp4_mainloop" ||
           b == "mxfp8_q0_tcgen05_block_scaled" || b == "nvfp4_skinny_q0" ||
           b == "nvfp4_q0_tc6_fused_epilogue" || b == "mxfp4_q0_tcgen05_block_scaled");
 }
@@ -750,6 +1022,16 @@ int main(int argc, char** argv) {
       write_row(csv, r, o, ref_gflops);
       all_ok &= r.matched;
     }
+  }
+  if (o.backend == "cublaslt_nvfp4_library") {
+    Row r = run_cublaslt_nvfp4(o);
+    write_row(csv, r, o, ref_gflops);
+    all_ok &= r.matched;
+  }
+  if (o.backend == "nvfp4_colpar_q0") {
+    Row r = run_colpar(o);
+    write_row(csv, r, o, ref_gflops);
+    all_ok &= r.matched;
   }
   if (want("nvfp4_skinny_q0")) {
     Row r = run_skinny(o);
