@@ -763,7 +763,18 @@ def cpu_baseline(w, budget_s: float = 20.0) -> dict:
     t_out = statistics.mean(r[3] for r in res)
     t_job = (m + n) * t_row + m * n * t_out
     flops = 2.0 * m * n * k
+    # The same per-row and per-output costs carried to the other NVFP4
+    # configs (both grow linearly in K): what the reference's CPU path would
+    # take for each whole job on this host.
+    per_config = {}
+    for cname in ("nvfp4_256", "nvfp4_8192", "colpar", "skinny_m16", "skinny_m64", "skinny_m128"):
+        cw = WORKLOADS[cname]
+        f = cw["k"] / k
+        tj = (cw["m"] + cw["n"]) * t_row * f + cw["m"] * cw["n"] * t_out * f
+        per_config[cname] = {"job_seconds": round(tj, 3),
+                             "tflops": round(2.0 * cw["m"] * cw["n"] * cw["k"] / tj / 1e12, 8)}
     return {"value": round(flops / t_job / 1e12, 8), "unit": "TFLOP/s", "cores": threads,
+            "per_config_extrapolated": per_config,
             "kind": kind,
             "sample": (f"{'oracle/_ref (reference headers)' if ref else 'oracle port'}: "
                        f"{len(res)} samples of NVFP4 quantise+dequantise of {blk['qrows']} rows "

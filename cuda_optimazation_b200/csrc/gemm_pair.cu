@@ -56,7 +56,11 @@ struct PairCfg {
   static constexpr int kBN = 256;       // N of the pair tile
   static constexpr int kBNHalf = 128;   // rows of B each CTA loads
   static constexpr int kBKBytes = 128;  // K bytes per stage (one SWIZZLE_128B row)
+#ifdef QG_PAIR_STAGES
+  static constexpr int kStages = QG_PAIR_STAGES;  // A/B builds only
+#else
   static constexpr int kStages = 5;
+#endif
   static constexpr int kMmaPerStage = 4;
   // 512-B scale chunks (4 scales per row) along K per 128 rows per stage:
   // 256 K elements (fp4) or 128 (fp8) at 16 or 32 elements per scale.
@@ -151,6 +155,26 @@ __device__ __forceinline__ void stage_scales(const uint8_t* ssfa, const uint8_t*
   tmem_st_32x32b<Cfg::kSfbCols>(t_quad + sfb_col, b);
 }
 
+// Tile order: groups of kGroupM m-tiles, n-tiles outer within a group, so
+// the pairs working at one time share a few A slices and B slices in L2
+// (a wave of 74 pairs covers kGroupM m-tiles x ~5 n-tiles instead of every
+// m-tile of one column, which re-read all of A from HBM once per wave when A
+// outgrew L2: 16384 x 8192 A is 67 MB of values next to a streaming output).
+#ifdef QG_PAIR_GROUP_M
+constexpr int kGroupM = QG_PAIR_GROUP_M;  // A/B builds only
+#else
+constexpr int kGroupM = 16;
+#endif
+__device__ __forceinline__ void tile_coords(int tile, int num_m_tiles, int num_n_tiles, int& mt,
+                                            int& nt) {
+  const int per_group = kGroupM * num_n_tiles;
+  const int g = tile / per_group, r = tile - g * per_group;
+  const int m0 = g * kGroupM;
+  const int gm = num_m_tiles - m0 < kGroupM ? num_m_tiles - m0 : kGroupM;
+  mt = m0 + r % gm;
+  nt = r / gm;
+}
+
 // kOut: 0 fp32 C, 1 bf16 C, 2 NVFP4 output (values + e4m3 block scales,
 // requantised in the epilogue as the reference's tc6 store_tile does,
 // GEMMsm110/include/backends/tc6_nvfp4.cuh:460-503).
@@ -227,10 +251,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
       const uint64_t pol = l2_policy_evict_last();
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      // Counters stepped incrementally: no division on the per-stage path.
+      // Counters stepped incrementally: no division on the per-stage path
+      // (the tile coordinates change once per tile).
       int stage = 0, kb = 0, tile = pair;
       uint32_t phase = 0;
-      int mt = tile % p.num_m_tiles, nt = tile / p.num_m_tiles;
+      int mt, nt;
+      tile_coords(tile, p.num_m_tiles, p.num_n_tiles, mt, nt);
       const bool skip_loads = (kDiag & 4u) != 0;
       for (int g = 0; g < total_kb; ++g) {
         if (g > 0) {
@@ -241,8 +267,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
           if (++kb == nkb) {
             kb = 0;
             tile += npairs;
-            mt = tile % p.num_m_tiles;
-            nt = tile / p.num_m_tiles;
+            tile_coords(tile, p.num_m_tiles, p.num_n_tiles, mt, nt);
           }
         }
         if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.timeout_ns, abort_flag, p.status,
@@ -265,15 +290,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
         // peer's scales complete on its own sf_full.  Scales go first: they
         // are small and land early.
         uint64_t* sf_bar = leader ? &full_bar[stage] : &sf_full[stage];
-        if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::kAbTx + Cfg::kSfTx);
-        else mbar_arrive_expect_tx(&sf_full[stage], Cfg::kSfTx);
+        // Diagnostic builds may leave out the B (kDiag bit 7) or the SFB
+        // (bit 8) loads to weigh the load path; shipped builds load all.
+        constexpr bool kLoadB = (kDiag & 128u) == 0, kLoadSfb = (kDiag & 256u) == 0;
+        constexpr uint32_t kSfTxHere = Cfg::kSfaBytes + (kLoadSfb ? Cfg::kSfbBytes : 0);
+        constexpr uint32_t kAbTxHere = Cfg::kABytes + (kLoadB ? Cfg::kBBytes : 0);
+        if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * kAbTxHere + kSfTxHere);
+        else mbar_arrive_expect_tx(&sf_full[stage], kSfTxHere);
         tma_load_3d(ssfa, &p.tm_sfa, sf_bar, 0, mt * 2 + static_cast<int>(rank),
                     kb * Cfg::kSfChunks, pol);
-        tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol);
+        if (kLoadSfb) tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol);
         tma_load_2d_pair(sa, &p.tm_a, full_leader, kb * Cfg::kBKBytes,
                          mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM, pol);
-        tma_load_2d_pair(sb, &p.tm_b, full_leader, kb * Cfg::kBKBytes,
-                         nt * Cfg::kBN + static_cast<int>(rank) * Cfg::kBNHalf, pol);
+        if (kLoadB)
+          tma_load_2d_pair(sb, &p.tm_b, full_leader, kb * Cfg::kBKBytes,
+                           nt * Cfg::kBN + static_cast<int>(rank) * Cfg::kBNHalf, pol);
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
       }
@@ -438,8 +469,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
     if constexpr (kOut == 2) rq_inv_ts = __fdiv_rn(1.0f, p.rq_ts ? *p.rq_ts : 1.0f);
     for (int it = 0; it < my_tiles; ++it) {
       const int tile = pair + it * npairs;
-      const int mt = tile % p.num_m_tiles;
-      const int nt = tile / p.num_m_tiles;
+      int mt, nt;
+      tile_coords(tile, p.num_m_tiles, p.num_n_tiles, mt, nt);
       bool ok = true;
       if (lane == 0)
         ok = mbar_wait_bounded<false, 32>(acc_full, it & 1, p.timeout_ns, abort_flag, p.status,

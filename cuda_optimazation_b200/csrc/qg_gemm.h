@@ -14,7 +14,8 @@ constexpr int kMaxDevices = 64;
 // through QG_EXTRA_NVCC); shipped builds have none and the branches vanish.
 // Results are wrong by design when bits 0-3 are set: bit 0 skips the scale
 // staging, bit 1 the MMAs, bit 2 the TMA loads (pair / solo kernels), bit 3
-// the epilogue stores; bit 6 makes the decode GEMM's CTA (kDiag >> 16) write
+// the epilogue stores, bit 7 the pair kernel's B loads, bit 8 its SFB loads;
+// bit 6 makes the decode GEMM's CTA (kDiag >> 16) write
 // %globaltimer stamps of its roles into an unused partial slice.  Used to
 // attribute kernel time to its parts.
 #ifndef QG_DIAG_FLAGS

@@ -535,8 +535,8 @@ Row run_colpar(const Options& o) {
   };
   Row r;
   r.backend = "nvfp4_colpar_q0";
-  r.version = "column-parallel tcgen05 GEMM, epilogue all-gather over NVLink (" +
-              std::to_string(P) + " GPU" + (P > 1 ? "s" : "") + ", B200)";
+  r.version = "column-parallel tcgen05 GEMM with epilogue all-gather over NVLink (" +
+              std::to_string(P) + " GPU" + (P > 1 ? "s" : "") + " B200)";
   r.precision = "nvfp4->bf16";
   const float gemm_ms = time_steps(false, o.iterations);
   r.ms = time_steps(true, o.iterations);
@@ -606,7 +606,7 @@ Row run_cublaslt_nvfp4(const Options& o) {
   void* lws = dalloc(kWorkspaceBytes);
   Row r;
   r.backend = "cublaslt_nvfp4_library";
-  r.version = "cuBLASLt block-scaled FP4 (e2m1, ue4m3/16), vendor library";
+  r.version = "cuBLASLt block-scaled FP4 e2m1 with ue4m3 per 16 (vendor library)";
   r.precision = "nvfp4->bf16";
   cublasLtHandle_t lt = nullptr;
   cublasLtMatmulDesc_t op = nullptr;
