@@ -79,8 +79,20 @@ struct PairCfg {
   static constexpr int kSfaCols = kSfChunks * 4;
   static constexpr int kSfbCols = kSfChunks * 8;
   static constexpr int kTmemSfBase = kBN;
-  static constexpr int kTmemSfStageCols = kSfaCols + kSfbCols;
+  // One stage's scales in TMEM: SFA then SFB columns.  Each tcgen05.st costs
+  // about the same whatever its width (measured at 8192^3 NVFP4: leaving
+  // out either of the two stores per stage gained ~15%), so where one slot
+  // per shared-memory stage still fits beside the 256-column accumulator
+  // when padded to the next store width, a stager warp writes a stage with
+  // ONE store (MXFP8: 12 -> 16 columns, MXFP4: 24 -> 32; measured MXFP8 FFN
+  // +10%).  NVFP4's 48 columns would pad to 64, and 5 x 64 does not fit:
+  // four slots with the stagers waiting for each slot's previous MMAs
+  // measured 5% slower than two stores into five 48-column slots.
   static constexpr int kTmemCols = 512;
+  static constexpr int kSfCols = kSfaCols + kSfbCols;
+  static constexpr int kSfColsPadded = kSfCols <= 16 ? 16 : (kSfCols <= 32 ? 32 : 64);
+  static constexpr bool kOneStore = kTmemSfBase + kStages * kSfColsPadded <= kTmemCols;
+  static constexpr int kTmemSfStageCols = kOneStore ? kSfColsPadded : kSfCols;
   static_assert(kTmemSfBase + kStages * kTmemSfStageCols <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   // One MMA issuer with N = 256 MMAs by default: each CTA's tensor core
@@ -108,23 +120,47 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
   }
 }
 
+// Diagnostic timeline (kDiag bit 9; the output buffer is overwritten): the
+// roles of the first pair's CTAs write %globaltimer stamps of their waits
+// into C, 2048 slots per event kind, so a host script can see which wait
+// bounds the pipeline.  Compiled out of shipped builds.
+constexpr bool kTracePair = (kDiag & 512u) != 0;
+
+// The leader's scales complete on the A/B barrier (default), or, with
+// -DQG_PAIR_SPLIT_FULL (A/B builds), on their own barrier with the issuer
+// waiting for both (measured 2% slower at 8192^3: the issuer's extra wait
+// costs more than staging the scales early saves).
+#ifdef QG_PAIR_SPLIT_FULL
+constexpr bool kSplitFull = true;
+#else
+constexpr bool kSplitFull = false;
+#endif
+__device__ __forceinline__ void trace_pair(const GemmParams& p, bool on, int kind, int slot) {
+  if (kTracePair && on && slot < 2048)
+    reinterpret_cast<unsigned long long*>(p.c)[kind * 2048 + slot] = globaltimer_ns();
+}
+
 // One stage's scales of this warp's TMEM quadrant: SFA chunks (4 columns
 // each, the 16-byte row r of a chunk holds rows r, r+32, r+64, r+96) and the
 // two 128-row SFB blocks per chunk (8 columns per chunk).
 template <int kFmt>
 __device__ __forceinline__ void stage_scales(const uint8_t* ssfa, const uint8_t* ssfb,
-                                             uint32_t t_quad, uint32_t sfa_col, uint32_t sfb_col,
-                                             int lane) {
+                                             uint32_t t_slot, int lane) {
   using Cfg = PairCfg<kFmt>;
-  uint32_t a[Cfg::kSfaCols];
-  uint32_t b[Cfg::kSfbCols];
+  // SFA columns [0, kSfaCols), SFB columns [kSfaCols, kSfCols), padding.
+  uint32_t v[Cfg::kOneStore ? Cfg::kTmemSfStageCols : Cfg::kSfCols];
+#pragma unroll
+  for (int i = Cfg::kSfCols; i < (Cfg::kOneStore ? Cfg::kTmemSfStageCols : Cfg::kSfCols); ++i)
+    v[i] = 0u;
+  uint32_t* a = v;
+  uint32_t* b = v + Cfg::kSfaCols;
 #pragma unroll
   for (int c = 0; c < Cfg::kSfChunks; ++c) {
-    const uint4 v = lds128(ssfa + c * 512 + lane * 16);
-    a[4 * c] = v.x;
-    a[4 * c + 1] = v.y;
-    a[4 * c + 2] = v.z;
-    a[4 * c + 3] = v.w;
+    const uint4 x = lds128(ssfa + c * 512 + lane * 16);
+    a[4 * c] = x.x;
+    a[4 * c + 1] = x.y;
+    a[4 * c + 2] = x.z;
+    a[4 * c + 3] = x.w;
     const uint4 w0 = lds128(ssfb + (c * 2) * 512 + lane * 16);
     const uint4 w1 = lds128(ssfb + (c * 2 + 1) * 512 + lane * 16);
     if (Cfg::kIssuers == 2) {
@@ -151,8 +187,13 @@ __device__ __forceinline__ void stage_scales(const uint8_t* ssfa, const uint8_t*
       b[8 * c + 7] = w1.w;
     }
   }
-  tmem_st_32x32b<Cfg::kSfaCols>(t_quad + sfa_col, a);
-  tmem_st_32x32b<Cfg::kSfbCols>(t_quad + sfb_col, b);
+  if constexpr (Cfg::kOneStore) {
+    tmem_st_32x32b<Cfg::kTmemSfStageCols>(t_slot, v);
+  } else {
+    tmem_st_32x32b<Cfg::kSfaCols>(t_slot, *reinterpret_cast<uint32_t(*)[Cfg::kSfaCols]>(a));
+    tmem_st_32x32b<Cfg::kSfbCols>(t_slot + Cfg::kSfaCols,
+                                  *reinterpret_cast<uint32_t(*)[Cfg::kSfbCols]>(b));
+  }
 }
 
 // Tile order: groups of kGroupM m-tiles, n-tiles outer within a group, so
@@ -249,6 +290,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
     // ---------------------------------------------------------------- TMA
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_last();
+      // B tiles (and their scales): within a group of kGroupM m-tiles the
+      // pairs working at one time share a B tile once, A slices are reused
+      // across the group's n-tiles.  A/B builds may mark B evict-first.
+#ifdef QG_PAIR_B_EVICT_FIRST
+      const uint64_t pol_b = l2_policy_evict_first();
+#else
+      const uint64_t pol_b = pol;
+#endif
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
       // Counters stepped incrementally: no division on the per-stage path
@@ -275,6 +324,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
           ok = false;
           break;
         }
+        trace_pair(p, pair == 0, leader ? 0 : 8, g);
         uint8_t* sa = smem + stage * Cfg::kStageBytes;
         uint8_t* sb = sa + Cfg::kABytes;
         uint8_t* ssfa = sb + Cfg::kBBytes;
@@ -286,25 +336,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
         const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
         // The leader's scales complete on its full barrier with both CTAs'
         // A/B bytes (its stagers then wait once per stage, and their arrival
-        // on sf_ready also tells the issuers that A/B have landed); the
+        // on sf_ready also tells the issuer that A/B have landed); the
         // peer's scales complete on its own sf_full.  Scales go first: they
         // are small and land early.
-        uint64_t* sf_bar = leader ? &full_bar[stage] : &sf_full[stage];
+        uint64_t* sf_bar = kSplitFull || !leader ? &sf_full[stage] : &full_bar[stage];
         // Diagnostic builds may leave out the B (kDiag bit 7) or the SFB
         // (bit 8) loads to weigh the load path; shipped builds load all.
         constexpr bool kLoadB = (kDiag & 128u) == 0, kLoadSfb = (kDiag & 256u) == 0;
         constexpr uint32_t kSfTxHere = Cfg::kSfaBytes + (kLoadSfb ? Cfg::kSfbBytes : 0);
         constexpr uint32_t kAbTxHere = Cfg::kABytes + (kLoadB ? Cfg::kBBytes : 0);
-        if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * kAbTxHere + kSfTxHere);
-        else mbar_arrive_expect_tx(&sf_full[stage], kSfTxHere);
+        if (leader)
+          mbar_arrive_expect_tx(&full_bar[stage], 2 * kAbTxHere + (kSplitFull ? 0 : kSfTxHere));
+        if (kSplitFull || !leader) mbar_arrive_expect_tx(&sf_full[stage], kSfTxHere);
         tma_load_3d(ssfa, &p.tm_sfa, sf_bar, 0, mt * 2 + static_cast<int>(rank),
                     kb * Cfg::kSfChunks, pol);
-        if (kLoadSfb) tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol);
+        if (kLoadSfb) tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol_b);
         tma_load_2d_pair(sa, &p.tm_a, full_leader, kb * Cfg::kBKBytes,
                          mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM, pol);
         if (kLoadB)
           tma_load_2d_pair(sb, &p.tm_b, full_leader, kb * Cfg::kBKBytes,
-                           nt * Cfg::kBN + static_cast<int>(rank) * Cfg::kBNHalf, pol);
+                           nt * Cfg::kBN + static_cast<int>(rank) * Cfg::kBNHalf, pol_b);
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
       }
@@ -315,8 +366,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
         uint32_t dummy = 0;
         for (int s = 0; s < Cfg::kStages; ++s) {
           if (!(issued_mask & (1u << s))) continue;
-          mbar_wait_bounded(leader ? &full_bar[s] : &sf_full[s], (issued_parity >> s) & 1u,
-                            p.timeout_ns, &dummy, nullptr, 0);
+          const uint32_t par = (issued_parity >> s) & 1u;
+          if (leader) mbar_wait_bounded(&full_bar[s], par, p.timeout_ns, &dummy, nullptr, 0);
+          if (kSplitFull || !leader)
+            mbar_wait_bounded(&sf_full[s], par, p.timeout_ns, &dummy, nullptr, 0);
         }
         if (!leader) spin_ns(200000);
       }
@@ -353,16 +406,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
           ok = false;
           break;
         }
+        trace_pair(p, pair == 0, 7, it);
         tc_fence_after();
         uint32_t acc = 0;
         for (int kb = 0; kb < nkb; ++kb) {
           // sf_ready covers the A/B bytes too: the leader's stagers arrive
-          // only after full_bar.
+          // only after full_bar (split-barrier builds also wait full_bar).
+          trace_pair(p, pair == 0, 20, it * nkb + kb);
           if (!mbar_wait_bounded(&sf_ready[stage], phase, p.timeout_ns, abort_flag, p.status,
-                                 kDevTimeoutMma)) {
+                                 kDevTimeoutMma) ||
+              (kSplitFull && !mbar_wait_bounded(&full_bar[stage], phase, p.timeout_ns, abort_flag,
+                                                p.status, kDevTimeoutMma))) {
             ok = false;
             break;
           }
+          trace_pair(p, pair == 0, 3, it * nkb + kb);
           tc_fence_after();
           const uint32_t sfb_col = sfa_col + Cfg::kSfaCols;
           if (!skip_mma) {
@@ -387,7 +445,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
               acc = 1;
             }
           }
+          trace_pair(p, pair == 0, 19, it * nkb + kb);
           tc_commit_pair(&empty_bar[stage], 0x3);
+          trace_pair(p, pair == 0, 4, it * nkb + kb);
           if (++stage == Cfg::kStages) {
             stage = 0;
             phase ^= 1u;
@@ -421,22 +481,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
       }
       // Every lane polls (and so acquires) the stage barrier itself: one
       // wait per stage on the stager's serial path.  Leader: the full
-      // barrier (its scales and both CTAs' A/B); peer: its sf_full.
-      bool ok = no_wait || mbar_wait_bounded(leader ? &full_bar[stage] : &sf_full[stage], phase,
-                                             p.timeout_ns, abort_flag, p.status, kDevTimeoutMma);
+      // barrier (its scales and both CTAs' A/B); peer: its sf_full.  The
+      // stage's TMEM slot is free then too (the producer refilled the
+      // stage after the MMAs that read both had completed).
+      bool ok = no_wait || mbar_wait_bounded(kSplitFull || !leader ? &sf_full[stage] : &full_bar[stage],
+                                             phase, p.timeout_ns, abort_flag, p.status,
+                                             kDevTimeoutMma);
       if (!__all_sync(0xffffffffu, ok)) break;
+      trace_pair(p, pair == 0 && warp == 6 && lane == 0, leader ? 1 : 9, g);
       const uint8_t* ssfa = smem + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
       const uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
       const uint32_t sfa_col = Cfg::kTmemSfBase + stage * Cfg::kTmemSfStageCols;
       if (!skip_st) {
-        stage_scales<kFmt>(ssfa, ssfb, t_quad, sfa_col, sfa_col + Cfg::kSfaCols, lane);
+        stage_scales<kFmt>(ssfa, ssfb, t_quad + sfa_col, lane);
         tmem_wait_st();
       }
       tc_fence_before();
       __syncwarp();
       if (leader) {
-        // The stage's A/B bytes are in (the full barrier was the wait), so
-        // sf_ready alone tells the MMA issuers the stage is complete.
         if (lane == 0) mbar_arrive(&sf_ready[stage]);
       } else if (lane == 0) {
         // A release-scoped arrive at cluster scope costs ~1 us here and
@@ -445,6 +507,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
         // writes and tcgen05.fence::before_thread_sync orders them before it.
         mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&sf_ready[stage]), 0));
       }
+      trace_pair(p, pair == 0 && warp == 6 && lane == 0, leader ? 2 : 10, g);
+      trace_pair(p, pair == 0 && lane == 0, 11 + (warp - 6) + (leader ? 0 : 4), g);
     }
   } else {
     // ---------------------------------------------------------------- epilogue
@@ -561,28 +625,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
         }
       } else if constexpr (kOut == 3) {
         // bf16 through TMA stores with eight epilogue warps (2-5, 11-14; two
-        // per TMEM lane quadrant).  For each issuer's 128-column half a warp
-        // loads its 64 columns and hands the half back at once, then
-        // converts, stages the 64 x 32 box in its own swizzled 4 KB buffer
-        // and TMA-stores it to each destination: the next tile's MMAs start
-        // while this tile's output is still being written.
+        // per TMEM lane quadrant); a warp owns TMEM blocks `sub` and
+        // 2 + `sub` (64 columns each) of its quadrant.  With one issuer the
+        // next tile's MMAs need the whole accumulator back, so a warp reads
+        // both blocks before any TMA store (the first converted to bf16 and
+        // staged in the warp's swizzled 4 KB box while the second is read),
+        // hands the accumulator back, and only then issues the box stores:
+        // the next tile's MMAs start while this tile's output is written.
         const int sub = warp >= 11 ? 1 : 0;
         const int row0 = mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM + quad * 32;
         uint8_t* box = epi_smem + (quad * 2 + sub) * 4096;
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          const int tb = 2 * h + sub;
-          uint32_t r0[32], r1[32];
-          tmem_ld_32x32b_x32(t_row + tb * 64, r0);
-          tmem_ld_32x32b_x32(t_row + tb * 64 + 32, r1);
-          tmem_wait_ld();
-          tc_fence_before();
-          __syncwarp();
-          // Two issuers: each 128-column half goes back on its own barrier;
-          // one issuer: the accumulator goes back once both halves are read.
-          if (lane == 0 && (Cfg::kIssuers == 2 || h == 1))
-            mbar_arrive_cluster_relaxed(h ? acc_empty_leader1 : acc_empty_leader0);
-          uint4 v[8];
+        trace_pair(p, pair == 0 && leader && warp == 2 && lane == 0, 5, it);
+        auto convert = [&](const uint32_t(&r0)[32], const uint32_t(&r1)[32], uint4(&v)[8]) {
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const uint32_t* src = c < 4 ? r0 + c * 8 : r1 + (c - 4) * 8;
@@ -592,6 +646,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
                 bf16x2_bits(__uint_as_float(src[4]) * alpha, __uint_as_float(src[5]) * alpha),
                 bf16x2_bits(__uint_as_float(src[6]) * alpha, __uint_as_float(src[7]) * alpha));
           }
+        };
+        auto write_box = [&](const uint4(&v)[8]) {
           if (lane == 0) tma_store_wait_read<0>();  // the box's previous store has read it
           __syncwarp();
 #pragma unroll
@@ -599,10 +655,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
             *reinterpret_cast<uint4*>(box + lane * 128 + ((c ^ (lane & 7)) * 16)) = v[c];
           fence_proxy_async_smem();
           __syncwarp();
+        };
+        auto store_box = [&](int tb) {
           if (lane == 0 && !(kDiag & 8u)) {
             for (int d = 0; d < p.n_out; ++d)
               tma_store_2d(&p.tm_out[d], box, n0 + tmem_block(tb) * 64, row0);
             tma_store_commit();
+          }
+        };
+        if constexpr (Cfg::kIssuers == 1) {
+          {
+            uint32_t r0[32], r1[32];
+            uint4 v[8];
+            tmem_ld_32x32b_x32(t_row + sub * 64, r0);
+            tmem_ld_32x32b_x32(t_row + sub * 64 + 32, r1);
+            tmem_wait_ld();
+            convert(r0, r1, v);
+            write_box(v);  // the previous tile's last store read this box long ago
+          }
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(t_row + (2 + sub) * 64, r0);
+          tmem_ld_32x32b_x32(t_row + (2 + sub) * 64 + 32, r1);
+          tmem_wait_ld();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster_relaxed(acc_empty_leader0);
+          trace_pair(p, pair == 0 && leader && warp == 2 && lane == 0, 6, it);
+          store_box(sub);
+          uint4 v[8];
+          convert(r0, r1, v);
+          write_box(v);
+          store_box(2 + sub);
+        } else {
+          // Two issuers: each 128-column half goes back on its own barrier
+          // as soon as it has been read.
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            const int tb = 2 * h + sub;
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(t_row + tb * 64, r0);
+            tmem_ld_32x32b_x32(t_row + tb * 64 + 32, r1);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster_relaxed(h ? acc_empty_leader1 : acc_empty_leader0);
+            uint4 v[8];
+            convert(r0, r1, v);
+            write_box(v);
+            store_box(tb);
           }
         }
       } else if (Cfg::kEpiBytes > 0 && kOutBf16 && p.n_out > 0) {

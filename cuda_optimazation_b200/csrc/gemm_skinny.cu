@@ -561,18 +561,22 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       mbar_try_wait(&full_bar[stage], phase);
       const uint8_t* ssfw = smem + stage * Cfg::kStageBytes + Cfg::kWBytes + Cfg::kXBytes;
       const uint8_t* ssfx = ssfw + Cfg::kSfwBytes;
-      uint32_t a[4 * Cfg::kSfChunks], b[4 * Cfg::kSfChunks];
+      // Weight scales in columns [0, 32), activation scales in [32, 64) of
+      // the stage's slot, written with ONE tcgen05.st (a store costs about
+      // the same whatever its width).
+      uint32_t v[8 * Cfg::kSfChunks];
+      uint32_t* a = v;
+      uint32_t* b = v + 4 * Cfg::kSfChunks;
 #pragma unroll
       for (int c = 0; c < Cfg::kSfChunks; ++c) {
-        const uint4 v = lds128(ssfw + c * 512 + lane * 16);
+        const uint4 x = lds128(ssfw + c * 512 + lane * 16);
         const uint4 w = lds128(ssfx + c * 512 + lane * 16);
-        a[4 * c] = v.x; a[4 * c + 1] = v.y; a[4 * c + 2] = v.z; a[4 * c + 3] = v.w;
+        a[4 * c] = x.x; a[4 * c + 1] = x.y; a[4 * c + 2] = x.z; a[4 * c + 3] = x.w;
         b[4 * c] = w.x; b[4 * c + 1] = w.y; b[4 * c + 2] = w.z; b[4 * c + 3] = w.w;
       }
       const uint32_t col = Cfg::kTmemSfBase + stage * Cfg::kSfStageCols;
       if (!(kDiag & 1u)) {
-        tmem_st_32x32b<4 * Cfg::kSfChunks>(t_quad + col, a);
-        tmem_st_32x32b<4 * Cfg::kSfChunks>(t_quad + col + 4 * Cfg::kSfChunks, b);
+        tmem_st_32x32b<8 * Cfg::kSfChunks>(t_quad + col, v);
         tmem_wait_st();
       }
       tc_fence_before();
