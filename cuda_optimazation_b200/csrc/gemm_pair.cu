@@ -67,8 +67,9 @@ struct PairCfg {
   static constexpr int kSfChunks = kFmt == kFmtNvfp4 ? 4 : (kFmt == kFmtMxfp4 ? 2 : 1);
   static constexpr int kABytes = kBM * kBKBytes;
   static constexpr int kBBytes = kBNHalf * kBKBytes;
-  static constexpr int kSfaBytes = kSfChunks * 512;
-  static constexpr int kSfbBytes = kSfChunks * 512 * 2;  // all 256 N rows in each CTA
+  // (kDiag bit 11: a diagnostic build without scale loads or their smem.)
+  static constexpr int kSfaBytes = (kDiag & 2048u) ? 0 : kSfChunks * 512;
+  static constexpr int kSfbBytes = (kDiag & 2048u) ? 0 : kSfChunks * 512 * 2;  // all 256 N rows in each CTA
   static constexpr int kAbTx = kABytes + kBBytes;
   static constexpr int kSfTx = kSfaBytes + kSfbBytes;
   static constexpr int kStageBytes = (kAbTx + kSfTx + 1023) / 1024 * 1024;
@@ -92,7 +93,8 @@ struct PairCfg {
   static constexpr int kSfCols = kSfaCols + kSfbCols;
   static constexpr int kSfColsPadded = kSfCols <= 16 ? 16 : (kSfCols <= 32 ? 32 : 64);
   static constexpr bool kOneStore = kTmemSfBase + kStages * kSfColsPadded <= kTmemCols;
-  static constexpr int kTmemSfStageCols = kOneStore ? kSfColsPadded : kSfCols;
+  static constexpr int kTmemSfStageCols =
+      (kDiag & 2048u) ? 16 : (kOneStore ? kSfColsPadded : kSfCols);
   static_assert(kTmemSfBase + kStages * kTmemSfStageCols <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   // One MMA issuer with N = 256 MMAs by default: each CTA's tensor core
@@ -342,14 +344,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
         uint64_t* sf_bar = kSplitFull || !leader ? &sf_full[stage] : &full_bar[stage];
         // Diagnostic builds may leave out the B (kDiag bit 7) or the SFB
         // (bit 8) loads to weigh the load path; shipped builds load all.
-        constexpr bool kLoadB = (kDiag & 128u) == 0, kLoadSfb = (kDiag & 256u) == 0;
+        constexpr bool kLoadB = (kDiag & 128u) == 0;
+        constexpr bool kLoadSfb = (kDiag & 256u) == 0 && Cfg::kSfbBytes > 0;
         constexpr uint32_t kSfTxHere = Cfg::kSfaBytes + (kLoadSfb ? Cfg::kSfbBytes : 0);
         constexpr uint32_t kAbTxHere = Cfg::kABytes + (kLoadB ? Cfg::kBBytes : 0);
         if (leader)
           mbar_arrive_expect_tx(&full_bar[stage], 2 * kAbTxHere + (kSplitFull ? 0 : kSfTxHere));
         if (kSplitFull || !leader) mbar_arrive_expect_tx(&sf_full[stage], kSfTxHere);
-        tma_load_3d(ssfa, &p.tm_sfa, sf_bar, 0, mt * 2 + static_cast<int>(rank),
-                    kb * Cfg::kSfChunks, pol);
+        if (Cfg::kSfaBytes > 0)
+          tma_load_3d(ssfa, &p.tm_sfa, sf_bar, 0, mt * 2 + static_cast<int>(rank),
+                      kb * Cfg::kSfChunks, pol);
         if (kLoadSfb) tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol_b);
         tma_load_2d_pair(sa, &p.tm_a, full_leader, kb * Cfg::kBKBytes,
                          mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM, pol);
