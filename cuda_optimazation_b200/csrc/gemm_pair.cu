@@ -137,6 +137,15 @@ constexpr bool kSplitFull = true;
 #else
 constexpr bool kSplitFull = false;
 #endif
+// A/B builds (-DQG_PAIR_SF_CP): the MMA issuer moves each stage's scales
+// into TMEM with tcgen05.cp (cta_group::2, 32x128b.warpx4, one per 512-byte
+// chunk) ahead of its MMAs instead of the stager warps' tcgen05.st; both
+// CTAs' scale loads then complete on the leader's full barrier.
+#ifdef QG_PAIR_SF_CP
+constexpr bool kSfCp = true;
+#else
+constexpr bool kSfCp = false;
+#endif
 __device__ __forceinline__ void trace_pair(const GemmParams& p, bool on, int kind, int slot) {
   if (kTracePair && on && slot < 2048)
     reinterpret_cast<unsigned long long*>(p.c)[kind * 2048 + slot] = globaltimer_ns();
@@ -341,7 +350,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
         // on sf_ready also tells the issuer that A/B have landed); the
         // peer's scales complete on its own sf_full.  Scales go first: they
         // are small and land early.
-        uint64_t* sf_bar = kSplitFull || !leader ? &sf_full[stage] : &full_bar[stage];
+        uint64_t* sf_bar = (kSplitFull || !leader) && !kSfCp ? &sf_full[stage] : &full_bar[stage];
         // Diagnostic builds may leave out the B (kDiag bit 7) or the SFB
         // (bit 8) loads to weigh the load path; shipped builds load all.
         constexpr bool kLoadB = (kDiag & 128u) == 0;
@@ -349,12 +358,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
         constexpr uint32_t kSfTxHere = Cfg::kSfaBytes + (kLoadSfb ? Cfg::kSfbBytes : 0);
         constexpr uint32_t kAbTxHere = Cfg::kABytes + (kLoadB ? Cfg::kBBytes : 0);
         if (leader)
-          mbar_arrive_expect_tx(&full_bar[stage], 2 * kAbTxHere + (kSplitFull ? 0 : kSfTxHere));
-        if (kSplitFull || !leader) mbar_arrive_expect_tx(&sf_full[stage], kSfTxHere);
-        if (Cfg::kSfaBytes > 0)
-          tma_load_3d(ssfa, &p.tm_sfa, sf_bar, 0, mt * 2 + static_cast<int>(rank),
-                      kb * Cfg::kSfChunks, pol);
-        if (kLoadSfb) tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol_b);
+          mbar_arrive_expect_tx(&full_bar[stage],
+                                2 * kAbTxHere + (kSfCp ? 2 * kSfTxHere : (kSplitFull ? 0 : kSfTxHere)));
+        if ((kSplitFull || !leader) && !kSfCp) mbar_arrive_expect_tx(&sf_full[stage], kSfTxHere);
+        if (kSfCp) {
+          if (Cfg::kSfaBytes > 0)
+            tma_load_3d_pair(ssfa, &p.tm_sfa, full_leader, 0, mt * 2 + static_cast<int>(rank),
+                             kb * Cfg::kSfChunks, pol);
+          if (kLoadSfb)
+            tma_load_3d_pair(ssfb, &p.tm_sfb, full_leader, 0, nt * 2, kb * Cfg::kSfChunks, pol_b);
+        } else {
+          if (Cfg::kSfaBytes > 0)
+            tma_load_3d(ssfa, &p.tm_sfa, sf_bar, 0, mt * 2 + static_cast<int>(rank),
+                        kb * Cfg::kSfChunks, pol);
+          if (kLoadSfb) tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol_b);
+        }
         tma_load_2d_pair(sa, &p.tm_a, full_leader, kb * Cfg::kBKBytes,
                          mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM, pol);
         if (kLoadB)
@@ -372,7 +390,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
           if (!(issued_mask & (1u << s))) continue;
           const uint32_t par = (issued_parity >> s) & 1u;
           if (leader) mbar_wait_bounded(&full_bar[s], par, p.timeout_ns, &dummy, nullptr, 0);
-          if (kSplitFull || !leader)
+          if ((kSplitFull || !leader) && !kSfCp)
             mbar_wait_bounded(&sf_full[s], par, p.timeout_ns, &dummy, nullptr, 0);
         }
         if (!leader) spin_ns(200000);
@@ -417,8 +435,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
           // sf_ready covers the A/B bytes too: the leader's stagers arrive
           // only after full_bar (split-barrier builds also wait full_bar).
           trace_pair(p, pair == 0, 20, it * nkb + kb);
-          if (!mbar_wait_bounded(&sf_ready[stage], phase, p.timeout_ns, abort_flag, p.status,
-                                 kDevTimeoutMma) ||
+          if (!mbar_wait_bounded(kSfCp ? &full_bar[stage] : &sf_ready[stage], phase, p.timeout_ns,
+                                 abort_flag, p.status, kDevTimeoutMma) ||
               (kSplitFull && !mbar_wait_bounded(&full_bar[stage], phase, p.timeout_ns, abort_flag,
                                                 p.status, kDevTimeoutMma))) {
             ok = false;
@@ -427,6 +445,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
           trace_pair(p, pair == 0, 3, it * nkb + kb);
           tc_fence_after();
           const uint32_t sfb_col = sfa_col + Cfg::kSfaCols;
+          if constexpr (kSfCp) {
+            const uint8_t* ssfa = smem + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
+#pragma unroll
+            for (int c = 0; c < Cfg::kSfChunks; ++c)
+              tmem_cp_pair_32x128b_warpx4(
+                  sfa_col + 4 * c, make_smem_desc(smem_u32(ssfa + c * 512), 0, 128, kSwizzleNone));
+#pragma unroll
+            for (int c = 0; c < 2 * Cfg::kSfChunks; ++c)
+              tmem_cp_pair_32x128b_warpx4(
+                  sfb_col + 4 * c,
+                  make_smem_desc(smem_u32(ssfa + Cfg::kSfaBytes + c * 512), 0, 128, kSwizzleNone));
+          }
           if (!skip_mma) {
 #pragma unroll
             for (int j = 0; j < Cfg::kMmaPerStage; ++j) {
@@ -472,6 +502,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
     }
   } else if (warp >= 6 && warp <= 9) {
     // ---------------------------------------------------------------- scale stagers
+    if constexpr (!kSfCp) {
     const int quad = warp % 4;
     const int stager_kb = total_kb;
     const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
@@ -514,6 +545,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
       trace_pair(p, pair == 0 && warp == 6 && lane == 0, leader ? 2 : 10, g);
       trace_pair(p, pair == 0 && lane == 0, 11 + (warp - 6) + (leader ? 0 : 4), g);
     }
+    }  // !kSfCp
   } else {
     // ---------------------------------------------------------------- epilogue
     const int quad = warp % 4;
