@@ -63,6 +63,13 @@ def _worker(rank, world, port, result_path):
     b_local = (np.ascontiguousarray(bv.reshape(n, k)[lo:hi]).ravel(),
                np.ascontiguousarray(bsf.reshape(n, k // 16)[lo:hi]).ravel())
     c = colpar.colpar_gemm((qa_t, sa_t, ta_t), b_local, n, local_gemm=local_gemm)
+    # The rank-major form of the same gather: shard r in [r, :, :n_r].
+    c_local = local_gemm((qa_t, sa_t, ta_t), b_local)
+    rm = colpar.gather_columns(c_local, n, rank_major=True)
+    assert rm.shape == (world, m, max(colpar.shard_sizes(n, world)))
+    for r in range(world):
+        a, b = colpar.shard_range(n, world, r)
+        assert torch.equal(rm[r, :, : b - a], c[:, a:b])
     if rank == 0:
         np.save(result_path, c.numpy())
     dist.barrier()
