@@ -96,6 +96,17 @@ struct PairCfg {
   static constexpr int kTmemSfStageCols =
       (kDiag & 2048u) ? 16 : (kOneStore ? kSfColsPadded : kSfCols);
   static_assert(kTmemSfBase + kStages * kTmemSfStageCols <= kTmemCols, "TMEM budget");
+  // A/B builds (-DQG_PAIR_SF_PAIRED, two-store formats): SFA of all slots
+  // in one TMEM region and SFB of all slots in another, so the stagers write
+  // two consecutive stages with one SFA and one SFB store.
+#ifdef QG_PAIR_SF_PAIRED
+  static constexpr bool kSfPaired = !kOneStore;
+#else
+  static constexpr bool kSfPaired = false;
+#endif
+  static constexpr int kSfaStep = kSfPaired ? kSfaCols : kTmemSfStageCols;
+  static constexpr int kSfbBase = kTmemSfBase + (kSfPaired ? kStages * kSfaCols : kSfaCols);
+  static constexpr int kSfbStep = kSfPaired ? kSfbCols : kTmemSfStageCols;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   // One MMA issuer with N = 256 MMAs by default: each CTA's tensor core
   // then reads its A tile once per K step.  Two issuers (N = 128 halves,
@@ -422,6 +433,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
       uint32_t phase = 0;
       uint64_t adesc = adesc0, bdesc = bdesc0;
       uint32_t sfa_col = sf0;
+      const uint32_t sfb0 = tmem_base + Cfg::kSfbBase;
+      uint32_t sfb_col = sfb0;
       for (int it = 0; it < my_tiles && ok; ++it) {
         if (!mbar_wait_bounded(&acc_empty[h], (it & 1) ^ 1u, p.timeout_ns, abort_flag, p.status,
                                kDevTimeoutMma)) {
@@ -444,7 +457,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
           }
           trace_pair(p, pair == 0, 3, it * nkb + kb);
           tc_fence_after();
-          const uint32_t sfb_col = sfa_col + Cfg::kSfaCols;
           if constexpr (kSfCp) {
             const uint8_t* ssfa = smem + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
 #pragma unroll
@@ -488,10 +500,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
             adesc = adesc0;
             bdesc = bdesc0;
             sfa_col = sf0;
+            sfb_col = sfb0;
           } else {
             adesc += kStageDesc;
             bdesc += kStageDesc;
-            sfa_col += Cfg::kTmemSfStageCols;
+            sfa_col += Cfg::kSfaStep;
+            sfb_col += Cfg::kSfbStep;
           }
         }
         if (ok) tc_commit_pair(acc_full, 0x3);
@@ -509,6 +523,76 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
     const bool no_wait = (kDiag & 32u) != 0, skip_st = (kDiag & 1u) != 0;
     int stage = 0;
     uint32_t phase = 0;
+    if constexpr (Cfg::kSfPaired) {
+      auto wait_stage = [&](int st, uint32_t ph) {
+        return no_wait || mbar_wait_bounded(!leader ? &sf_full[st] : &full_bar[st], ph,
+                                            p.timeout_ns, abort_flag, p.status, kDevTimeoutMma);
+      };
+      auto arrive = [&](int st) {
+        if (lane != 0) return;
+        if (leader) mbar_arrive(&sf_ready[st]);
+        else mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&sf_ready[st]), 0));
+      };
+      auto scales_of = [&](int st) {
+        return smem + st * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
+      };
+      // Fill SFA / SFB registers of one stage (same layout as stage_scales).
+      auto load_sfa = [&](const uint8_t* ssfa, uint32_t* a) {
+#pragma unroll
+        for (int c = 0; c < Cfg::kSfChunks; ++c) {
+          const uint4 x = lds128(ssfa + c * 512 + lane * 16);
+          a[4 * c] = x.x; a[4 * c + 1] = x.y; a[4 * c + 2] = x.z; a[4 * c + 3] = x.w;
+        }
+      };
+      auto load_sfb = [&](const uint8_t* ssfb, uint32_t* b) {
+#pragma unroll
+        for (int c = 0; c < 2 * Cfg::kSfChunks; ++c) {
+          const uint4 x = lds128(ssfb + c * 512 + lane * 16);
+          b[4 * c] = x.x; b[4 * c + 1] = x.y; b[4 * c + 2] = x.z; b[4 * c + 3] = x.w;
+        }
+      };
+      for (int g = 0; g < stager_kb;) {
+        // Stages in slots (0,1), (2,3), ... are written together; an odd
+        // last slot alone.  The wait on the second stage of a pair delays
+        // the first by one stage, which the stagers' lead over the issuer
+        // (0.5-0.8 us) covers.
+        const bool two = (stage % 2) == 0 && stage + 1 < Cfg::kStages && g + 1 < stager_kb;
+        bool ok = wait_stage(stage, phase);
+        if (two) ok = ok && wait_stage(stage + 1, phase);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        const uint32_t sfa = t_quad + Cfg::kTmemSfBase + stage * Cfg::kSfaStep;
+        const uint32_t sfb = t_quad + Cfg::kSfbBase + stage * Cfg::kSfbStep;
+        if (two) {
+          uint32_t a[2 * Cfg::kSfaCols];
+          load_sfa(scales_of(stage), a);
+          load_sfa(scales_of(stage + 1), a + Cfg::kSfaCols);
+          tmem_st_32x32b<2 * Cfg::kSfaCols>(sfa, a);
+          uint32_t b[2 * Cfg::kSfbCols];
+          load_sfb(scales_of(stage) + Cfg::kSfaBytes, b);
+          load_sfb(scales_of(stage + 1) + Cfg::kSfaBytes, b + Cfg::kSfbCols);
+          tmem_st_32x32b<2 * Cfg::kSfbCols>(sfb, b);
+        } else {
+          uint32_t a[Cfg::kSfaCols];
+          load_sfa(scales_of(stage), a);
+          tmem_st_32x32b<Cfg::kSfaCols>(sfa, a);
+          uint32_t b[Cfg::kSfbCols];
+          load_sfb(scales_of(stage) + Cfg::kSfaBytes, b);
+          tmem_st_32x32b<Cfg::kSfbCols>(sfb, b);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        arrive(stage);
+        if (two) arrive(stage + 1);
+        for (int i = 0; i < (two ? 2 : 1); ++i) {
+          ++g;
+          if (++stage == Cfg::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    } else
     for (int g = 0; g < stager_kb; ++g) {
       if (g > 0 && ++stage == Cfg::kStages) {
         stage = 0;
