@@ -96,17 +96,10 @@ struct PairCfg {
   static constexpr int kTmemSfStageCols =
       (kDiag & 2048u) ? 16 : (kOneStore ? kSfColsPadded : kSfCols);
   static_assert(kTmemSfBase + kStages * kTmemSfStageCols <= kTmemCols, "TMEM budget");
-  // A/B builds (-DQG_PAIR_SF_PAIRED, two-store formats): SFA of all slots
-  // in one TMEM region and SFB of all slots in another, so the stagers write
-  // two consecutive stages with one SFA and one SFB store.
-#ifdef QG_PAIR_SF_PAIRED
-  static constexpr bool kSfPaired = !kOneStore;
-#else
-  static constexpr bool kSfPaired = false;
-#endif
-  static constexpr int kSfaStep = kSfPaired ? kSfaCols : kTmemSfStageCols;
-  static constexpr int kSfbBase = kTmemSfBase + (kSfPaired ? kStages * kSfaCols : kSfaCols);
-  static constexpr int kSfbStep = kSfPaired ? kSfbCols : kTmemSfStageCols;
+  // TMEM column of a slot's SFA and SFB (SFB right after SFA).
+  static constexpr int kSfaStep = kTmemSfStageCols;
+  static constexpr int kSfbBase = kTmemSfBase + kSfaCols;
+  static constexpr int kSfbStep = kTmemSfStageCols;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   // One MMA issuer with N = 256 MMAs by default: each CTA's tensor core
   // then reads its A tile once per K step.  Two issuers (N = 128 halves,
@@ -138,25 +131,6 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
 // into C, 2048 slots per event kind, so a host script can see which wait
 // bounds the pipeline.  Compiled out of shipped builds.
 constexpr bool kTracePair = (kDiag & 512u) != 0;
-
-// The leader's scales complete on the A/B barrier (default), or, with
-// -DQG_PAIR_SPLIT_FULL (A/B builds), on their own barrier with the issuer
-// waiting for both (measured 2% slower at 8192^3: the issuer's extra wait
-// costs more than staging the scales early saves).
-#ifdef QG_PAIR_SPLIT_FULL
-constexpr bool kSplitFull = true;
-#else
-constexpr bool kSplitFull = false;
-#endif
-// A/B builds (-DQG_PAIR_SF_CP): the MMA issuer moves each stage's scales
-// into TMEM with tcgen05.cp (cta_group::2, 32x128b.warpx4, one per 512-byte
-// chunk) ahead of its MMAs instead of the stager warps' tcgen05.st; both
-// CTAs' scale loads then complete on the leader's full barrier.
-#ifdef QG_PAIR_SF_CP
-constexpr bool kSfCp = true;
-#else
-constexpr bool kSfCp = false;
-#endif
 __device__ __forceinline__ void trace_pair(const GemmParams& p, bool on, int kind, int slot) {
   if (kTracePair && on && slot < 2048)
     reinterpret_cast<unsigned long long*>(p.c)[kind * 2048 + slot] = globaltimer_ns();
@@ -361,29 +335,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
         // on sf_ready also tells the issuer that A/B have landed); the
         // peer's scales complete on its own sf_full.  Scales go first: they
         // are small and land early.
-        uint64_t* sf_bar = (kSplitFull || !leader) && !kSfCp ? &sf_full[stage] : &full_bar[stage];
+        uint64_t* sf_bar = leader ? &full_bar[stage] : &sf_full[stage];
         // Diagnostic builds may leave out the B (kDiag bit 7) or the SFB
         // (bit 8) loads to weigh the load path; shipped builds load all.
         constexpr bool kLoadB = (kDiag & 128u) == 0;
         constexpr bool kLoadSfb = (kDiag & 256u) == 0 && Cfg::kSfbBytes > 0;
         constexpr uint32_t kSfTxHere = Cfg::kSfaBytes + (kLoadSfb ? Cfg::kSfbBytes : 0);
         constexpr uint32_t kAbTxHere = Cfg::kABytes + (kLoadB ? Cfg::kBBytes : 0);
-        if (leader)
-          mbar_arrive_expect_tx(&full_bar[stage],
-                                2 * kAbTxHere + (kSfCp ? 2 * kSfTxHere : (kSplitFull ? 0 : kSfTxHere)));
-        if ((kSplitFull || !leader) && !kSfCp) mbar_arrive_expect_tx(&sf_full[stage], kSfTxHere);
-        if (kSfCp) {
-          if (Cfg::kSfaBytes > 0)
-            tma_load_3d_pair(ssfa, &p.tm_sfa, full_leader, 0, mt * 2 + static_cast<int>(rank),
-                             kb * Cfg::kSfChunks, pol);
-          if (kLoadSfb)
-            tma_load_3d_pair(ssfb, &p.tm_sfb, full_leader, 0, nt * 2, kb * Cfg::kSfChunks, pol_b);
-        } else {
-          if (Cfg::kSfaBytes > 0)
-            tma_load_3d(ssfa, &p.tm_sfa, sf_bar, 0, mt * 2 + static_cast<int>(rank),
-                        kb * Cfg::kSfChunks, pol);
-          if (kLoadSfb) tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol_b);
-        }
+        if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * kAbTxHere + kSfTxHere);
+        else mbar_arrive_expect_tx(&sf_full[stage], kSfTxHere);
+        if (Cfg::kSfaBytes > 0)
+          tma_load_3d(ssfa, &p.tm_sfa, sf_bar, 0, mt * 2 + static_cast<int>(rank),
+                      kb * Cfg::kSfChunks, pol);
+        if (kLoadSfb) tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol_b);
         tma_load_2d_pair(sa, &p.tm_a, full_leader, kb * Cfg::kBKBytes,
                          mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM, pol);
         if (kLoadB)
@@ -399,10 +363,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
         uint32_t dummy = 0;
         for (int s = 0; s < Cfg::kStages; ++s) {
           if (!(issued_mask & (1u << s))) continue;
-          const uint32_t par = (issued_parity >> s) & 1u;
-          if (leader) mbar_wait_bounded(&full_bar[s], par, p.timeout_ns, &dummy, nullptr, 0);
-          if ((kSplitFull || !leader) && !kSfCp)
-            mbar_wait_bounded(&sf_full[s], par, p.timeout_ns, &dummy, nullptr, 0);
+          mbar_wait_bounded(leader ? &full_bar[s] : &sf_full[s], (issued_parity >> s) & 1u,
+                            p.timeout_ns, &dummy, nullptr, 0);
         }
         if (!leader) spin_ns(200000);
       }
@@ -446,29 +408,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
         uint32_t acc = 0;
         for (int kb = 0; kb < nkb; ++kb) {
           // sf_ready covers the A/B bytes too: the leader's stagers arrive
-          // only after full_bar (split-barrier builds also wait full_bar).
+          // only after full_bar.
           trace_pair(p, pair == 0, 20, it * nkb + kb);
-          if (!mbar_wait_bounded(kSfCp ? &full_bar[stage] : &sf_ready[stage], phase, p.timeout_ns,
-                                 abort_flag, p.status, kDevTimeoutMma) ||
-              (kSplitFull && !mbar_wait_bounded(&full_bar[stage], phase, p.timeout_ns, abort_flag,
-                                                p.status, kDevTimeoutMma))) {
+          if (!mbar_wait_bounded(&sf_ready[stage], phase, p.timeout_ns, abort_flag, p.status,
+                                 kDevTimeoutMma)) {
             ok = false;
             break;
           }
           trace_pair(p, pair == 0, 3, it * nkb + kb);
           tc_fence_after();
-          if constexpr (kSfCp) {
-            const uint8_t* ssfa = smem + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
-#pragma unroll
-            for (int c = 0; c < Cfg::kSfChunks; ++c)
-              tmem_cp_pair_32x128b_warpx4(
-                  sfa_col + 4 * c, make_smem_desc(smem_u32(ssfa + c * 512), 0, 128, kSwizzleNone));
-#pragma unroll
-            for (int c = 0; c < 2 * Cfg::kSfChunks; ++c)
-              tmem_cp_pair_32x128b_warpx4(
-                  sfb_col + 4 * c,
-                  make_smem_desc(smem_u32(ssfa + Cfg::kSfaBytes + c * 512), 0, 128, kSwizzleNone));
-          }
           if (!skip_mma) {
 #pragma unroll
             for (int j = 0; j < Cfg::kMmaPerStage; ++j) {
@@ -516,83 +464,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
     }
   } else if (warp >= 6 && warp <= 9) {
     // ---------------------------------------------------------------- scale stagers
-    if constexpr (!kSfCp) {
     const int quad = warp % 4;
     const int stager_kb = total_kb;
     const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const bool no_wait = (kDiag & 32u) != 0, skip_st = (kDiag & 1u) != 0;
     int stage = 0;
     uint32_t phase = 0;
-    if constexpr (Cfg::kSfPaired) {
-      auto wait_stage = [&](int st, uint32_t ph) {
-        return no_wait || mbar_wait_bounded(!leader ? &sf_full[st] : &full_bar[st], ph,
-                                            p.timeout_ns, abort_flag, p.status, kDevTimeoutMma);
-      };
-      auto arrive = [&](int st) {
-        if (lane != 0) return;
-        if (leader) mbar_arrive(&sf_ready[st]);
-        else mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&sf_ready[st]), 0));
-      };
-      auto scales_of = [&](int st) {
-        return smem + st * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
-      };
-      // Fill SFA / SFB registers of one stage (same layout as stage_scales).
-      auto load_sfa = [&](const uint8_t* ssfa, uint32_t* a) {
-#pragma unroll
-        for (int c = 0; c < Cfg::kSfChunks; ++c) {
-          const uint4 x = lds128(ssfa + c * 512 + lane * 16);
-          a[4 * c] = x.x; a[4 * c + 1] = x.y; a[4 * c + 2] = x.z; a[4 * c + 3] = x.w;
-        }
-      };
-      auto load_sfb = [&](const uint8_t* ssfb, uint32_t* b) {
-#pragma unroll
-        for (int c = 0; c < 2 * Cfg::kSfChunks; ++c) {
-          const uint4 x = lds128(ssfb + c * 512 + lane * 16);
-          b[4 * c] = x.x; b[4 * c + 1] = x.y; b[4 * c + 2] = x.z; b[4 * c + 3] = x.w;
-        }
-      };
-      for (int g = 0; g < stager_kb;) {
-        // Stages in slots (0,1), (2,3), ... are written together; an odd
-        // last slot alone.  The wait on the second stage of a pair delays
-        // the first by one stage, which the stagers' lead over the issuer
-        // (0.5-0.8 us) covers.
-        const bool two = (stage % 2) == 0 && stage + 1 < Cfg::kStages && g + 1 < stager_kb;
-        bool ok = wait_stage(stage, phase);
-        if (two) ok = ok && wait_stage(stage + 1, phase);
-        if (!__all_sync(0xffffffffu, ok)) break;
-        const uint32_t sfa = t_quad + Cfg::kTmemSfBase + stage * Cfg::kSfaStep;
-        const uint32_t sfb = t_quad + Cfg::kSfbBase + stage * Cfg::kSfbStep;
-        if (two) {
-          uint32_t a[2 * Cfg::kSfaCols];
-          load_sfa(scales_of(stage), a);
-          load_sfa(scales_of(stage + 1), a + Cfg::kSfaCols);
-          tmem_st_32x32b<2 * Cfg::kSfaCols>(sfa, a);
-          uint32_t b[2 * Cfg::kSfbCols];
-          load_sfb(scales_of(stage) + Cfg::kSfaBytes, b);
-          load_sfb(scales_of(stage + 1) + Cfg::kSfaBytes, b + Cfg::kSfbCols);
-          tmem_st_32x32b<2 * Cfg::kSfbCols>(sfb, b);
-        } else {
-          uint32_t a[Cfg::kSfaCols];
-          load_sfa(scales_of(stage), a);
-          tmem_st_32x32b<Cfg::kSfaCols>(sfa, a);
-          uint32_t b[Cfg::kSfbCols];
-          load_sfb(scales_of(stage) + Cfg::kSfaBytes, b);
-          tmem_st_32x32b<Cfg::kSfbCols>(sfb, b);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        arrive(stage);
-        if (two) arrive(stage + 1);
-        for (int i = 0; i < (two ? 2 : 1); ++i) {
-          ++g;
-          if (++stage == Cfg::kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-      }
-    } else
     for (int g = 0; g < stager_kb; ++g) {
       if (g > 0 && ++stage == Cfg::kStages) {
         stage = 0;
@@ -603,9 +480,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
       // barrier (its scales and both CTAs' A/B); peer: its sf_full.  The
       // stage's TMEM slot is free then too (the producer refilled the
       // stage after the MMAs that read both had completed).
-      bool ok = no_wait || mbar_wait_bounded(kSplitFull || !leader ? &sf_full[stage] : &full_bar[stage],
-                                             phase, p.timeout_ns, abort_flag, p.status,
-                                             kDevTimeoutMma);
+      bool ok = no_wait || mbar_wait_bounded(leader ? &full_bar[stage] : &sf_full[stage], phase,
+                                             p.timeout_ns, abort_flag, p.status, kDevTimeoutMma);
       if (!__all_sync(0xffffffffu, ok)) break;
       trace_pair(p, pair == 0 && warp == 6 && lane == 0, leader ? 1 : 9, g);
       const uint8_t* ssfa = smem + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
@@ -629,7 +505,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
       trace_pair(p, pair == 0 && warp == 6 && lane == 0, leader ? 2 : 10, g);
       trace_pair(p, pair == 0 && lane == 0, 11 + (warp - 6) + (leader ? 0 : 4), g);
     }
-    }  // !kSfCp
   } else {
     // ---------------------------------------------------------------- epilogue
     const int quad = warp % 4;
