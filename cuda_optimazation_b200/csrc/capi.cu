@@ -261,8 +261,10 @@ int gemm_prepare(int fmt, const void* a_q, const void* a_sf, const float* a_ts, 
   out->variant = variant;
   out->out_bf16 = c_dtype == QG_DTYPE_BF16;
   if (pair) {
-    const int64_t pairs = num_sms() / 2;
-    out->grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
+    // One CTA pair per tile: the pairs that fit run persistently and take
+    // the rest of the tiles with cluster launch control (gemm_pair.cu).
+    if (2 * tiles > (1ll << 31) - 1) return QG_ERR_SHAPE;
+    out->grid = 2 * static_cast<int>(tiles);
     // bf16 through TMA stores: the eight-warp epilogue (kind 3).
     out->out_kind = rq ? 2 : (out->out_bf16 ? (p.n_out > 0 && kPairEpi8 ? 3 : 1) : 0);
   } else {

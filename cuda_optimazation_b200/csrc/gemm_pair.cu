@@ -6,7 +6,10 @@
 // GEMMquant_sm110/build_and_run.sh:38-75; the disabled 2-SM tc6 kernel,
 // GEMMsm110/include/backends/tc6_nvfp4.cuh:86-332).
 //
-// A cluster of two CTAs (one per SM) owns a 256 x 256 output tile.  Each CTA
+// A cluster of two CTAs (one per SM) owns a 256 x 256 output tile at a time;
+// the grid has one cluster per tile, the clusters that fit run persistently
+// and take the tiles of the clusters not yet started through cluster launch
+// control (clusterlaunchcontrol.try_cancel; see the tile scheduler).  Each CTA
 // loads its own 128 rows of A and its own 128-row half of B; the leader CTA
 // (rank 0) issues tcgen05.mma.cta_group::2, which reads A and B from both
 // CTAs' shared memory and accumulates rows [0,128) in the leader's TMEM and
@@ -223,6 +226,89 @@ constexpr int pair_threads() {
   return kOut >= 2 ? 480 : 352;
 }
 
+// ------------------------------------------------------------------ tile scheduler
+// The grid holds one CTA pair per output tile; the pairs that fit run
+// persistently and take the tiles of pairs not yet started with cluster
+// launch control (clusterlaunchcontrol.try_cancel): the hardware cancels a
+// pending cluster and hands its index to the caller, so the work is spread
+// over whatever SMs are running it, with no static assignment.  The leader's
+// producer thread is the scheduler.  It asks for the next tile while the
+// current tile's loads stream and publishes each tile index (-1: no work
+// left) through a small ring in both CTAs' shared memory: the index word
+// plus a full barrier per slot in each CTA (the peer's written over the
+// cluster's shared-memory window), and one empty barrier per slot in the
+// leader that every consumer (both CTAs' producer / issuer / stager /
+// epilogue warps) arrives on once it has read the index.
+constexpr int kTileRing = 2;
+
+// Consumers of a ring slot: the leader's issuer thread(s), 4 stager warps
+// and the epilogue warps of each CTA, and the peer's producer thread.
+template <int kOut>
+__host__ __device__ constexpr int tile_consumers(int issuers) {
+  return issuers + 1 + 2 * (4 + (kOut >= 2 ? 8 : 4));
+}
+
+struct TileRing {
+  volatile int32_t* ids;  // [kTileRing] this CTA's copy of each slot's tile index
+  uint64_t* full;         // [kTileRing] this CTA
+  uint64_t* empty;        // [kTileRing] leader's
+  bool leader;
+  int slot = 0;
+  uint32_t phase = 0;
+
+  // Consumer: the next tile index (-1 when the work is done, -2 when a wait
+  // timed out).  One thread of the consuming warp calls it.
+  __device__ int next(const GemmParams& p, volatile uint32_t* abort_flag) {
+    // The leader's slots are written locally (release.cta arrive), the
+    // peer's over the cluster window (release.cluster arrive).
+    const bool ok = leader ? mbar_wait_bounded(&full[slot], phase, p.timeout_ns, abort_flag,
+                                               p.status, kDevTimeoutMma)
+                           : mbar_wait_bounded<true>(&full[slot], phase, p.timeout_ns,
+                                                     abort_flag, p.status, kDevTimeoutMma);
+    if (!ok) return -2;
+    // Acquire load, then a relaxed arrive: the arrive that frees the slot
+    // cannot pass the read, and it need not wait for this warp's earlier
+    // writes (a release-scoped arrive would, e.g. for the epilogue's
+    // stores, on the tile boundary's critical path).
+    const int t = ld_acquire_shared_s32(&ids[slot]);
+    if (leader) mbar_arrive_relaxed(&empty[slot]);
+    else mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&empty[slot]), 0));
+    if (++slot == kTileRing) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    return t;
+  }
+  // Warp-wide form: lane 0 takes the index, every lane gets it.
+  __device__ int next_warp(const GemmParams& p, volatile uint32_t* abort_flag, int lane) {
+    int t = 0;
+    if (lane == 0) t = next(p, abort_flag);
+    t = __shfl_sync(0xffffffffu, t, 0);
+    if (lane != 0 && ++slot == kTileRing) {  // keep every lane's cursor in step
+      slot = 0;
+      phase ^= 1u;
+    }
+    return t;
+  }
+  // Scheduler (leader's producer thread): publish `t` into the next slot of
+  // both CTAs once every consumer has read the slot's previous index.
+  __device__ bool publish(const GemmParams& p, volatile uint32_t* abort_flag, int t) {
+    if (!mbar_wait_bounded(&empty[slot], phase ^ 1u, p.timeout_ns, abort_flag, p.status,
+                           kDevTimeoutProducer))
+      return false;
+    ids[slot] = t;
+    st_shared_cluster_u32(mapa_shared(smem_u32(const_cast<int32_t*>(&ids[slot])), 1),
+                          static_cast<uint32_t>(t));
+    mbar_arrive(&full[slot]);
+    mbar_arrive_cluster(mapa_shared(smem_u32(&full[slot]), 1));  // release: the word first
+    if (++slot == kTileRing) {
+      slot = 0;
+      phase ^= 1u;
+    }
+    return true;
+  }
+};
+
 template <int kFmt, int kOut>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>(), 1)
     gemm_pair_kernel(const __grid_constant__ GemmParams p) {
@@ -241,7 +327,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
   uint64_t* acc_full = bars + 4 * Cfg::kStages;     // each CTA
   uint64_t* acc_empty = acc_full + 1;               // leader: [kIssuers], 8 epilogue warps
   uint64_t* drain_bar = acc_full + 3;               // leader: [kIssuers]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 5);
+  uint64_t* tile_full = acc_full + 5;               // each CTA: [kTileRing], the scheduler
+  uint64_t* tile_empty = tile_full + kTileRing;      // leader: [kTileRing], every consumer
+  uint64_t* clc_bar = tile_empty + kTileRing;        // leader: the cancel response
+  uint8_t* clc_resp = reinterpret_cast<uint8_t*>(  // 16 B, 16-byte aligned
+      (reinterpret_cast<uintptr_t>(clc_bar + 1) + 15) & ~static_cast<uintptr_t>(15));
+  volatile int32_t* tile_ids = reinterpret_cast<volatile int32_t*>(clc_resp + 16);  // [kTileRing]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(clc_resp + 16 + 4 * kTileRing);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x / 32;
@@ -261,6 +353,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
     mbar_init(acc_full, Cfg::kIssuers);
     for (int i = 0; i < Cfg::kIssuers; ++i) mbar_init(&acc_empty[i], kOut >= 2 ? 16 : 8);
     for (int i = 0; i < Cfg::kIssuers; ++i) mbar_init(&drain_bar[i], 1);
+    for (int i = 0; i < kTileRing; ++i) {
+      mbar_init(&tile_full[i], 1);
+      mbar_init(&tile_empty[i], tile_consumers<kOut>(Cfg::kIssuers));
+    }
+    mbar_init(clc_bar, 1);
     *abort_flag = 0u;
     fence_barrier_init();
     tma_prefetch_desc(&p.tm_a);
@@ -279,8 +376,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
 
   const int num_tiles = p.num_m_tiles * p.num_n_tiles;
   const int nkb = p.num_k_blocks;
-  const int my_tiles = pair < num_tiles ? (num_tiles - 1 - pair) / npairs + 1 : 0;
-  const int total_kb = my_tiles * nkb;
+  (void)num_tiles;
+  (void)npairs;
+  // Every role of both CTAs takes the cluster's tiles from the tile ring:
+  // the first is the cluster's own index, later ones come from the
+  // leader's producer through cluster launch control (see TileRing).
+  TileRing ring{tile_ids, tile_full, tile_empty, leader};
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA
@@ -296,65 +397,103 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
 #endif
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
-      // Counters stepped incrementally: no division on the per-stage path
-      // (the tile coordinates change once per tile).
-      int stage = 0, kb = 0, tile = pair;
+      bool clc_pending = false;
+      uint32_t clc_phase = 0;
+      int stage = 0, kb = 0, g = 0;
       uint32_t phase = 0;
-      int mt, nt;
-      tile_coords(tile, p.num_m_tiles, p.num_n_tiles, mt, nt);
+      int mt = 0, nt = 0;
       const bool skip_loads = (kDiag & 4u) != 0;
-      for (int g = 0; g < total_kb; ++g) {
-        if (g > 0) {
-          if (++stage == Cfg::kStages) {
+      // The leader's producer schedules: the cluster's own tile first.
+      int tile = leader ? pair : ring.next(p, abort_flag);
+      int next_tile = -1;
+      // The cancelled cluster's tile (its first CTA's index / 2), or -1,
+      // published to every consumer of both CTAs.
+      auto publish_next = [&]() -> bool {
+        if (!mbar_wait_bounded(clc_bar, clc_phase, p.timeout_ns, abort_flag, p.status,
+                               kDevTimeoutProducer))
+          return false;
+        clc_pending = false;
+        clc_phase ^= 1u;
+        const int x = clc_first_ctaid_x(clc_resp);
+        next_tile = x < 0 ? -1 : x / 2;
+        return ring.publish(p, abort_flag, next_tile);
+      };
+      if (leader) ok = ring.publish(p, abort_flag, tile);
+      if (tile < 0) ok = ok && tile == -1;
+      while (ok && tile >= 0) {
+        tile_coords(tile, p.num_m_tiles, p.num_n_tiles, mt, nt);
+        if (leader) {
+          // Ask for the next tile now; the answer is read after this tile's
+          // loads are issued.
+          mbar_arrive_expect_tx(clc_bar, 16);
+          clc_try_cancel(clc_resp, clc_bar);
+          clc_pending = true;
+        }
+        for (kb = 0; kb < nkb; ++kb, ++g) {
+          if (g > 0 && ++stage == Cfg::kStages) {
             stage = 0;
             phase ^= 1u;
           }
-          if (++kb == nkb) {
-            kb = 0;
-            tile += npairs;
-            tile_coords(tile, p.num_m_tiles, p.num_n_tiles, mt, nt);
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.timeout_ns, abort_flag, p.status,
+                                 kDevTimeoutProducer)) {
+            ok = false;
+            break;
           }
+          trace_pair(p, pair == 0, leader ? 0 : 8, g);
+          uint8_t* sa = smem + stage * Cfg::kStageBytes;
+          uint8_t* sb = sa + Cfg::kABytes;
+          uint8_t* ssfa = sb + Cfg::kBBytes;
+          uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
+          if (skip_loads) {
+            mbar_arrive(leader ? &full_bar[stage] : &sf_full[stage]);
+            continue;
+          }
+          const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          // The leader's scales complete on its full barrier with both CTAs'
+          // A/B bytes (its stagers then wait once per stage, and their arrival
+          // on sf_ready also tells the issuer that A/B have landed); the
+          // peer's scales complete on its own sf_full.  Scales go first: they
+          // are small and land early.
+          uint64_t* sf_bar = leader ? &full_bar[stage] : &sf_full[stage];
+          // Diagnostic builds may leave out the B (kDiag bit 7) or the SFB
+          // (bit 8) loads to weigh the load path; shipped builds load all.
+          constexpr bool kLoadB = (kDiag & 128u) == 0;
+          constexpr bool kLoadSfb = (kDiag & 256u) == 0 && Cfg::kSfbBytes > 0;
+          constexpr uint32_t kSfTxHere = Cfg::kSfaBytes + (kLoadSfb ? Cfg::kSfbBytes : 0);
+          constexpr uint32_t kAbTxHere = Cfg::kABytes + (kLoadB ? Cfg::kBBytes : 0);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * kAbTxHere + kSfTxHere);
+          else mbar_arrive_expect_tx(&sf_full[stage], kSfTxHere);
+          if (Cfg::kSfaBytes > 0)
+            tma_load_3d(ssfa, &p.tm_sfa, sf_bar, 0, mt * 2 + static_cast<int>(rank),
+                        kb * Cfg::kSfChunks, pol);
+          if (kLoadSfb) tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol_b);
+          tma_load_2d_pair(sa, &p.tm_a, full_leader, kb * Cfg::kBKBytes,
+                           mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM, pol);
+          if (kLoadB)
+            tma_load_2d_pair(sb, &p.tm_b, full_leader, kb * Cfg::kBKBytes,
+                             nt * Cfg::kBN + static_cast<int>(rank) * Cfg::kBNHalf, pol_b);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
         }
-        if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.timeout_ns, abort_flag, p.status,
-                               kDevTimeoutProducer)) {
-          ok = false;
-          break;
+        if (!ok) break;
+        if (leader) {
+          // The next tile, published once this tile's loads are issued
+          // (publishing it a few stages earlier measured 1-4% slower).
+          if (!publish_next()) {
+            ok = false;
+            break;
+          }
+          tile = next_tile;
+        } else {
+          tile = ring.next(p, abort_flag);
+          if (tile == -2) ok = false;
         }
-        trace_pair(p, pair == 0, leader ? 0 : 8, g);
-        uint8_t* sa = smem + stage * Cfg::kStageBytes;
-        uint8_t* sb = sa + Cfg::kABytes;
-        uint8_t* ssfa = sb + Cfg::kBBytes;
-        uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
-        if (skip_loads) {
-          mbar_arrive(leader ? &full_bar[stage] : &sf_full[stage]);
-          continue;
-        }
-        const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
-        // The leader's scales complete on its full barrier with both CTAs'
-        // A/B bytes (its stagers then wait once per stage, and their arrival
-        // on sf_ready also tells the issuer that A/B have landed); the
-        // peer's scales complete on its own sf_full.  Scales go first: they
-        // are small and land early.
-        uint64_t* sf_bar = leader ? &full_bar[stage] : &sf_full[stage];
-        // Diagnostic builds may leave out the B (kDiag bit 7) or the SFB
-        // (bit 8) loads to weigh the load path; shipped builds load all.
-        constexpr bool kLoadB = (kDiag & 128u) == 0;
-        constexpr bool kLoadSfb = (kDiag & 256u) == 0 && Cfg::kSfbBytes > 0;
-        constexpr uint32_t kSfTxHere = Cfg::kSfaBytes + (kLoadSfb ? Cfg::kSfbBytes : 0);
-        constexpr uint32_t kAbTxHere = Cfg::kABytes + (kLoadB ? Cfg::kBBytes : 0);
-        if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * kAbTxHere + kSfTxHere);
-        else mbar_arrive_expect_tx(&sf_full[stage], kSfTxHere);
-        if (Cfg::kSfaBytes > 0)
-          tma_load_3d(ssfa, &p.tm_sfa, sf_bar, 0, mt * 2 + static_cast<int>(rank),
-                      kb * Cfg::kSfChunks, pol);
-        if (kLoadSfb) tma_load_3d(ssfb, &p.tm_sfb, sf_bar, 0, nt * 2, kb * Cfg::kSfChunks, pol_b);
-        tma_load_2d_pair(sa, &p.tm_a, full_leader, kb * Cfg::kBKBytes,
-                         mt * 2 * Cfg::kBM + static_cast<int>(rank) * Cfg::kBM, pol);
-        if (kLoadB)
-          tma_load_2d_pair(sb, &p.tm_b, full_leader, kb * Cfg::kBKBytes,
-                           nt * Cfg::kBN + static_cast<int>(rank) * Cfg::kBNHalf, pol_b);
-        issued_mask |= 1u << stage;
-        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+      }
+      if (clc_pending) {
+        // A cancel request still in flight writes this CTA's shared memory:
+        // let it land before the CTA exits.
+        uint32_t dummy = 0;
+        mbar_wait_bounded(clc_bar, clc_phase, p.timeout_ns, &dummy, nullptr, 0);
       }
       if (!ok) {
         // Drain: every issued stage's copies land before the CTA retires its
@@ -397,7 +536,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
       uint32_t sfa_col = sf0;
       const uint32_t sfb0 = tmem_base + Cfg::kSfbBase;
       uint32_t sfb_col = sfb0;
-      for (int it = 0; it < my_tiles && ok; ++it) {
+      for (int it = 0; ok; ++it) {
+        const int tile = ring.next(p, abort_flag);
+        if (tile < 0) {
+          ok = tile == -1;
+          break;
+        }
         if (!mbar_wait_bounded(&acc_empty[h], (it & 1) ^ 1u, p.timeout_ns, abort_flag, p.status,
                                kDevTimeoutMma)) {
           ok = false;
@@ -465,45 +609,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
   } else if (warp >= 6 && warp <= 9) {
     // ---------------------------------------------------------------- scale stagers
     const int quad = warp % 4;
-    const int stager_kb = total_kb;
     const uint32_t t_quad = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const bool no_wait = (kDiag & 32u) != 0, skip_st = (kDiag & 1u) != 0;
     int stage = 0;
     uint32_t phase = 0;
-    for (int g = 0; g < stager_kb; ++g) {
-      if (g > 0 && ++stage == Cfg::kStages) {
-        stage = 0;
-        phase ^= 1u;
+    bool run = true;
+    for (int g = 0; run;) {
+      const int tile = ring.next_warp(p, abort_flag, lane);
+      if (tile < 0) break;
+      for (int kb = 0; kb < nkb; ++kb, ++g) {
+        if (g > 0 && ++stage == Cfg::kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+        // Every lane polls (and so acquires) the stage barrier itself: one
+        // wait per stage on the stager's serial path.  Leader: the full
+        // barrier (its scales and both CTAs' A/B); peer: its sf_full.  The
+        // stage's TMEM slot is free then too (the producer refilled the
+        // stage after the MMAs that read both had completed).
+        bool ok = no_wait || mbar_wait_bounded(leader ? &full_bar[stage] : &sf_full[stage], phase,
+                                               p.timeout_ns, abort_flag, p.status, kDevTimeoutMma);
+        if (!__all_sync(0xffffffffu, ok)) {
+          run = false;
+          break;
+        }
+        trace_pair(p, pair == 0 && warp == 6 && lane == 0, leader ? 1 : 9, g);
+        const uint8_t* ssfa = smem + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
+        const uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
+        const uint32_t sfa_col = Cfg::kTmemSfBase + stage * Cfg::kTmemSfStageCols;
+        if (!skip_st) {
+          stage_scales<kFmt>(ssfa, ssfb, t_quad + sfa_col, lane);
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (leader) {
+          if (lane == 0) mbar_arrive(&sf_ready[stage]);
+        } else if (lane == 0) {
+          // A release-scoped arrive at cluster scope costs ~1 us here and
+          // serialises the stagers (measured: 2.2 vs 4.1 PF/s).  The relaxed
+          // arrive is enough: tcgen05.wait::st has already completed the TMEM
+          // writes and tcgen05.fence::before_thread_sync orders them before it.
+          mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&sf_ready[stage]), 0));
+        }
+        trace_pair(p, pair == 0 && warp == 6 && lane == 0, leader ? 2 : 10, g);
+        trace_pair(p, pair == 0 && lane == 0, 11 + (warp - 6) + (leader ? 0 : 4), g);
       }
-      // Every lane polls (and so acquires) the stage barrier itself: one
-      // wait per stage on the stager's serial path.  Leader: the full
-      // barrier (its scales and both CTAs' A/B); peer: its sf_full.  The
-      // stage's TMEM slot is free then too (the producer refilled the
-      // stage after the MMAs that read both had completed).
-      bool ok = no_wait || mbar_wait_bounded(leader ? &full_bar[stage] : &sf_full[stage], phase,
-                                             p.timeout_ns, abort_flag, p.status, kDevTimeoutMma);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      trace_pair(p, pair == 0 && warp == 6 && lane == 0, leader ? 1 : 9, g);
-      const uint8_t* ssfa = smem + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
-      const uint8_t* ssfb = ssfa + Cfg::kSfaBytes;
-      const uint32_t sfa_col = Cfg::kTmemSfBase + stage * Cfg::kTmemSfStageCols;
-      if (!skip_st) {
-        stage_scales<kFmt>(ssfa, ssfb, t_quad + sfa_col, lane);
-        tmem_wait_st();
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (leader) {
-        if (lane == 0) mbar_arrive(&sf_ready[stage]);
-      } else if (lane == 0) {
-        // A release-scoped arrive at cluster scope costs ~1 us here and
-        // serialises the stagers (measured: 2.2 vs 4.1 PF/s).  The relaxed
-        // arrive is enough: tcgen05.wait::st has already completed the TMEM
-        // writes and tcgen05.fence::before_thread_sync orders them before it.
-        mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&sf_ready[stage]), 0));
-      }
-      trace_pair(p, pair == 0 && warp == 6 && lane == 0, leader ? 2 : 10, g);
-      trace_pair(p, pair == 0 && lane == 0, 11 + (warp - 6) + (leader ? 0 : 4), g);
     }
   } else {
     // ---------------------------------------------------------------- epilogue
@@ -526,8 +677,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_threads<kOut>()
     // quantizer forms it) and the running amax of this lane's outputs.
     float rq_inv_ts = 1.0f, rq_max = 0.0f;
     if constexpr (kOut == 2) rq_inv_ts = __fdiv_rn(1.0f, p.rq_ts ? *p.rq_ts : 1.0f);
-    for (int it = 0; it < my_tiles; ++it) {
-      const int tile = pair + it * npairs;
+    for (int it = 0;; ++it) {
+      const int tile = ring.next_warp(p, abort_flag, lane);
+      if (tile < 0) break;
       int mt, nt;
       tile_coords(tile, p.num_m_tiles, p.num_n_tiles, mt, nt);
       bool ok = true;

@@ -563,3 +563,57 @@ __device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_add
                : "memory");
 }
 }  // namespace qg
+
+namespace qg {
+// ------------------------------------------------------------------ cluster launch control
+// Ask the hardware to cancel the launch of a cluster of this grid that has
+// not started yet; the 16-byte response lands at `resp` (this CTA's shared
+// memory, 16-byte aligned) and completes 16 bytes on the mbarrier `bar`
+// (armed by the caller with expect_tx).  The plain form: the response goes
+// to this CTA only.
+__device__ __forceinline__ void clc_try_cancel(void* resp, uint64_t* bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], "
+      "[%1];" ::"r"(smem_u32(resp)),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+// Decode a response: returns the x index of the first CTA of the cancelled
+// cluster, or -1 when nothing was cancelled (no cluster left to take).
+__device__ __forceinline__ int clc_first_ctaid_x(const void* resp) {
+  uint32_t ok, x;
+  asm volatile(
+      "{\n\t.reg .b128 r;\n\t.reg .pred p;\n\t"
+      "ld.shared.b128 r, [%2];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r;\n\t}"
+      : "=r"(ok), "=r"(x)
+      : "r"(smem_u32(resp))
+      : "memory");
+  return ok ? static_cast<int>(x) : -1;
+}
+// Store a 32-bit word into the shared memory of another CTA of the cluster
+// (shared::cluster address from mapa_shared).
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+}  // namespace qg
+
+namespace qg {
+// Acquire load of a shared-memory word: later memory operations of this
+// thread (an arrive that releases the word's slot) stay after it.
+__device__ __forceinline__ int ld_acquire_shared_s32(const volatile int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.s32 %0, [%1];"
+               : "=r"(v)
+               : "r"(smem_u32(const_cast<const int32_t*>(p)))
+               : "memory");
+  return v;
+}
+// Relaxed arrive on this CTA's mbarrier (no release of prior writes).
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+}  // namespace qg
