@@ -375,8 +375,17 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
   bool quant_ok = true;
   if (warp >= 2) {
     const int qt = threadIdx.x - 64;
-    quant_ok = p.x_bf16 ? quantize_phase<true>(p, qt, qred, abort_flag, x_loaded, x_ready)
-                        : quantize_phase<false>(p, qt, qred, abort_flag, x_loaded, x_ready);
+    if (kDiag & 4096u) {
+      // Diagnostic: the activations taken as already quantised (results
+      // wrong by design), to weigh the in-kernel quantisation's cost.
+      if (qt == 0) {
+        mbar_arrive(x_loaded);
+        mbar_arrive(x_ready);
+      }
+    } else {
+      quant_ok = p.x_bf16 ? quantize_phase<true>(p, qt, qred, abort_flag, x_loaded, x_ready)
+                          : quantize_phase<false>(p, qt, qred, abort_flag, x_loaded, x_ready);
+    }
   }
 
   if (warp == 0) {

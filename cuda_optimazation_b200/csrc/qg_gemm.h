@@ -12,12 +12,15 @@ constexpr int kMaxDevices = 64;
 
 // Diagnostic switches, fixed when the library is compiled (-DQG_DIAG_FLAGS=...
 // through QG_EXTRA_NVCC); shipped builds have none and the branches vanish.
-// Results are wrong by design when bits 0-3 are set: bit 0 skips the scale
-// staging, bit 1 the MMAs, bit 2 the TMA loads (pair / solo kernels), bit 3
-// the epilogue stores, bit 7 the pair kernel's B loads, bit 8 its SFB loads;
-// bit 6 makes the decode GEMM's CTA (kDiag >> 16) write
-// %globaltimer stamps of its roles into an unused partial slice.  Used to
-// attribute kernel time to its parts.
+// Results are wrong by design when any of bits 0-3, 7, 8, 11, 12 is set:
+// bit 0 skips the scale staging, bit 1 the MMAs, bit 2 the TMA loads (pair /
+// solo kernels), bit 3 the epilogue stores, bit 7 the pair kernel's B loads,
+// bit 8 its SFB loads, bit 11 all its scale loads and their shared memory,
+// bit 12 the decode GEMM's activation quantisation (activations taken as
+// already quantised).  Bit 6 makes the decode GEMM's CTA (kDiag >> 16) and
+// bit 9 the pair kernel's first pair write %globaltimer stamps of their
+// roles (into an unused partial slice, resp. into C).  Used to attribute
+// kernel time to its parts.
 #ifndef QG_DIAG_FLAGS
 #define QG_DIAG_FLAGS 0u
 #endif
