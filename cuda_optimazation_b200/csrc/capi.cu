@@ -523,13 +523,12 @@ int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void
 
 // Workspace of qg_gemm_nvfp4_skinny, each part 256-byte aligned: the
 // per-CTA partial tiles [max_ctas][2][m][128] fp32, the tile counters
-// [tiles][4], the quantised activations (values, scales), the tensor scale,
-// the quantiser's per-CTA amax slots and its grid arrival counters.  The
-// counters must be zero before the first call (zero-filled workspace); every
-// call that completes leaves them zero.
+// [tiles][4] (zeroed by the quantiser kernel of every call), the quantised
+// activations (values, scales), the tensor scale and the quantiser's per-CTA
+// amax slots.
 static int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 struct SkinnyWs {
-  int64_t part, cnt, xq, xsf, xts, amax, sync, total;
+  int64_t part, cnt, xq, xsf, xts, amax, total;
 };
 static SkinnyWs skinny_ws_layout(int64_t m, int64_t n, int64_t k) {
   SkinnyWs w;
@@ -539,8 +538,7 @@ static SkinnyWs skinny_ws_layout(int64_t m, int64_t n, int64_t k) {
   w.xsf = w.xq + align256(m * k / 2);
   w.xts = w.xsf + align256(qg_scale_bytes(m, k, 16));
   w.amax = w.xts + 256;
-  w.sync = w.amax + align256(skinny_max_ctas() * 4);
-  w.total = w.sync + 256;
+  w.total = w.amax + align256(skinny_max_ctas() * 4);
   return w;
 }
 size_t qg_gemm_nvfp4_skinny_workspace_bytes(int64_t m, int64_t n, int64_t k) {
@@ -588,7 +586,6 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   p.xsf = xsf;
   p.x_ts = xts;
   p.amax_part = reinterpret_cast<float*>(base + wl.amax);
-  p.sync = reinterpret_cast<uint32_t*>(base + wl.sync);
   p.w_ts = w_ts;
   p.out_bf16 = c_dtype == QG_DTYPE_BF16 ? 1 : 0;
   p.vec_ok = (reinterpret_cast<uintptr_t>(c) % 16 == 0) &&
@@ -600,9 +597,14 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   p.num_k_blocks = static_cast<int>((row_bytes + 255) / 256);  // 512 of K per stage
   p.status = status;
   p.timeout_ns = default_timeout_ns();
+  // Activation quantiser (two small kernels), then the GEMM, which starts
+  // streaming weights while they run (programmatic dependent launch).
+  const int64_t xblocks = m * (k / 16);
   const int64_t units = static_cast<int64_t>(p.num_tiles) * p.num_k_blocks;
   int64_t grid = units < num_sms() ? units : num_sms();
   if (grid > skinny_max_ctas()) grid = skinny_max_ctas();
+  if (launch_skinny_quant(p, skinny_quant_grid(xblocks, num_sms()), s) != cudaSuccess)
+    return QG_ERR_CUDA;
   if (launch_gemm_skinny(p, static_cast<int>(grid), s) != cudaSuccess) return QG_ERR_CUDA;
   return QG_OK;
 }

@@ -12,15 +12,15 @@ constexpr int kMaxDevices = 64;
 
 // Diagnostic switches, fixed when the library is compiled (-DQG_DIAG_FLAGS=...
 // through QG_EXTRA_NVCC); shipped builds have none and the branches vanish.
-// Results are wrong by design when any of bits 0-3, 7, 8, 11, 12 is set:
+// Results are wrong by design when any of bits 0-3, 7, 8, 11 is set:
 // bit 0 skips the scale staging, bit 1 the MMAs, bit 2 the TMA loads (pair /
 // solo kernels), bit 3 the epilogue stores, bit 7 the pair kernel's B loads,
-// bit 8 its SFB loads, bit 11 all its scale loads and their shared memory,
-// bit 12 the decode GEMM's activation quantisation (activations taken as
-// already quantised).  Bit 6 makes the decode GEMM's CTA (kDiag >> 16) and
-// bit 9 the pair kernel's first pair write %globaltimer stamps of their
-// roles (into an unused partial slice, resp. into C).  Used to attribute
-// kernel time to its parts.
+// bit 8 its SFB loads, bit 11 all its scale loads and their shared memory.
+// Bit 6 makes the decode GEMM's CTA (kDiag >> 16) and its quantiser kernels
+// write %globaltimer stamps of their roles, and every decode GEMM CTA its
+// start, end and epilogue milestones (into an unused partial slice); bit 9
+// makes the pair kernel's first pair stamp its roles into C.  Used to
+// attribute kernel time to its parts.
 #ifndef QG_DIAG_FLAGS
 #define QG_DIAG_FLAGS 0u
 #endif
@@ -61,11 +61,12 @@ struct GemmParams {
 
 // Decode-shaped NVFP4 GEMM (gemm_skinny.cu): weights W [n][k] on the MMA's M
 // side, activations X [m][k] (m <= 128) on its N side, stream-K over
-// (weight tile, K block) units.  The activation quantisation runs inside the
-// same (cooperative) grid, on the warps that are idle while the first weight
-// stages stream in.  A tile split between CTAs is summed by the last
-// contributor to finish it (per-tile counters), in a fixed order, from
-// per-CTA partial slices; whole tiles are written straight to C.
+// (weight tile, K block) units.  The activations are quantised by two small
+// kernels launched ahead of it (launch_skinny_quant) with programmatic
+// dependent launch, so the GEMM streams weights meanwhile.  A tile split
+// between CTAs is summed by the last contributor to finish it (per-tile
+// counters), in a fixed order, from per-CTA partial slices; whole tiles are
+// written straight to C.
 struct SkinnyParams {
   CUtensorMap tm_w;    // uint8 [n][k/2], box 128 B x 128 rows, SWIZZLE_128B
   CUtensorMap tm_x;    // uint8 [m][k/2] (the quantised xq), box 128 B x mma_n rows
@@ -76,10 +77,9 @@ struct SkinnyParams {
   uint8_t* xq;         // quantised activations [m][k/2]
   uint8_t* xsf;        // their scales, MMA layout
   float* x_ts;         // their tensor scale
-  float* amax_part;    // [grid] per-CTA amax
-  uint32_t* sync;      // [3] grid arrival counters, zero between calls
+  float* amax_part;    // [quantiser grid] per-CTA amax
   float* part;         // [grid][2][m][128] fp32 partial tiles
-  uint32_t* cnt;       // [num_tiles][4] tile arrival counters, zero between calls
+  uint32_t* cnt;       // [num_tiles][4] tile arrival counters, zeroed by the quantiser
   void* c;
   int64_t ldc;
   const float* w_ts;   // weight tensor scale (may be null)
@@ -91,6 +91,8 @@ struct SkinnyParams {
   uint64_t timeout_ns;
 };
 cudaError_t launch_gemm_skinny(const SkinnyParams& p, int grid, cudaStream_t stream);
+int skinny_quant_grid(int64_t xblocks, int sms);
+cudaError_t launch_skinny_quant(const SkinnyParams& p, int grid, cudaStream_t stream);
 int skinny_max_ctas();
 int skinny_mma_n(int64_t m);
 

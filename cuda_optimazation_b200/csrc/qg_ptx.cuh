@@ -617,3 +617,16 @@ __device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
                : "memory");
 }
 }  // namespace qg
+
+namespace qg {
+// Programmatic dependent launch: let the next kernel of the stream (launched
+// with programmatic stream serialization) start now, resp. wait until the
+// kernels this one depends on have completed and their writes are visible.
+// Both are no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+}  // namespace qg

@@ -383,8 +383,9 @@ class GemmPlan:
 
 
 def skinny_workspace(m: int, n: int, k: int, device) -> torch.Tensor:
-    """A zero-filled workspace for gemm_nvfp4_skinny (reusable across calls
-    on one stream: every completed call leaves its counters zero)."""
+    """A workspace for gemm_nvfp4_skinny (reusable across calls on one
+    stream; every call rewrites the state it reads, so no zero fill is
+    needed -- it is zero-filled here only to make it deterministic)."""
     need = int(lib().qg_gemm_nvfp4_skinny_workspace_bytes(m, n, k))
     return torch.zeros(need, dtype=torch.uint8, device=device)
 

@@ -243,12 +243,14 @@ int qg_plan_destroy(qg_plan plan);
  * qg_quantize_nvfp4 would, then C[m, n] = (ts_x * w_ts) * x_q . w_q^T with the
  * pre-quantised weights w_q (n x k, MMA layout, scales in sf_layout).  The
  * weights are streamed once at HBM rate (stream-K over 128-row weight tiles
- * on every SM), in ONE cooperative launch that also quantises x.
- * `workspace` (device, qg_gemm_nvfp4_skinny_workspace_bytes) holds the
- * partial tiles, the quantised activations and grid arrival counters: it
- * must be zero-filled before its first use and is left ready for the next
- * call (re-zero it after a call that returned a device timeout).  One
- * workspace serves one stream at a time.  K % 32 == 0.  The result is
+ * on every SM).  Three launches on `stream`: an amax pass over x, the
+ * quantiser, and the GEMM, the last two with programmatic dependent launch so
+ * the GEMM streams weights while x is quantised.  `workspace` (device,
+ * qg_gemm_nvfp4_skinny_workspace_bytes) holds the partial tiles, the
+ * quantised activations and the tile counters; it needs no initialisation
+ * (every call rewrites what it reads, counters and scale padding included,
+ * also after a call that returned a device timeout).  One workspace serves
+ * one stream at a time.  K % 32 == 0.  The result is
  * deterministic (split tiles are summed in a fixed order).
  * No reference counterpart kernel: the reference harness runs square
  * problems only (GEMMquant_sm110/src/quant_gemm_bench.cu:3038-3079); this is

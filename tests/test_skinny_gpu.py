@@ -83,9 +83,9 @@ def test_skinny_fp32_activations(qlib, oracle):
 
 
 def test_skinny_workspace_reuse_and_determinism(qlib, oracle):
-    """One workspace across calls with different activations: the grid and
-    tile counters reset themselves, and split tiles are summed in a fixed
-    order, so a repeated call is bit-identical."""
+    """One workspace across calls with different activations: the tile
+    counters are re-zeroed by every call's quantiser, and split tiles are
+    summed in a fixed order, so a repeated call is bit-identical."""
     m, n, k = 16, 28672, 2048
     xw = oracle.normal(n * k, 9, 0.0, 0.02).reshape(n, k)
     W = qlib.make_nvfp4(torch.from_numpy(xw).cuda())
@@ -98,7 +98,7 @@ def test_skinny_workspace_reuse_and_determinism(qlib, oracle):
     assert rc == qlib.OK, code
     assert torch.equal(outs[0], outs[2]) and torch.equal(outs[1], outs[3])
     assert not torch.equal(outs[0], outs[1])
-    # Counters are left zero (the trailing grid-arrival words included).
+    # A fresh workspace gives the same bits.
     fresh = qlib.gemm_nvfp4_skinny(xs[0], W, torch.float32)
     assert torch.equal(fresh, outs[0])
 
