@@ -532,9 +532,10 @@ struct SkinnyWs {
 };
 static SkinnyWs skinny_ws_layout(int64_t m, int64_t n, int64_t k) {
   SkinnyWs w;
+  const int64_t slices = 2 * skinny_shape(m).halves;
   w.part = 0;
-  w.cnt = w.part + align256(static_cast<int64_t>(skinny_max_ctas()) * 2 * m * 128 * 4);
-  w.xq = w.cnt + align256((n + 127) / 128 * 4 * 4);
+  w.cnt = w.part + align256(static_cast<int64_t>(skinny_max_ctas()) * slices * m * 128 * 4);
+  w.xq = w.cnt + align256((n + 255) / 256 * 2 * 4 * 4);  // 4 counters per 128 rows
   w.xsf = w.xq + align256(m * k / 2);
   w.xts = w.xsf + align256(qg_scale_bytes(m, k, 16));
   w.amax = w.xts + 256;
@@ -569,13 +570,15 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   uint8_t* xsf = base + wl.xsf;
   float* xts = reinterpret_cast<float*>(base + wl.xts);
   const int mma_n = skinny_mma_n(m);
+  const SkinnyShape sh = skinny_shape(m);
   SkinnyParams p;
   std::memset(&p, 0, sizeof(p));
   const int64_t row_bytes = k / 2;
   if (!make_operand_map(&p.tm_w, w_q, n, row_bytes, 128)) return QG_ERR_CUDA;
   if (!make_operand_map(&p.tm_x, xq, m, row_bytes, mma_n)) return QG_ERR_CUDA;
-  if (!make_scale_map(&p.tm_sfw, w_sf, n, k, 16, sf_layout, 1, 8)) return QG_ERR_CUDA;
-  if (!make_scale_map(&p.tm_sfx, xsf, m, k, 16, QG_LAYOUT_MMA, 1, 8)) return QG_ERR_CUDA;
+  if (!make_scale_map(&p.tm_sfw, w_sf, n, k, 16, sf_layout, 1, sh.sf_chunks)) return QG_ERR_CUDA;
+  if (!make_scale_map(&p.tm_sfx, xsf, m, k, 16, QG_LAYOUT_MMA, 1, sh.sf_chunks))
+    return QG_ERR_CUDA;
   p.part = reinterpret_cast<float*>(base + wl.part);
   p.cnt = cnt;
   p.c = c;
@@ -593,8 +596,10 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
-  p.num_tiles = static_cast<int>((n + 127) / 128);
-  p.num_k_blocks = static_cast<int>((row_bytes + 255) / 256);  // 512 of K per stage
+  p.num_tiles = static_cast<int>((n + sh.tile_rows - 1) / sh.tile_rows);
+  p.num_k_blocks = static_cast<int>((row_bytes + sh.stage_k_bytes - 1) / sh.stage_k_bytes);
+  p.slices = 2 * sh.halves;
+  p.num_counters = p.num_tiles * sh.halves * 4;
   p.status = status;
   p.timeout_ns = default_timeout_ns();
   // Activation quantiser (two small kernels), then the GEMM, which starts
@@ -602,6 +607,12 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   const int64_t xblocks = m * (k / 16);
   const int64_t units = static_cast<int64_t>(p.num_tiles) * p.num_k_blocks;
   int64_t grid = units < num_sms() ? units : num_sms();
+  // 256-row tiles that nearly fill the SMs (n = 28672: 112 tiles on 148):
+  // one whole tile per CTA.  Stream-K over all SMs would leave every tile
+  // split and every CTA's last segment a sum of partials after the weight
+  // stream (measured 2.5 TB/s against 4.1 at m = 128).
+  if (sh.halves == 2 && p.num_tiles <= num_sms() && 4 * p.num_tiles >= 3 * num_sms())
+    grid = p.num_tiles;
   if (grid > skinny_max_ctas()) grid = skinny_max_ctas();
   if (launch_skinny_quant(p, skinny_quant_grid(xblocks, num_sms()), s) != cudaSuccess)
     return QG_ERR_CUDA;

@@ -32,6 +32,9 @@
 
 namespace qg {
 
+#ifndef QG_SKINNY_WIDE
+#define QG_SKINNY_WIDE 1
+#endif
 #ifndef QG_SQ_THREADS
 #define QG_SQ_THREADS 256
 #endif
@@ -42,26 +45,40 @@ namespace qg {
 // Upper bound of the GEMM grid; sizes the partial-tile workspace.
 constexpr int kSkinnyMaxCtas = 256;
 
+// Tile shape by MMA N.  N <= 64: a tile is 128 weight rows, a stage 512 of
+// K, two accumulator buffers (the next segment's MMAs overlap the epilogue).
+// N = 128 ("wide"): a tile is 256 weight rows as two 128-row MMA halves
+// that share the stage's activations, a stage 256 of K, one accumulator
+// buffer of both halves.  The activation bytes per weight byte halve (16 KB
+// per 32 KB of weights instead of 32 KB), so four stages fit in shared
+// memory instead of three and more weight bytes are in flight per SM.
 template <int kN>
 struct SkinnyCfg {
-  static constexpr int kBM = 128;        // weight rows per tile
+  static constexpr int kH = (QG_SKINNY_WIDE && kN == 128) ? 2 : 1;  // 128-row halves per tile
+  static constexpr int kBM = 128;        // weight rows per MMA (half)
+  static constexpr int kTileRows = kBM * kH;
   static constexpr int kBoxBytes = 128;  // one SWIZZLE_128B box: 256 fp4 of K
-  static constexpr int kBoxes = 2;       // boxes per stage: 512 of K
+  static constexpr int kBoxes = kH == 1 ? 2 : 1;  // boxes per stage: 512 / 256 of K
   static constexpr int kBKBytes = kBoxes * kBoxBytes;
   // A stage carries 8 MMAs: the serial per-stage cost of the issue loops
   // (barrier waits, commit) is paid once per 32 KB of weights.
-  static constexpr int kMmaPerStage = 4 * kBoxes;
   static constexpr int kSfChunks = 4 * kBoxes;  // 512-byte chunks, 64 of K each
+  static constexpr int kMmaPerStage = kSfChunks * kH;
   static constexpr int kWBox = kBM * kBoxBytes;
   static constexpr int kXBox = kN * kBoxBytes;
-  static constexpr int kWBytes = kWBox * kBoxes;
+  static constexpr int kWBytes = kWBox * kBoxes * kH;  // [box][half] boxes
   static constexpr int kXBytes = kXBox * kBoxes;
-  static constexpr int kSfwBytes = kSfChunks * 512;
+  static constexpr int kSfwBytes = kSfChunks * 512 * kH;  // [half][chunk]
   static constexpr int kSfxBytes = kSfChunks * 512;
   static constexpr int kStageTx = kWBytes + kXBytes + kSfwBytes + kSfxBytes;
   static constexpr int kStageBytes = (kStageTx + 1023) / 1024 * 1024;
-  static constexpr int kSfStageCols = 8 * kSfChunks;  // 4 weight + 4 activation per chunk
-  static constexpr int kTmemSfBase = 2 * kN < 64 ? 64 : 2 * kN;
+  // A stage's scale slot: weight scales of each half, then the activation
+  // scales (4 columns per chunk each), padded to a tcgen05.st width.
+  static constexpr int kSfWords = 4 * kSfChunks * (kH + 1);
+  static constexpr int kSfStageCols = kSfWords <= 32 ? 32 : kSfWords <= 64 ? 64 : 128;
+  static constexpr int kAccBufs = kH == 1 ? 2 : 1;
+  static constexpr int kAccCols = kAccBufs * kH * kN;
+  static constexpr int kTmemSfBase = kAccCols < 64 ? 64 : kAccCols;
   static constexpr int kTmemCols = 512;
   static constexpr int kSmemStages = (232448 - 512 - 1024) / kStageBytes;
   static constexpr int kTmemStages = (kTmemCols - kTmemSfBase) / kSfStageCols;
@@ -69,7 +86,7 @@ struct SkinnyCfg {
   static constexpr int kStages = kStages0 < 8 ? kStages0 : 8;
   static constexpr int kSmemBytes = kStages * kStageBytes + 512 + 1024;
   static_assert(kStages >= 2, "pipeline depth");
-  static_assert(2 * kN <= kTmemSfBase, "accumulators");
+  static_assert(kAccCols <= kTmemSfBase, "accumulators");
   static_assert(kTmemSfBase + kStages * kSfStageCols <= kTmemCols, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static constexpr int kThreads = 320;
@@ -172,11 +189,11 @@ struct SegCursor {
 // slot `i` of the last (never used by a launched CTA) partial slice pair.
 __device__ __forceinline__ void trace_cta(const SkinnyParams& p, int i) {
   if (kDiag & 64u)
-    reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * 2 * p.m * 128)[i] = globaltimer_ns();
+    reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * p.slices * p.m * 128)[i] = globaltimer_ns();
 }
 __device__ __forceinline__ void trace(const SkinnyParams& p, int i) {
   if ((kDiag & 64u) && blockIdx.x == (kDiag >> 16) && i < 512)
-    reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * 2 * p.m * 128)[i] = globaltimer_ns();
+    reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * p.slices * p.m * 128)[i] = globaltimer_ns();
 }
 
 // ------------------------------------------------------------------ activation quantiser
@@ -211,7 +228,7 @@ __global__ void __launch_bounds__(kSqThreads) skinny_amax_kernel(const __grid_co
   griddep_launch_dependents();
   if (kDiag & 64u) {
     if (threadIdx.x == 0 && blockIdx.x == (kDiag >> 16)) {
-      auto* tr = reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * 2 * p.m * 128);
+      auto* tr = reinterpret_cast<unsigned long long*>(p.part + static_cast<int64_t>(kSkinnyMaxCtas - 1) * p.slices * p.m * 128);
       tr[506] = tr[1];  // the previous call's GEMM end
     }
     if (threadIdx.x == 0) trace(p, 500);
@@ -344,7 +361,7 @@ __global__ void __launch_bounds__(kSqThreads)
       if (row >= p.m || sc >= sfk) p.xsf[mma_scale_offset(row, sc, 1, sf_blocks, 1)] = 0u;
     }
   }
-  for (int64_t i = gt; i < static_cast<int64_t>(p.num_tiles) * 4; i += gstride) p.cnt[i] = 0u;
+  for (int64_t i = gt; i < static_cast<int64_t>(p.num_counters); i += gstride) p.cnt[i] = 0u;
   if (threadIdx.x == 0) trace(p, 504);
 }
 
@@ -430,11 +447,15 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       bool dep_done = false;
       auto release_deferred = [&](SegCursor ahead, bool more) {
         for (int i = 0; more && i < kL2Ahead; ++i) {
-          tma_prefetch_l2_3d(&p.tm_sfw, 0, ahead.t, ahead.kb * Cfg::kSfChunks);
 #pragma unroll
-          for (int h = 0; h < Cfg::kBoxes; ++h)
-            tma_prefetch_l2_2d(&p.tm_w, ahead.kb * Cfg::kBKBytes + h * Cfg::kBoxBytes,
-                               ahead.t * Cfg::kBM);
+          for (int hf = 0; hf < Cfg::kH; ++hf) {
+            const int rb = ahead.t * Cfg::kH + hf;  // 128-row block
+            tma_prefetch_l2_3d(&p.tm_sfw, 0, rb, ahead.kb * Cfg::kSfChunks);
+#pragma unroll
+            for (int h = 0; h < Cfg::kBoxes; ++h)
+              tma_prefetch_l2_2d(&p.tm_w, ahead.kb * Cfg::kBKBytes + h * Cfg::kBoxBytes,
+                                 rb * Cfg::kBM);
+          }
           more = ahead.next();
         }
         griddep_wait();  // the quantiser kernels have written xq / xsf
@@ -461,11 +482,16 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
         uint8_t* ssfw = sw + Cfg::kWBytes + Cfg::kXBytes;
         trace(p, 16 + g);
         mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageTx);
-        tma_load_3d(ssfw, &p.tm_sfw, &full_bar[stage], 0, cur.t, cur.kb * Cfg::kSfChunks, pol_w);
 #pragma unroll
-        for (int h = 0; h < Cfg::kBoxes; ++h)
-          tma_load_2d(sw + h * Cfg::kWBox, &p.tm_w, &full_bar[stage],
-                      cur.kb * Cfg::kBKBytes + h * Cfg::kBoxBytes, cur.t * Cfg::kBM, pol_w);
+        for (int hf = 0; hf < Cfg::kH; ++hf) {
+          const int rb = cur.t * Cfg::kH + hf;  // 128-row block
+          tma_load_3d(ssfw + hf * Cfg::kSfChunks * 512, &p.tm_sfw, &full_bar[stage], 0, rb,
+                      cur.kb * Cfg::kSfChunks, pol_w);
+#pragma unroll
+          for (int h = 0; h < Cfg::kBoxes; ++h)
+            tma_load_2d(sw + (h * Cfg::kH + hf) * Cfg::kWBox, &p.tm_w, &full_bar[stage],
+                        cur.kb * Cfg::kBKBytes + h * Cfg::kBoxBytes, rb * Cfg::kBM, pol_w);
+        }
         if (dep_done) {
           issue_x(stage, cur.kb);
         } else {
@@ -511,14 +537,14 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
         const int t = order.tile_of(seg);
         const int kb_lo = order.kb_lo(seg);
         const int kb_hi = order.kb_hi(seg);
-        const int buf = seg & 1;
-        if (!mbar_wait_bounded(&acc_empty[buf], ((seg >> 1) & 1) ^ 1u, p.timeout_ns, abort_flag,
-                               p.status, kDevTimeoutMma)) {
+        const int buf = seg % Cfg::kAccBufs;
+        if (!mbar_wait_bounded(&acc_empty[buf], ((seg / Cfg::kAccBufs) & 1) ^ 1u, p.timeout_ns,
+                               abort_flag, p.status, kDevTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * Cfg::kH * kN);
         uint32_t acc = 0;
         for (int j = kb_lo; j < kb_hi; ++j, ++g) {
           // sf_ready is arrived by the stagers only after they observed
@@ -532,13 +558,17 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
 #pragma unroll
           for (int i = 0; i < Cfg::kMmaPerStage; ++i) {
             if (skip_mma) break;
-            // MMA i: box i / 4, 32-byte K step (i % 4) inside the 128-byte row.
-            const uint64_t wo = static_cast<uint64_t>((i / 4) * (Cfg::kWBox >> 4) + (i % 4) * 2);
-            const uint64_t xo = static_cast<uint64_t>((i / 4) * (Cfg::kXBox >> 4) + (i % 4) * 2);
-            mma_mxf4nvf4(d_tmem, wdesc + wo, xdesc + xo, idesc, sfw_col + i * 4,
-                         sfw_col + 4 * Cfg::kSfChunks + i * 4, acc);
-            acc = 1;
+            // MMA i: half hf = i / kSfChunks, chunk c (box c / 4, 32-byte K
+            // step c % 4 inside the 128-byte row).
+            const int hf = i / Cfg::kSfChunks, c = i % Cfg::kSfChunks;
+            const uint64_t wo = static_cast<uint64_t>(((c / 4) * Cfg::kH + hf) * (Cfg::kWBox >> 4) +
+                                                      (c % 4) * 2);
+            const uint64_t xo = static_cast<uint64_t>((c / 4) * (Cfg::kXBox >> 4) + (c % 4) * 2);
+            mma_mxf4nvf4(d_tmem + static_cast<uint32_t>(hf * kN), wdesc + wo, xdesc + xo, idesc,
+                         sfw_col + hf * 4 * Cfg::kSfChunks + c * 4,
+                         sfw_col + Cfg::kH * 4 * Cfg::kSfChunks + c * 4, (acc | c) != 0 ? 1u : 0u);
           }
+          acc = 1;
           tc_commit(&empty_bar[stage]);
           trace(p, 320 + g);
           if (++stage == Cfg::kStages) {
@@ -576,22 +606,24 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       mbar_try_wait(&full_bar[stage], phase);
       const uint8_t* ssfw = smem + stage * Cfg::kStageBytes + Cfg::kWBytes + Cfg::kXBytes;
       const uint8_t* ssfx = ssfw + Cfg::kSfwBytes;
-      // Weight scales in columns [0, 32), activation scales in [32, 64) of
-      // the stage's slot, written with ONE tcgen05.st (a store costs about
-      // the same whatever its width).
-      uint32_t v[8 * Cfg::kSfChunks];
-      uint32_t* a = v;
-      uint32_t* b = v + 4 * Cfg::kSfChunks;
+      // The weight scales of each half, then the activation scales (4
+      // columns per 64-K chunk each) in the stage's slot, written with ONE
+      // tcgen05.st (a store costs about the same whatever its width).
+      uint32_t v[Cfg::kSfStageCols];
 #pragma unroll
-      for (int c = 0; c < Cfg::kSfChunks; ++c) {
-        const uint4 x = lds128(ssfw + c * 512 + lane * 16);
-        const uint4 w = lds128(ssfx + c * 512 + lane * 16);
-        a[4 * c] = x.x; a[4 * c + 1] = x.y; a[4 * c + 2] = x.z; a[4 * c + 3] = x.w;
-        b[4 * c] = w.x; b[4 * c + 1] = w.y; b[4 * c + 2] = w.z; b[4 * c + 3] = w.w;
-      }
+      for (int j = 0; j < Cfg::kH + 1; ++j)
+#pragma unroll
+        for (int c = 0; c < Cfg::kSfChunks; ++c) {
+          const uint4 x = lds128((j < Cfg::kH ? ssfw + j * Cfg::kSfChunks * 512 : ssfx) + c * 512 +
+                                 lane * 16);
+          uint32_t* d = v + (j * Cfg::kSfChunks + c) * 4;
+          d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+        }
+#pragma unroll
+      for (int j = Cfg::kSfWords; j < Cfg::kSfStageCols; ++j) v[j] = 0u;
       const uint32_t col = Cfg::kTmemSfBase + stage * Cfg::kSfStageCols;
       if (!(kDiag & 1u)) {
-        tmem_st_32x32b<8 * Cfg::kSfChunks>(t_quad + col, v);
+        tmem_st_32x32b<Cfg::kSfStageCols>(t_quad + col, v);
         tmem_wait_st();
       }
       tc_fence_before();
@@ -629,27 +661,34 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
     const int my_first = order.tile_lo;
     for (int seg = 0; seg < order.nseg(); ++seg) {
       const int t = order.tile_of(seg);
-      const int buf = seg & 1;
+      const int buf = seg % Cfg::kAccBufs;
+      const uint32_t par = static_cast<uint32_t>(seg / Cfg::kAccBufs) & 1u;
       bool ok = true;
       if (lane == 0)
-        ok = mbar_wait_bounded<false, 128>(&acc_full[buf], (seg >> 1) & 1, p.timeout_ns,
-                                           abort_flag, p.status, kDevTimeoutEpilogue);
+        ok = mbar_wait_bounded<false, 128>(&acc_full[buf], par, p.timeout_ns, abort_flag,
+                                           p.status, kDevTimeoutEpilogue);
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-      mbar_try_wait(&acc_full[buf], (seg >> 1) & 1);
+      mbar_try_wait(&acc_full[buf], par);
       tc_fence_after();
       if (quad == 0 && lane == 0) trace(p, 120 + seg);
       if (quad == 0 && lane == 0 && seg == order.nseg() - 1) trace_cta(p, 1536 + blockIdx.x);
-      const int col = quad * 32 + lane;
-      const int n = t * Cfg::kBM + col;
-      const bool n_ok = n < p.n;
       // Contributors of a split tile (whole tiles: this CTA alone).
       const bool split = order.split(seg);
       const int cf = split ? ur.contributor(static_cast<int64_t>(t) * ur.nkb, grid)
                            : static_cast<int>(blockIdx.x);
       const int cl = split ? ur.contributor(static_cast<int64_t>(t + 1) * ur.nkb - 1, grid)
                            : static_cast<int>(blockIdx.x);
-      float* mine = p.part + static_cast<int64_t>(blockIdx.x * 2 + (t == my_first ? 0 : 1)) *
-                                 p.m * Cfg::kBM;
+      // Each 128-row half of the tile is stored, counted and summed as a
+      // tile of its own (vt: its 128-row block; its counter and slices):
+      // first both halves' stores, then both halves' counting.
+#pragma unroll 1
+      for (int hf = 0; hf < Cfg::kH; ++hf) {
+      const int vt = t * Cfg::kH + hf;
+      const int col = quad * 32 + lane;
+      const int n = vt * Cfg::kBM + col;
+      const bool n_ok = n < p.n;
+      float* mine = p.part + (static_cast<int64_t>(blockIdx.x * 2 + (t == my_first ? 0 : 1)) *
+                                  Cfg::kH + hf) * p.m * Cfg::kBM;
       // TMEM reads queue behind the MMAs already issued for the next
       // segment, so each wait can cost the queued MMA time: read up to 64
       // columns per wait (one wait for kN <= 64, two for kN = 128).
@@ -667,17 +706,18 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       float* dstf = whole ? reinterpret_cast<float*>(p.c) + n : mine + col;
       __nv_bfloat16* dstb = reinterpret_cast<__nv_bfloat16*>(p.c) + n;
       const int mrows = p.m;
-      const int n_tail = t * Cfg::kBM + quad * 32;
+      const int n_tail = vt * Cfg::kBM + quad * 32;
       const bool bf16_tail = bf16_dst && seg == order.nseg() - 1 && p.vec_ok && n_tail + 32 <= p.n;
 #pragma unroll
       for (int gc = 0; gc < kN / kGroup; ++gc) {
         uint32_t r[kGroup];
 #pragma unroll
         for (int cc = 0; cc < kGroup / 16; ++cc)
-          tmem_ld_32x32b_x16(t_quad + static_cast<uint32_t>(buf * kN + gc * kGroup + cc * 16),
+          tmem_ld_32x32b_x16(t_quad + static_cast<uint32_t>((buf * Cfg::kH + hf) * kN +
+                                                            gc * kGroup + cc * 16),
                              *reinterpret_cast<uint32_t(*)[16]>(r + cc * 16));
         tmem_wait_ld();
-        if (gc == kN / kGroup - 1) {
+        if (gc == kN / kGroup - 1 && hf == Cfg::kH - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -724,7 +764,14 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
         }
       }
       if (quad == 0 && lane == 0) trace(p, 100 + seg);
+      }  // halves: stores
       if (cf == cl) continue;
+      // The accumulator is released (after the last half's reads) before
+      // any counting or summing, so the next segment's MMAs do not wait for
+      // a sum pass.
+#pragma unroll 1
+      for (int hf = 0; hf < Cfg::kH; ++hf) {
+      const int vt = t * Cfg::kH + hf;
       // Publish the slice and count this contributor with one acquire-release
       // atomic from lane 0: the warp barrier before it orders every lane's
       // slice stores ahead of the release (fence cumulativity), the one after
@@ -734,7 +781,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       if (quad == 0 && lane == 0) trace(p, 300 + 4 * seg);
       __syncwarp();
       uint32_t old = 0;
-      if (lane == 0) old = atom_add_acq_rel_gpu(&p.cnt[t * 4 + quad], 1u);
+      if (lane == 0) old = atom_add_acq_rel_gpu(&p.cnt[vt * 4 + quad], 1u);
       old = __shfl_sync(0xffffffffu, old, 0);
       __syncwarp();
       if (quad == 0 && lane == 0) trace(p, 301 + 4 * seg);
@@ -747,7 +794,7 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
       {
         const int sub = lane >> 2, c8 = (lane & 3) * 8;
         const int64_t slice = static_cast<int64_t>(p.m) * Cfg::kBM;
-        const int nb = t * Cfg::kBM + quad * 32 + c8;
+        const int nb = vt * Cfg::kBM + quad * 32 + c8;
         const bool vec = p.vec_ok && nb + 8 <= p.n;
 #pragma unroll 1
         for (int m0 = 0; m0 < p.m; m0 += 32) {
@@ -761,13 +808,13 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
             // Up to three contributors' loads in flight at once (a split
             // tile has two or three): one memory round per 32 rows.
             const bool two = c + 1 <= cl, three = c + 2 <= cl;
-            const float* s0 = p.part + (c * 2 + (t == first_tile(c) ? 0 : 1)) * slice + quad * 32 + c8;
-            const float* s1 = two ? p.part + ((c + 1) * 2 + (t == first_tile(c + 1) ? 0 : 1)) * slice +
-                                        quad * 32 + c8
-                                  : s0;
-            const float* s2 = three ? p.part + ((c + 2) * 2 + (t == first_tile(c + 2) ? 0 : 1)) * slice +
-                                          quad * 32 + c8
-                                    : s0;
+            auto slice_of = [&](int cc) {
+              return p.part + ((cc * 2 + (t == first_tile(cc) ? 0 : 1)) * Cfg::kH + hf) * slice +
+                     quad * 32 + c8;
+            };
+            const float* s0 = slice_of(c);
+            const float* s1 = two ? slice_of(c + 1) : s0;
+            const float* s2 = three ? slice_of(c + 2) : s0;
             float4 v0[4][2], v1[4][2], v2[4][2];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -832,9 +879,10 @@ __global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_consta
           }
         }
       }
-      if (lane == 0) p.cnt[t * 4 + quad] = 0u;  // ready for the next call
+      if (lane == 0) p.cnt[vt * 4 + quad] = 0u;  // ready for the next call
       if (quad == 0 && lane == 0) trace_cta(p, 1280 + blockIdx.x);
       if (quad == 0 && lane == 0) trace(p, 200 + seg);
+      }  // halves: counting and sums
     }
   }
 
@@ -924,6 +972,26 @@ int skinny_quant_grid(int64_t xblocks, int sms) {
   int64_t g = (xblocks + kSqThreads - 1) / kSqThreads;  // one block per thread
   if (g > sms) g = sms;
   return g < 1 ? 1 : static_cast<int>(g);
+}
+
+template <int kN>
+static SkinnyShape shape_of() {
+  using Cfg = SkinnyCfg<kN>;
+  SkinnyShape sh;
+  sh.tile_rows = Cfg::kTileRows;
+  sh.stage_k_bytes = Cfg::kBKBytes;
+  sh.sf_chunks = Cfg::kSfChunks;
+  sh.halves = Cfg::kH;
+  return sh;
+}
+
+SkinnyShape skinny_shape(int64_t m) {
+  switch (skinny_mma_n(m)) {
+    case 16: return shape_of<16>();
+    case 32: return shape_of<32>();
+    case 64: return shape_of<64>();
+    default: return shape_of<128>();
+  }
 }
 
 int skinny_max_ctas() { return kSkinnyMaxCtas; }

@@ -86,10 +86,20 @@ struct SkinnyParams {
   int out_bf16;
   int vec_ok;          // C rows start 16-byte aligned (16-byte stores legal)
   int m, n, k;
-  int num_tiles, num_k_blocks;
+  int num_tiles, num_k_blocks;  // tiles of SkinnyShape::tile_rows, K blocks per stage
+  int slices;                    // partial slices per CTA (2 per 128-row half)
+  int num_counters;              // words of cnt the quantiser zeroes
   uint32_t* status;
   uint64_t timeout_ns;
 };
+// Tile geometry of the decode GEMM for m activation rows.
+struct SkinnyShape {
+  int tile_rows;      // weight rows per tile (128, or 256 as two halves)
+  int stage_k_bytes;  // K bytes per stage (256 or 128)
+  int sf_chunks;      // 64-K scale chunks per stage
+  int halves;         // 128-row halves per tile
+};
+SkinnyShape skinny_shape(int64_t m);
 cudaError_t launch_gemm_skinny(const SkinnyParams& p, int grid, cudaStream_t stream);
 int skinny_quant_grid(int64_t xblocks, int sms);
 cudaError_t launch_skinny_quant(const SkinnyParams& p, int grid, cudaStream_t stream);
