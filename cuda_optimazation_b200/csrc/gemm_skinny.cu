@@ -35,8 +35,20 @@ namespace qg {
 #ifndef QG_SKINNY_WIDE
 #define QG_SKINNY_WIDE 1
 #endif
+// Register budgets that let one quantiser CTA (128 threads, <= 56
+// registers) sit on an SM beside a GEMM CTA (320 threads, <= 152): an SM
+// sub-partition holds three GEMM warps (3 x 152 x 32 registers) and one
+// quantiser warp (56 x 32) in its 16384 registers, so the GEMM's CTAs start
+// streaming weights at once on every SM instead of waiting for the
+// quantiser CTAs there to exit.
+#ifndef QG_SQ_MAXREG
+#define QG_SQ_MAXREG 56
+#endif
+#ifndef QG_SKINNY_BOUNDS
+#define QG_SKINNY_BOUNDS __maxnreg__(152)
+#endif
 #ifndef QG_SQ_THREADS
-#define QG_SQ_THREADS 256
+#define QG_SQ_THREADS 128
 #endif
 #ifndef QG_SKINNY_L2_AHEAD
 #define QG_SKINNY_L2_AHEAD 8
@@ -213,18 +225,18 @@ __device__ __forceinline__ void trace(const SkinnyParams& p, int i) {
 // epilogue.  Measured against quantising inside the GEMM (two grid-wide
 // arrivals under the weight stream): the GEMM without any quantisation is
 // 17 % (m = 16) and 22 % (m = 128) faster, the bound this design aims at.
-// A GEMM CTA leaves too few registers in some SM sub-partitions for a
-// quantiser CTA beside it, so the GEMM CTAs on the SMs the quantiser uses
-// start when it exits: the quantiser spreads over many SMs and keeps its
-// per-block work short (hardware e2m1 conversion, a per-CTA table of the
-// 127 possible element multipliers instead of a division per block).
+// The quantiser CTAs fit beside the GEMM's (register budgets above); their
+// per-block work is kept short (hardware e2m1 conversion, a per-CTA table
+// of the 127 possible element multipliers instead of a division per block).
 constexpr int kSqThreads = QG_SQ_THREADS;
+constexpr int kSqMinCtas = 65536 / (kSqThreads * QG_SQ_MAXREG);
+static_assert(kSqThreads >= 128, "one thread per multiplier-table entry");
 // Blocks whose loads are in flight together in one thread.
 template <bool kBf16>
 constexpr int kSqUnroll = kBf16 ? 2 : 1;
 
 template <bool kBf16>
-__global__ void __launch_bounds__(kSqThreads) skinny_amax_kernel(const __grid_constant__ SkinnyParams p) {
+__global__ void __launch_bounds__(kSqThreads, kSqMinCtas) skinny_amax_kernel(const __grid_constant__ SkinnyParams p) {
   griddep_launch_dependents();
   if (kDiag & 64u) {
     if (threadIdx.x == 0 && blockIdx.x == (kDiag >> 16)) {
@@ -266,7 +278,7 @@ __global__ void __launch_bounds__(kSqThreads) skinny_amax_kernel(const __grid_co
 }
 
 template <bool kBf16>
-__global__ void __launch_bounds__(kSqThreads)
+__global__ void __launch_bounds__(kSqThreads, kSqMinCtas)
     skinny_quant_kernel(const __grid_constant__ SkinnyParams p, int amax_ctas) {
   griddep_launch_dependents();
   const int G = gridDim.x, c = blockIdx.x;
@@ -366,7 +378,7 @@ __global__ void __launch_bounds__(kSqThreads)
 }
 
 template <int kN>
-__global__ void __launch_bounds__(320, 1) gemm_skinny_kernel(const __grid_constant__ SkinnyParams p) {
+__global__ void QG_SKINNY_BOUNDS gemm_skinny_kernel(const __grid_constant__ SkinnyParams p) {
   using Cfg = SkinnyCfg<kN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
