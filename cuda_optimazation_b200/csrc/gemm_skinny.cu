@@ -50,8 +50,17 @@ namespace qg {
 #ifndef QG_SQ_THREADS
 #define QG_SQ_THREADS 128
 #endif
+#ifndef QG_SKINNY_L2_ROLL
+#define QG_SKINNY_L2_ROLL 1
+#endif
 #ifndef QG_SKINNY_L2_AHEAD
-#define QG_SKINNY_L2_AHEAD 8
+#define QG_SKINNY_L2_AHEAD 1
+#endif
+#ifndef QG_SKINNY_L2_ROLL_WIDE
+#define QG_SKINNY_L2_ROLL_WIDE 0
+#endif
+#ifndef QG_SKINNY_L2_AHEAD_WIDE
+#define QG_SKINNY_L2_AHEAD_WIDE 8
 #endif
 
 // Upper bound of the GEMM grid; sizes the partial-tile workspace.
@@ -444,7 +453,15 @@ __global__ void QG_SKINNY_BOUNDS gemm_skinny_kernel(const __grid_constant__ Skin
       // next kL2Ahead units' weights are prefetched into L2; the activation
       // loads wait for the quantiser kernels (griddepcontrol.wait), so the
       // weight stream runs while the activations are being quantised.
-      constexpr int kL2Ahead = QG_SKINNY_L2_AHEAD;  // units (32 KB of weights each)
+      // 128-row tiles: a rolling lead of kL2Ahead units ahead of the stage
+      // ring (prefetched as each stage is issued); wide tiles: kL2Ahead
+      // units once, when the activation loads are released.  Swept on one
+      // box (GB/s, m = 16 / 64 / 128): no rolling lead, 8 units: 5185 /
+      // 4241 / 4299; rolling 1: 5595 / 4366 / 4275; rolling 2: 5580 / 4335 /
+      // 4067; rolling 4: 5355 / 4200 / 4063; rolling 8: 4770 / 3631 / 3911.
+      // A deeper lead competes with the ring's own loads for the same HBM.
+      constexpr bool kL2Roll = Cfg::kH == 1 ? QG_SKINNY_L2_ROLL : QG_SKINNY_L2_ROLL_WIDE;
+      constexpr int kL2Ahead = Cfg::kH == 1 ? QG_SKINNY_L2_AHEAD : QG_SKINNY_L2_AHEAD_WIDE;  // units (32 KB of weights each)
       int deferred = 0;
       int dkb[Cfg::kStages];
       auto issue_x = [&](int s, int k_blk) {
@@ -457,19 +474,26 @@ __global__ void QG_SKINNY_BOUNDS gemm_skinny_kernel(const __grid_constant__ Skin
                       k_blk * Cfg::kBKBytes + h * Cfg::kBoxBytes, 0, pol_x);
       };
       bool dep_done = false;
+      auto prefetch_unit = [&](const SegCursor& u) {
+#pragma unroll
+        for (int hf = 0; hf < Cfg::kH; ++hf) {
+          const int rb = u.t * Cfg::kH + hf;  // 128-row block
+          tma_prefetch_l2_3d(&p.tm_sfw, 0, rb, u.kb * Cfg::kSfChunks);
+#pragma unroll
+          for (int h = 0; h < Cfg::kBoxes; ++h)
+            tma_prefetch_l2_2d(&p.tm_w, u.kb * Cfg::kBKBytes + h * Cfg::kBoxBytes,
+                               rb * Cfg::kBM);
+        }
+      };
+      SegCursor pf;
+      bool pf_more = false;
       auto release_deferred = [&](SegCursor ahead, bool more) {
         for (int i = 0; more && i < kL2Ahead; ++i) {
-#pragma unroll
-          for (int hf = 0; hf < Cfg::kH; ++hf) {
-            const int rb = ahead.t * Cfg::kH + hf;  // 128-row block
-            tma_prefetch_l2_3d(&p.tm_sfw, 0, rb, ahead.kb * Cfg::kSfChunks);
-#pragma unroll
-            for (int h = 0; h < Cfg::kBoxes; ++h)
-              tma_prefetch_l2_2d(&p.tm_w, ahead.kb * Cfg::kBKBytes + h * Cfg::kBoxBytes,
-                                 rb * Cfg::kBM);
-          }
+          prefetch_unit(ahead);
           more = ahead.next();
         }
+        pf = ahead;
+        pf_more = more;
         griddep_wait();  // the quantiser kernels have written xq / xsf
         asm volatile("fence.proxy.async.global;" ::: "memory");  // read by TMA
         trace(p, 2);
@@ -506,6 +530,10 @@ __global__ void QG_SKINNY_BOUNDS gemm_skinny_kernel(const __grid_constant__ Skin
         }
         if (dep_done) {
           issue_x(stage, cur.kb);
+          if (kL2Roll && pf_more) {  // keep kL2Ahead units in L2 ahead
+            prefetch_unit(pf);
+            pf_more = pf.next();
+          }
         } else {
           dkb[deferred++] = cur.kb;
         }
