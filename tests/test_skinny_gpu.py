@@ -139,3 +139,30 @@ def test_skinny_wide_whole_tiles_ragged_n(qlib, oracle, m, n, out):
     partly (28736) or wholly (28800) past the weights' end."""
     cols = np.unique(np.concatenate([np.arange(0, n, 89), np.arange(n - 300, n)]))
     run_case(qlib, oracle, m, n, 1024, out, cols=cols)
+
+
+def test_skinny_chained_calls_read_previous_output(qlib, oracle):
+    """A decode call whose activations are the previous call's output on the
+    same stream (its amax kernel must start only after that GEMM has
+    finished; the quantiser and GEMM launch early and wait on it): the
+    chained result equals the same call made after a device synchronise."""
+    m, k, n1, n2 = 16, 1024, 4096, 2048
+    W1 = qlib.make_nvfp4(torch.from_numpy(oracle.normal(n1 * k, 21, 0.0, 0.02).reshape(n1, k)).cuda())
+    W2 = qlib.make_nvfp4(torch.from_numpy(oracle.normal(n2 * n1, 22, 0.0, 0.02).reshape(n2, n1)).cuda())
+    x = activations(oracle, m, k, 5).cuda()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ws1 = qlib.skinny_workspace(m, n1, k, "cuda")
+    ws2 = qlib.skinny_workspace(m, n2, n1, "cuda")
+    chained = []
+    for _ in range(3):
+        y1 = qlib.gemm_nvfp4_skinny(x * 2.0, W1, torch.bfloat16, workspace=ws1, status=status)
+        chained.append(qlib.gemm_nvfp4_skinny(y1, W2, torch.float32, workspace=ws2, status=status))
+    torch.cuda.synchronize()
+    rc, code = qlib.read_status(status)
+    assert rc == qlib.OK, code
+    y1 = qlib.gemm_nvfp4_skinny(x * 2.0, W1, torch.bfloat16, workspace=ws1, status=status)
+    torch.cuda.synchronize()
+    ref = qlib.gemm_nvfp4_skinny(y1.clone(), W2, torch.float32, workspace=ws2, status=status)
+    torch.cuda.synchronize()
+    for c in chained:
+        assert torch.equal(c, ref)
