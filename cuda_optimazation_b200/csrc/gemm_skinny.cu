@@ -35,6 +35,14 @@ namespace qg {
 #ifndef QG_SKINNY_WIDE
 #define QG_SKINNY_WIDE 1
 #endif
+// Smallest MMA N (activation rows, padded) that takes the wide tiles.  A/B on
+// one box, GB/s (m = 16 / 64 / 128): wide from N = 128: 5282 / 4132 / 4082;
+// from N = 64: 5239 / 4444 / 4067; from N = 16: 4632 / 4434 / 4104 (at
+// m = 16 the 128-row tiles' double-buffered accumulator and rolling L2 lead
+// outweigh the activation bytes saved).
+#ifndef QG_SKINNY_WIDE_MIN_N
+#define QG_SKINNY_WIDE_MIN_N 64
+#endif
 // Register budgets that let one quantiser CTA (128 threads, <= 56
 // registers) sit on an SM beside a GEMM CTA (320 threads, <= 152): an SM
 // sub-partition holds three GEMM warps (3 x 152 x 32 registers) and one
@@ -66,16 +74,16 @@ namespace qg {
 // Upper bound of the GEMM grid; sizes the partial-tile workspace.
 constexpr int kSkinnyMaxCtas = 256;
 
-// Tile shape by MMA N.  N <= 64: a tile is 128 weight rows, a stage 512 of
+// Tile shape by MMA N.  N <= 32: a tile is 128 weight rows, a stage 512 of
 // K, two accumulator buffers (the next segment's MMAs overlap the epilogue).
-// N = 128 ("wide"): a tile is 256 weight rows as two 128-row MMA halves
+// N = 64 and 128 ("wide"): a tile is 256 weight rows as two 128-row MMA halves
 // that share the stage's activations, a stage 256 of K, one accumulator
 // buffer of both halves.  The activation bytes per weight byte halve (16 KB
 // per 32 KB of weights instead of 32 KB), so four stages fit in shared
 // memory instead of three and more weight bytes are in flight per SM.
 template <int kN>
 struct SkinnyCfg {
-  static constexpr int kH = (QG_SKINNY_WIDE && kN == 128) ? 2 : 1;  // 128-row halves per tile
+  static constexpr int kH = (QG_SKINNY_WIDE && kN >= QG_SKINNY_WIDE_MIN_N) ? 2 : 1;  // 128-row halves per tile
   static constexpr int kBM = 128;        // weight rows per MMA (half)
   static constexpr int kTileRows = kBM * kH;
   static constexpr int kBoxBytes = 128;  // one SWIZZLE_128B box: 256 fp4 of K

@@ -132,9 +132,10 @@ def test_skinny_schedules(qlib, oracle, m, n, k):
     run_case(qlib, oracle, m, n, k, torch.bfloat16, cols=cols)
 
 
-@pytest.mark.parametrize("m,n,out", [(128, 28736, torch.bfloat16), (100, 28800, torch.float32)])
+@pytest.mark.parametrize("m,n,out", [(128, 28736, torch.bfloat16), (100, 28800, torch.float32),
+                                     (64, 28736, torch.float32), (40, 28800, torch.bfloat16)])
 def test_skinny_wide_whole_tiles_ragged_n(qlib, oracle, m, n, out):
-    """m > 64 at a decode-sized N takes 256-row wide tiles, one whole tile
+    """m > 32 at a decode-sized N takes 256-row wide tiles, one whole tile
     per CTA; N not a multiple of 256 leaves the last tile's second half
     partly (28736) or wholly (28800) past the weights' end."""
     cols = np.unique(np.concatenate([np.arange(0, n, 89), np.arange(n - 300, n)]))
