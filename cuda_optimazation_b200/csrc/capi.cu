@@ -521,6 +521,13 @@ int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void
                      sf_layout, status, reinterpret_cast<cudaStream_t>(stream));
 }
 
+// Decode GEMM on CTA pairs for m in (32, 128] at the decode shapes (a build
+// with -DQG_SKINNY_PAIR=0 keeps the single-CTA wide tiles, for A/B
+// measurement).
+#ifndef QG_SKINNY_PAIR
+#define QG_SKINNY_PAIR 1
+#endif
+
 // Workspace of qg_gemm_nvfp4_skinny, each part 256-byte aligned: the
 // per-CTA partial tiles [max_ctas][2][m][128] fp32, the tile counters
 // [tiles][4] (zeroed by the quantiser kernel of every call), the quantised
@@ -571,11 +578,18 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   float* xts = reinterpret_cast<float*>(base + wl.xts);
   const int mma_n = skinny_mma_n(m);
   const SkinnyShape sh = skinny_shape(m);
+  // CTA pairs (one whole 512-row weight tile each, half of the activation
+  // rows loaded per CTA) when the tiles nearly fill the SMs, as at the
+  // decode shapes (n = 28672: 56 pairs on 148 SMs); stream-K otherwise.
+  const int64_t pair_tiles = (n + skinny_pair_tile_rows() - 1) / skinny_pair_tile_rows();
+  const bool use_pair = QG_SKINNY_PAIR && mma_n >= 64 && 2 * pair_tiles <= num_sms() &&
+                        8 * pair_tiles >= 3 * num_sms();
   SkinnyParams p;
   std::memset(&p, 0, sizeof(p));
   const int64_t row_bytes = k / 2;
   if (!make_operand_map(&p.tm_w, w_q, n, row_bytes, 128)) return QG_ERR_CUDA;
-  if (!make_operand_map(&p.tm_x, xq, m, row_bytes, mma_n)) return QG_ERR_CUDA;
+  if (!make_operand_map(&p.tm_x, xq, m, row_bytes, use_pair ? mma_n / 2 : mma_n))
+    return QG_ERR_CUDA;
   if (!make_scale_map(&p.tm_sfw, w_sf, n, k, 16, sf_layout, 1, sh.sf_chunks)) return QG_ERR_CUDA;
   if (!make_scale_map(&p.tm_sfx, xsf, m, k, 16, QG_LAYOUT_MMA, 1, sh.sf_chunks))
     return QG_ERR_CUDA;
@@ -614,9 +628,16 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
   if (sh.halves == 2 && p.num_tiles <= num_sms() && 4 * p.num_tiles >= 3 * num_sms())
     grid = p.num_tiles;
   if (grid > skinny_max_ctas()) grid = skinny_max_ctas();
+  if (use_pair) {
+    p.num_tiles = static_cast<int>(pair_tiles);
+    p.num_counters = 0;  // no split tiles
+    grid = 2 * pair_tiles;
+  }
   if (launch_skinny_quant(p, skinny_quant_grid(xblocks, num_sms()), s) != cudaSuccess)
     return QG_ERR_CUDA;
-  if (launch_gemm_skinny(p, static_cast<int>(grid), s) != cudaSuccess) return QG_ERR_CUDA;
+  const cudaError_t le = use_pair ? launch_gemm_skinny_pair(p, static_cast<int>(grid), s)
+                                  : launch_gemm_skinny(p, static_cast<int>(grid), s);
+  if (le != cudaSuccess) return QG_ERR_CUDA;
   return QG_OK;
 }
 

@@ -101,6 +101,11 @@ struct SkinnyShape {
 };
 SkinnyShape skinny_shape(int64_t m);
 cudaError_t launch_gemm_skinny(const SkinnyParams& p, int grid, cudaStream_t stream);
+// Decode GEMM on CTA pairs (gemm_skinny_pair.cu), MMA N = 64 or 128: one whole
+// skinny_pair_tile_rows()-row weight tile per pair (grid = 2 x tiles); tm_x
+// has a box of mma_n / 2 rows (each CTA loads half of the activation rows).
+cudaError_t launch_gemm_skinny_pair(const SkinnyParams& p, int grid, cudaStream_t stream);
+int skinny_pair_tile_rows();
 int skinny_quant_grid(int64_t xblocks, int sms);
 cudaError_t launch_skinny_quant(const SkinnyParams& p, int grid, cudaStream_t stream);
 int skinny_max_ctas();

@@ -167,3 +167,23 @@ def test_skinny_chained_calls_read_previous_output(qlib, oracle):
     torch.cuda.synchronize()
     for c in chained:
         assert torch.equal(c, ref)
+
+
+@pytest.mark.parametrize("m,k,out", [(64, 1056, torch.bfloat16), (128, 2080, torch.float32),
+                                     (33, 8192, torch.bfloat16)])
+def test_skinny_pair_tiles(qlib, oracle, m, k, out):
+    """m in (32, 128] at a decode-sized N runs on CTA pairs (one 512-row
+    weight tile per pair, each CTA loading half of the activation rows):
+    K not a multiple of the 256-element stage (the last stage partly past
+    the operands' end), fp32 and bf16 output, and the fewest rows that take
+    the pairs; sampled columns in every tile, and repeated calls give the
+    same bits."""
+    n = 28672
+    cols = np.unique(np.concatenate([np.arange(0, n, 127), np.arange(n - 512, n)]))
+    run_case(qlib, oracle, m, n, k, out, cols=cols)
+    xw = oracle.normal(n * k, 7, 0.0, 0.02).reshape(n, k)
+    W = qlib.make_nvfp4(torch.from_numpy(xw).cuda())
+    x = activations(oracle, m, k, 100 + m).cuda()
+    a = qlib.gemm_nvfp4_skinny(x, W, out)
+    b = qlib.gemm_nvfp4_skinny(x, W, out)
+    assert torch.equal(a, b)
