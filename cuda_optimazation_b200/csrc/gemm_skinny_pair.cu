@@ -43,8 +43,13 @@ namespace qg {
 #ifndef QG_SKINNY_BOUNDS
 #define QG_SKINNY_BOUNDS __maxnreg__(152)
 #endif
+// Units (32 KB of weights each) prefetched into L2 in one burst before the
+// producer waits for the quantiser kernels.  Swept on one box (GB/s,
+// m = 64 / 128): 4: 4706 / 4306, 8: 4734 / 4362, 16: 4754 / 4440-4458,
+// 24: 4443 / 4312, 32: 4442 / 4306; a rolling lead (8 units kept ahead of
+// the ring as each stage is issued): 4443 / 4052.
 #ifndef QG_SKINNY_PAIR_L2_AHEAD
-#define QG_SKINNY_PAIR_L2_AHEAD 8
+#define QG_SKINNY_PAIR_L2_AHEAD 16
 #endif
 
 template <int kN>
@@ -169,14 +174,17 @@ __global__ void __cluster_dims__(2, 1, 1) QG_SKINNY_BOUNDS
       // Before waiting for the quantiser kernels: the next units' weights
       // into L2, so the weight stream runs on while the activations are
       // quantised.
+      auto prefetch_unit = [&](int kb) {
+#pragma unroll
+        for (int hf = 0; hf < Cfg::kH; ++hf) {
+          const int rb = t * 4 + hf * 2 + static_cast<int>(rank);
+          tma_prefetch_l2_3d(&p.tm_sfw, 0, rb, kb * Cfg::kSfChunks);
+          tma_prefetch_l2_2d(&p.tm_w, kb * Cfg::kBoxBytes, rb * Cfg::kBM);
+        }
+      };
       auto release = [&](int next_kb) {
         for (int kb = next_kb; kb < nkb && kb < next_kb + QG_SKINNY_PAIR_L2_AHEAD; ++kb)
-#pragma unroll
-          for (int hf = 0; hf < Cfg::kH; ++hf) {
-            const int rb = t * 4 + hf * 2 + static_cast<int>(rank);
-            tma_prefetch_l2_3d(&p.tm_sfw, 0, rb, kb * Cfg::kSfChunks);
-            tma_prefetch_l2_2d(&p.tm_w, kb * Cfg::kBoxBytes, rb * Cfg::kBM);
-          }
+          prefetch_unit(kb);
         griddep_wait();  // the quantiser kernels have written xq / xsf
         asm volatile("fence.proxy.async.global;" ::: "memory");  // read by TMA
         for (int s = 0; s < deferred; ++s) issue_x(s, s);
