@@ -135,9 +135,10 @@ def test_skinny_schedules(qlib, oracle, m, n, k):
 @pytest.mark.parametrize("m,n,out", [(128, 28736, torch.bfloat16), (100, 28800, torch.float32),
                                      (64, 28736, torch.float32), (40, 28800, torch.bfloat16)])
 def test_skinny_wide_whole_tiles_ragged_n(qlib, oracle, m, n, out):
-    """m > 32 at a decode-sized N takes 256-row wide tiles, one whole tile
-    per CTA; N not a multiple of 256 leaves the last tile's second half
-    partly (28736) or wholly (28800) past the weights' end."""
+    """m > 32 at a decode-sized N takes whole 512-row tiles on CTA pairs
+    (two 128-row halves per CTA); N = 28736 and 28800 (57 pair tiles) leave
+    the last tile's first CTA partly past the weights' end and its second
+    CTA wholly past it."""
     cols = np.unique(np.concatenate([np.arange(0, n, 89), np.arange(n - 300, n)]))
     run_case(qlib, oracle, m, n, 1024, out, cols=cols)
 
