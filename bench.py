@@ -624,8 +624,11 @@ def run_skinny(args, name, w, rank, world, dist, torch, steps, headline=True):
                      "peak_basis": f"{pk['source']} STREAM copy GB/s; achieved counts the whole "
                                    "fused call (amax + quantiser + GEMM launches) as the unit",
                      "algorithmic_bytes_per_call": int(bytes_step),
-                     "kernel": "gemm_skinny_kernel (with skinny_amax_kernel and "
-                               "skinny_quant_kernel ahead of it in each call)"},
+                     # m in (32, 128] at this n runs on CTA pairs (the library's choice
+                     # for decode shapes whose 512-row tiles nearly fill the SMs)
+                     "kernel": ("gemm_skinny_pair_kernel" if m > 32 else "gemm_skinny_kernel")
+                               + " (with skinny_amax_kernel and skinny_quant_kernel ahead of "
+                                 "it in each call)"},
         "gpu_launches": 3 * steps,  # amax, quantiser, GEMM per call
         "clocks": clocks.summary(),
     }
