@@ -242,8 +242,12 @@ int qg_plan_destroy(qg_plan plan);
  * call: x (m x k, bf16 or fp32, m <= 128) is quantised to NVFP4 exactly as
  * qg_quantize_nvfp4 would, then C[m, n] = (ts_x * w_ts) * x_q . w_q^T with the
  * pre-quantised weights w_q (n x k, MMA layout, scales in sf_layout).  The
- * weights are streamed once at HBM rate (stream-K over 128-row weight tiles
- * on every SM).  Three launches on `stream`: an amax pass over x, the
+ * weights are streamed once from HBM: stream-K over 128-row weight tiles
+ * (256-row tiles of two halves for m > 32) on every SM, or, for m in
+ * (32, 128] when n's 512-row tiles nearly fill the SMs (decode shapes such
+ * as n = 28672), one whole tile per CTA pair (a thread-block cluster of two)
+ * with each CTA loading half of the activation rows.  Three launches on
+ * `stream`: an amax pass over x, the
  * quantiser, and the GEMM, the last two with programmatic dependent launch so
  * the GEMM streams weights while x is quantised.  `workspace` (device,
  * qg_gemm_nvfp4_skinny_workspace_bytes) holds the partial tiles, the
@@ -251,7 +255,8 @@ int qg_plan_destroy(qg_plan plan);
  * (every call rewrites what it reads, counters and scale padding included,
  * also after a call that returned a device timeout).  One workspace serves
  * one stream at a time.  K % 32 == 0.  The result is
- * deterministic (split tiles are summed in a fixed order).
+ * deterministic (split tiles are summed in a fixed order; pair tiles are
+ * never split).
  * No reference counterpart kernel: the reference harness runs square
  * problems only (GEMMquant_sm110/src/quant_gemm_bench.cu:3038-3079); this is
  * the decode configuration of its quant-GEMM path. */
