@@ -527,6 +527,9 @@ int qg_gemm_mxfp8(const void* a_q, const void* a_sf, const void* b_q, const void
 #ifndef QG_SKINNY_PAIR
 #define QG_SKINNY_PAIR 1
 #endif
+#ifndef QG_SKINNY_PAIR_QUANT_WIDE
+#define QG_SKINNY_PAIR_QUANT_WIDE 1
+#endif
 
 // Workspace of qg_gemm_nvfp4_skinny, each part 256-byte aligned: the
 // per-CTA partial tiles [max_ctas][2][m][128] fp32, the tile counters
@@ -633,7 +636,16 @@ int qg_gemm_nvfp4_skinny(const void* x, int x_dtype, int64_t m, const void* w_q,
     p.num_counters = 0;  // no split tiles
     grid = 2 * pair_tiles;
   }
-  if (launch_skinny_quant(p, skinny_quant_grid(xblocks, num_sms()), s) != cudaSuccess)
+  // Quantiser CTAs (128 threads, <= 56 registers) beside the GEMM's: two fit
+  // next to a pair-kernel CTA (<= 112 registers per thread), so for m > 64
+  // the quantiser may use up to skinny_max_ctas() CTAs there (at m = 128 two
+  // 16-element blocks per thread instead of ~3.5: one load round instead of
+  // two).  A/B on one box, GB/s: m = 128 4347 / 4373 / 4357 -> 4517 / 4535 /
+  // 4572; m = 64 (one block per thread either way) 4717 / 4737 / 4712 ->
+  // 4690 / 4725 / 4705, so m <= 64 keeps one CTA per SM.
+  const int quant_ctas =
+      use_pair && mma_n == 128 && QG_SKINNY_PAIR_QUANT_WIDE ? skinny_max_ctas() : num_sms();
+  if (launch_skinny_quant(p, skinny_quant_grid(xblocks, quant_ctas), s) != cudaSuccess)
     return QG_ERR_CUDA;
   const cudaError_t le = use_pair ? launch_gemm_skinny_pair(p, static_cast<int>(grid), s)
                                   : launch_gemm_skinny(p, static_cast<int>(grid), s);
