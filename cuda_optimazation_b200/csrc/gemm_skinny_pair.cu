@@ -47,9 +47,11 @@ namespace qg {
 // producer waits for the quantiser kernels.  Swept on one box (GB/s,
 // m = 64 / 128): 4: 4706 / 4306, 8: 4734 / 4362, 16: 4754 / 4440-4458,
 // 24: 4443 / 4312, 32: 4442 / 4306; a rolling lead (8 units kept ahead of
-// the ring as each stage is issued): 4443 / 4052.
+// the ring as each stage is issued): 4443 / 4052.  Again with the wider
+// quantiser grid at m = 128: 8: 4690-4719 / 4551-4563, 12: 4730-4747 /
+// 4543-4571, 16: 4715 / 4492-4513, 20: 4593-4606 / 4379-4383.
 #ifndef QG_SKINNY_PAIR_L2_AHEAD
-#define QG_SKINNY_PAIR_L2_AHEAD 16
+#define QG_SKINNY_PAIR_L2_AHEAD 12
 #endif
 
 template <int kN>
